@@ -1,0 +1,214 @@
+/*
+ * tthrml.h — C ABI of the B200 block-Gibbs sweep library (libtthrml_b200.so).
+ *
+ * The reference (tt-thrml) runs one fused device kernel per sampling group per
+ * sweep with the signature
+ *     (global_state, *rng_slices) -> new_global_state
+ * (tt_thrml/compiler.py:3-4, 436-450; tt_thrml/executor.py:187-212, 240-275),
+ * launched through `tt_runtime.submit` (tt_thrml/executor.py:269).  This
+ * library replaces that kernel: one call per sampling group per sweep, in
+ * place on device memory, on the caller's CUDA stream.  The state gains a
+ * chain axis the reference does not have: every state buffer here is
+ * chain-innermost, `state[row][chain]`, row = the reference's flat
+ * block-ordered node index (tt_thrml/compiler.py:117-153).
+ *
+ * Conventions
+ *   - Every entry point returns TTHRML_OK (0) or a negative error code and
+ *     never aborts, traps or throws.  `tthrml_last_error()` returns the
+ *     message of the calling thread's last failure.
+ *   - All pointers named `*_dev` or documented as device memory must be
+ *     device pointers valid on the current CUDA device; host pointers are
+ *     named `*_host`.
+ *   - `stream` is a cudaStream_t passed as `void*` (NULL = legacy default).
+ *   - Run control: when `ctl` (a device tthrml_run_ctl) is given, kernels use
+ *     sweep index `sweep + ctl->sweep` and Philox seed `ctl->seed`, so one
+ *     captured CUDA graph of n sweeps serves every position of every run.
+ *   - RNG: with `variates == NULL` the kernels draw from an on-device
+ *     counter-based Philox4x32-10 stream keyed by `seed`, counter
+ *     (chain/4, row, sweep, salt).  With `variates != NULL` they consume
+ *     caller-provided variates exactly like the reference's uploaded RNG
+ *     slices (tt_thrml/rng.py:132-222): spin threshold logits, categorical
+ *     Gumbel noise, gaussian standard normals.
+ */
+#ifndef TTHRML_H_
+#define TTHRML_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTHRML_ABI_VERSION 1
+
+/* status codes */
+#define TTHRML_OK 0
+#define TTHRML_ERR_ARG -1     /* invalid argument (sizes, alignment, NULL) */
+#define TTHRML_ERR_CUDA -2    /* a CUDA runtime call failed */
+#define TTHRML_ERR_UNSUPPORTED -3
+
+/* parameter families (tt_thrml/core.py:15-18) */
+#define TTHRML_SPIN 0
+#define TTHRML_CATEGORICAL 1
+#define TTHRML_GAUSSIAN 2
+
+/* contribution kinds (tt_thrml/compiler.py:82-114) */
+#define TTHRML_KIND_LINEAR 0    /* "default" or "linear" */
+#define TTHRML_KIND_PRECISION 1 /* "precision" (reciprocal of inverse_weights) */
+
+/* state element types */
+#define TTHRML_STATE_F32 0 /* float32: spin ±1.0, categorical index, gaussian value */
+#define TTHRML_STATE_I8 1  /* int8:    spin ±1, categorical index (no gaussian) */
+
+#define TTHRML_MAX_CAT_SOURCES 4
+#define TTHRML_MAX_CATEGORIES 64
+
+/* Device-resident run control read by graph-captured kernels. */
+typedef struct tthrml_run_ctl {
+  uint32_t sweep;  /* added to the kernel's sweep argument */
+  uint32_t reserved;
+  uint64_t seed;   /* Philox seed, replaces the kernel's seed argument */
+} tthrml_run_ctl;
+
+/*
+ * One lowered interaction of one block, in ragged-ELL form: the terms of
+ * target node i are t in [row_ptr[i], row_ptr[i+1]).  A dense reference
+ * table (n_nodes, n_terms) is the special case row_ptr[i] = i*n_terms.
+ * Mirrors FusedInteractionSpec (tt_thrml/core.py:43-57) as built by
+ * _build_interaction_spec (tt_thrml/compiler.py:156-217).
+ */
+typedef struct tthrml_interaction {
+  const int64_t* row_ptr;   /* device, [n_nodes + 1] */
+  const float* weights;     /* device, [nnz][w_inner]: weights x active mask */
+  const int32_t* sources;   /* device, [n_sources][nnz]: flat state rows */
+  int64_t nnz;              /* terms in this interaction (row_ptr[n_nodes]) */
+  int32_t n_sources;        /* gathered sources per term */
+  int32_t n_categorical;    /* trailing sources that select a weight slice */
+  int32_t kind;             /* TTHRML_KIND_* */
+  int32_t w_inner;          /* q_target (categorical target, else 1) x prod(cat_q) */
+  int32_t cat_q[TTHRML_MAX_CAT_SOURCES]; /* categories of each categorical source */
+} tthrml_interaction;
+
+/*
+ * One block of a sampling group.  Mirrors FusedBlockSpec
+ * (tt_thrml/core.py:60-70).
+ */
+typedef struct tthrml_block {
+  int32_t family;           /* TTHRML_SPIN / _CATEGORICAL / _GAUSSIAN */
+  int32_t n_categories;     /* categorical q (<= TTHRML_MAX_CATEGORIES), else 1 */
+  int32_t n_interactions;
+  int32_t reserved;
+  int64_t n_nodes;
+  int64_t row_start;        /* first flat state row of the block */
+  const tthrml_interaction* interactions; /* device array [n_interactions] */
+  const float* variates;    /* device, [n_sweeps][n_nodes][qv][n_chains] or NULL
+                               (qv = n_categories for categorical, else 1) */
+  int64_t variates_sweeps;  /* sweeps held by `variates` */
+} tthrml_block;
+
+/*
+ * Generic group step (any mix of spin / categorical / gaussian blocks).
+ * Every block of the group reads the pre-group state and the group commits
+ * together (tt_thrml/compiler.py:436-450).  When `in_place` is 0 the new
+ * values go to `scratch` ([sum n_nodes][n_chains] elements of the state
+ * type) and a second kernel commits them; `in_place` = 1 is allowed only
+ * when no block of the group reads a row of the group.
+ * Reference: _sample_block and helpers, tt_thrml/compiler.py:274-385.
+ */
+typedef struct tthrml_group {
+  const tthrml_block* blocks; /* device array [n_blocks] */
+  int32_t n_blocks;
+  int32_t state_dtype;        /* TTHRML_STATE_* */
+  int64_t group_rows;         /* sum of the blocks' n_nodes */
+  int64_t n_chains;           /* chains held by this state (row length) */
+  int64_t chain_offset;       /* global index of chain 0 (multiple of 4) */
+  void* state;                /* device, [total_rows][n_chains] */
+  void* scratch;              /* device, [group_rows][n_chains] or NULL */
+  int32_t in_place;
+  int32_t use_variates;       /* 1: read blocks[].variates; 0: Philox */
+  uint64_t seed;
+  uint32_t sweep;             /* sweep index (ctl->sweep is added when ctl is set) */
+  uint32_t reserved;
+  const tthrml_run_ctl* ctl;  /* device run control or NULL (CUDA-graph replay) */
+} tthrml_group;
+
+int tthrml_group_step(const tthrml_group* group_host, void* stream);
+
+/*
+ * Sparse spin block (pairwise spin couplings + bias) on int8 ±1 state:
+ * gamma = bias + sum_e w_e * s[col_e], s = +1 where 2*gamma > logit(u).
+ * Reference: _accumulate_gamma + _sample_spin_block
+ * (tt_thrml/compiler.py:303-324) for a block whose interactions are one
+ * bias (no source) and one pair interaction (one spin source).
+ * Writes the block's rows in place; the caller guarantees the block reads
+ * none of its own rows (a proper colouring).
+ * Requires n_chains % 32 == 0 and chain_offset % 4 == 0.
+ */
+int tthrml_spin_csr_step(const int64_t* row_ptr_dev, /* [n_rows + 1] */
+                         const int32_t* cols_dev,    /* [nnz] flat rows */
+                         const float* vals_dev,      /* [nnz] */
+                         const float* bias_dev,      /* [n_rows] or NULL */
+                         int64_t row_start, int64_t n_rows,
+                         int8_t* state_dev, int64_t n_chains, int64_t chain_offset,
+                         const float* variates_dev,  /* [variates_sweeps][n_rows][n_chains] logits, or NULL */
+                         int64_t variates_sweeps,
+                         uint64_t seed, uint32_t sweep,
+                         const tthrml_run_ctl* ctl_dev, /* device run control, or NULL */
+                         void* stream);
+
+/*
+ * Adds `delta` to ctl->sweep on `stream` (the last node of a captured
+ * multi-sweep CUDA graph, so each replay continues the run).
+ */
+int tthrml_ctl_advance(tthrml_run_ctl* ctl_dev, uint32_t delta, void* stream);
+
+/*
+ * Read-back helper: copies rows [row_start, row_start+n_rows) of a
+ * chain-innermost state into a chain-major buffer out[chain][row] decoded
+ * like _global_chunk_to_block_state (tt_thrml/executor.py:433-438):
+ *   out_kind 0: uint8 bool   (spin: value > 0)
+ *   out_kind 1: int32        (categorical: rounded index)
+ *   out_kind 2: float32      (gaussian / raw)
+ */
+int tthrml_decode_rows(const void* state_dev, int32_t state_dtype, int64_t n_chains,
+                       int64_t row_start, int64_t n_rows, int32_t out_kind,
+                       void* out_dev, void* stream);
+
+/*
+ * Inverse of tthrml_decode_rows for load_state
+ * (tt_thrml/executor.py:104-136): in_dev is chain-major [n_chains][n_rows]
+ * values of type in_dtype (TTHRML_STATE_F32 or TTHRML_STATE_I8; bool data
+ * passes as I8).  With as_spin set a value v is stored as +1 if v > 0 else
+ * -1 (tt_thrml/executor.py:132-133); otherwise it is stored as is
+ * (categorical index, gaussian value).
+ */
+int tthrml_encode_rows(const void* in_dev, int32_t in_dtype, int32_t as_spin, int64_t n_rows,
+                       int32_t state_dtype, int64_t n_chains, int64_t row_start, void* state_dev,
+                       void* stream);
+
+/*
+ * Per-chain sum of rows [row_start, row_start+n_rows): out[chain] (float64,
+ * accumulated with atomics onto the existing value).  Magnetisation of spin
+ * blocks; the observable of the lattice configurations.
+ */
+int tthrml_sum_rows(const void* state_dev, int32_t state_dtype, int64_t n_chains,
+                    int64_t row_start, int64_t n_rows, double* out_dev, void* stream);
+
+/* Host-only: greedy graph colouring in node order (smallest free colour).
+ * Returns the number of colours in *n_colours.  No device work. */
+int tthrml_greedy_colouring(int64_t n_nodes, const int64_t* row_ptr_host,
+                            const int32_t* cols_host, int32_t* colour_host,
+                            int32_t* n_colours);
+
+/* Makes `device` current for this library's CUDA runtime on the calling
+ * thread (the library links its own runtime; callers that switch devices
+ * call this before launching on another device). */
+int tthrml_set_device(int32_t device);
+
+const char* tthrml_last_error(void);
+int tthrml_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TTHRML_H_ */

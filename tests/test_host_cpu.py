@@ -1,0 +1,344 @@
+"""Host-side logic on CPU: lowering, planning, API contracts, library exports, PRNG restatement."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import thrml_shim as th
+import tt_thrml
+import tt_thrml_b200 as tb
+from oracle import oracle as orc
+from tt_thrml_b200 import _native as nat
+from tt_thrml_b200 import jax_prng, workloads
+from tt_thrml_b200.compiler import lower_program
+from tt_thrml_b200.core import Family
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+# --------------------------------------------------------------- library ABI
+
+
+def _header_symbols():
+    text = (ROOT / "include" / "tthrml.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tthrml_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    lib = nat.lib()
+    syms = _header_symbols()
+    assert "tthrml_group_step" in syms and "tthrml_spin_csr_step" in syms
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) <= set(nat.exported_symbols())
+    assert lib.tthrml_abi_version() == 1
+
+
+def test_struct_layouts_match_header_sizes():
+    assert ctypes.sizeof(nat.Interaction) == 64
+    assert ctypes.sizeof(nat.BlockDesc) == 56
+    assert ctypes.sizeof(nat.GroupDesc) == 88
+
+
+def test_library_rejects_bad_arguments_without_a_gpu():
+    lib = nat.lib()
+    rc = lib.tthrml_spin_csr_step(1, 1, 1, None, 0, 10, 16, 33, 0, None, 0, 0, 0, None, None)
+    assert rc == -1
+    assert b"multiple of 32" in lib.tthrml_last_error()
+    g = nat.GroupDesc()
+    assert lib.tthrml_group_step(ctypes.byref(g), None) == -1
+
+
+def test_greedy_colouring_is_proper():
+    rp, cols = workloads.lattice_2d_csr(6, 8)
+    col = workloads.greedy_colouring(rp, cols)
+    for v in range(rp.shape[0] - 1):
+        for e in range(rp[v], rp[v + 1]):
+            assert col[v] != col[cols[e]]
+
+
+# ------------------------------------------------------------------ lowering
+
+
+def _ragged(it, n):
+    return it.ragged(n)
+
+
+@pytest.mark.parametrize(
+    "make", [th.make_spin_case, th.make_categorical_case, th.make_gaussian_case, th.make_mixed_case]
+)
+def test_product_lowering_matches_oracle_lowering(make):
+    prog = make().program
+    lp = lower_program(prog)
+    op = orc.lower_program(prog)
+    assert [list(g) for g in lp.sampling_order] == op.sampling_order
+    assert lp.total_nodes == op.total
+    for spec, ob in zip(lp.specs[: lp.n_free_blocks], op.blocks):
+        assert spec.family.value == ob.family
+        assert spec.block_global_start == ob.start
+        assert len(spec.interactions) == len(ob.interactions)
+        for it, oit in zip(spec.interactions, ob.interactions):
+            rp, w, src = _ragged(it, spec.n_nodes)
+            np.testing.assert_array_equal(rp, oit.row_ptr)
+            np.testing.assert_array_equal(w, oit.weights)
+            np.testing.assert_array_equal(src, oit.sources)
+            assert it.n_categorical == oit.n_categorical
+
+
+def test_clamped_program_layout_puts_clamped_blocks_last():
+    prog, *_ = th.make_clamp_case()
+    lp = lower_program(prog)
+    assert lp.block_global_starts == (0, 1, 2)
+    assert lp.n_free_blocks == 2
+
+
+def test_global_map_must_be_dense():
+    prog = th.make_spin_case().program
+    gs = prog.gibbs_spec
+    node = gs.free_blocks[0].nodes[0]
+    gi, off = gs.node_global_location_map[node]
+    gs.node_global_location_map[node] = (gi, off + 100)
+    with pytest.raises(ValueError, match="not dense"):
+        lower_program(prog)
+
+
+def test_unknown_interaction_raises_type_error():
+    from tt_thrml_b200.compiler import _lower_interaction
+
+    with pytest.raises(TypeError):
+        _lower_interaction(object(), Family.SPIN)
+
+
+# ------------------------------------------------------------------ planning
+
+
+def test_plans_pick_the_spin_csr_kernel_for_ising_programs():
+    pytest.importorskip("torch")
+    from tt_thrml_b200.compiler import plan_program
+
+    prog = workloads.ising_lattice_2d(8, 8)
+    lp = lower_program(prog)
+    dtype, plans = plan_program(lp, 64, "cpu")
+    assert dtype == "int8" and all(p.kind == "spin_csr" for p in plans)
+    dtype, plans = plan_program(lp, 8, "cpu")  # chains not a multiple of 32
+    assert all(p.kind == "generic" for p in plans)
+
+
+def test_plans_use_scratch_for_self_reading_superblocks():
+    from tt_thrml_b200.compiler import plan_program
+
+    lp = lower_program(th.two_spin_superblock_program())
+    _, plans = plan_program(lp, 64, "cpu")
+    assert plans[0].kind == "generic" and not plans[0].in_place
+    lp = lower_program(th.make_mixed_case().program)
+    dtype, plans = plan_program(lp, 4, "cpu")
+    assert dtype == "float32"
+    assert [p.kind for p in plans] == ["generic", "generic"]
+
+
+def test_spin_csr_drops_masked_terms_exactly():
+    from tt_thrml_b200.compiler import plan_program
+
+    n = [th.SpinNode() for _ in range(4)]
+    # one interaction group in which node 0 is head twice and node 2 once: node 2's second slot is padding
+    group = th.InteractionGroup(
+        th.DiscreteEBMInteraction(1, [0.5, -0.25, 0.75]), th.Block([n[0], n[0], n[2]]), [th.Block([n[1], n[3], n[1]])]
+    )
+    free = [th.Block([n[0], n[2]]), th.Block([n[1], n[3]])]
+    prog = th.FactorSamplingProgram(
+        th.BlockGibbsSpec(free, []), [th.SpinGibbsConditional()] * 2, [th.SpinEBMFactor([th.Block(n)], [0.1] * 4)],
+        [group],
+    )
+    lp = lower_program(prog)
+    assert lp.specs[0].interactions[1].n_terms == 2
+    _, plans = plan_program(lp, 32, "cpu")
+    assert [p.kind for p in plans] == ["spin_csr", "spin_csr"]
+    blk = plans[0].blocks[0]
+    assert blk.row_ptr.tolist() == [0, 2, 3]
+    assert blk.cols.tolist() == [2, 3, 2]
+    np.testing.assert_array_equal(blk.vals.numpy(), np.float32([0.5, -0.25, 0.75]))
+
+
+# ------------------------------------------------------------------ API surface
+
+
+class _FakeTTNN:
+    class MeshShape:
+        def __init__(self, *dims):
+            self.dims = dims
+
+    def __init__(self):
+        self.open_device_calls, self.close_device_calls = [], []
+        self.open_mesh_calls, self.close_mesh_calls = [], []
+
+    def open_device(self, *, device_id):
+        self.open_device_calls.append(device_id)
+        return f"device:{device_id}"
+
+    def close_device(self, device):
+        self.close_device_calls.append(device)
+
+    def open_mesh_device(self, **kwargs):
+        self.open_mesh_calls.append(kwargs)
+        return f"mesh:{kwargs['mesh_shape'].dims}"
+
+    def close_mesh_device(self, device):
+        self.close_mesh_calls.append(device)
+
+
+def test_device_helpers_delegate_like_the_reference():
+    """tests/test_device_open.py of the reference, through the tt_thrml alias."""
+    t = _FakeTTNN()
+    assert tt_thrml.open_device(t, device_id=3) == "device:3"
+    tt_thrml.open_device(t)
+    assert t.open_device_calls == [3, 0]
+    assert tt_thrml.open_devices(t, device_ids=(0, 1, 2)) == ("device:0", "device:1", "device:2")
+    with pytest.raises(ValueError):
+        tt_thrml.open_devices(t, device_ids=())
+    tt_thrml.open_mesh_device(t, mesh_shape=(2, 4), device_ids=range(8), num_command_queues=2)
+    call = t.open_mesh_calls[-1]
+    assert call["mesh_shape"].dims == (2, 4) and call["physical_device_ids"] == list(range(8))
+    assert call["num_command_queues"] == 2
+    tt_thrml.open_mesh_device(t, mesh_shape=(1, 4))
+    assert "physical_device_ids" not in t.open_mesh_calls[-1]
+    tt_thrml.close_device(t, "d")
+    tt_thrml.close_mesh_device(t, "m")
+    tt_thrml.close_devices(t, ["a", "b"])
+    assert t.close_device_calls == ["d", "a", "b"] and t.close_mesh_calls == ["m"]
+
+
+class _FakeObserver:
+    def init(self):
+        return "observer-init"
+
+    def __call__(self, program, state_free, state_clamped, carry, sample_index):
+        return f"{carry}:{int(sample_index)}", np.asarray(int(sample_index))
+
+
+class _ExecutorShell:
+    program = object()
+
+    def load_state(self, state_free, state_clamp):
+        self.loaded = (state_free, state_clamp)
+
+    def _prepare_rng_thrml_compat(self, key, schedule, n_total):
+        self.rng = (key, schedule, n_total)
+
+    def run_warmup(self, n_warmup):
+        self.warmup = n_warmup
+
+    def _read_state_lists(self):
+        return [], []
+
+
+def test_sample_with_observation_uses_supplied_initial_carry():
+    """tests/test_executor_api.py of the reference."""
+    shell = _ExecutorShell()
+    carry, obs = tb.Executor.sample_with_observation(
+        shell,
+        key=object(),
+        schedule=th.SamplingSchedule(n_warmup=0, n_samples=1, steps_per_sample=1),
+        f_observe=_FakeObserver(),
+        init_state_free=[],
+        state_clamp=[],
+        observation_carry_init="caller-init",
+    )
+    assert carry == "caller-init:0"
+    assert obs.tolist() == [0]
+    assert shell.rng[2] == 0
+
+
+def test_schedule_sweep_count_matches_reference():
+    shell = _ExecutorShell()
+    shell.run_sweeps = lambda n: None
+    sched = th.SamplingSchedule(n_warmup=32, n_samples=64, steps_per_sample=2)
+    tb.Executor.sample_with_observation(
+        shell, key=0, schedule=sched, f_observe=_FakeObserver(), init_state_free=[], state_clamp=[]
+    )
+    assert shell.rng[2] == 32 + 63 * 2
+
+
+def test_make_ttmlir_config_keeps_reference_argument_checks():
+    with pytest.raises(ValueError):
+        tb.make_ttmlir_config(system_desc_path="x", build_dir="b", ttmlir_opt="o", ttmlir_translate="t")
+    with pytest.raises(ValueError):
+        tb.make_ttmlir_config(system_desc_path="x", ttmlir_opt="o")
+    cfg = tb.make_ttmlir_config(system_desc_path="x", build_dir="b")
+    assert isinstance(cfg, tb.CUDAConfig) and cfg.rng_mode == "philox"
+    with pytest.raises(ValueError):
+        tb.make_cuda_config(rng_mode="bogus")
+
+
+def test_public_surface_matches_reference():
+    ref_all = {
+        "TTMLIRConfig", "make_ttmlir_config", "open_device", "open_devices", "open_mesh_device", "close_device",
+        "close_mesh_device", "close_devices", "Executor", "make_executor", "MeshExecutor", "make_mesh_executor",
+        "sample_states", "sample_with_observation", "GaussianConditional",
+    }
+    assert ref_all <= set(tt_thrml.__all__)
+    import tt_thrml.compiler as c
+    import tt_thrml.executor as e
+
+    assert c.compile_program is tb.compile_program and e.Executor is tb.Executor
+
+
+def test_executor_requires_cuda():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("CUDA present")
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        tb.make_executor(None, None, workloads.ising_lattice_2d(4, 4), tb.make_cuda_config())
+
+
+# ------------------------------------------------------------------ PRNG restatement
+
+# Published Threefry-2x32-20 known-answer vectors (Salmon et al., Random123 distribution).
+THREEFRY_KAT = [
+    ((0, 0), (0, 0), (0x6B200159, 0x99BA4EFE)),
+    ((0xFFFFFFFF, 0xFFFFFFFF), (0xFFFFFFFF, 0xFFFFFFFF), (0x1CB996FC, 0xBB002BE7)),
+    ((0x13198A2E, 0x03707344), (0x243F6A88, 0x85A308D3), (0xC4923A9C, 0x483DF7A0)),
+]
+
+
+@pytest.mark.parametrize("key,ctr,expected", THREEFRY_KAT)
+def test_threefry_known_answers(key, ctr, expected):
+    a, b = jax_prng.threefry2x32(key[0], key[1], ctr[0], ctr[1])
+    assert (int(a), int(b)) == expected
+
+
+def test_prng_restatement_shapes_and_ranges():
+    k = jax_prng.key_from_seed(42)
+    assert k.tolist() == [0, 42]
+    ks = jax_prng.split(k, 5)
+    assert ks.shape == (5, 2) and len({tuple(x) for x in ks.tolist()}) == 5
+    u = jax_prng.uniform(k, (1000,))
+    assert u.dtype == np.float32 and (u >= 0).all() and (u < 1).all()
+    g = jax_prng.gumbel(k, (10, 3))
+    assert np.isfinite(g).all()
+    z = jax_prng.normal(jax_prng.split(k, 3), (4000,))
+    assert z.shape == (3, 4000) and abs(float(z.mean())) < 0.1 and abs(float(z.std()) - 1) < 0.1
+
+
+def test_parity_variates_follow_schedule_key_tree():
+    torch = pytest.importorskip("torch")
+    from tt_thrml_b200.rng import _NumpySource, generate_bulk_rng_for_schedule, make_rng_spec
+    from tt_thrml_b200.core import CompiledFusedBlock
+
+    prog = th.make_mixed_case().program
+    lp = lower_program(prog)
+    blocks = tuple(CompiledFusedBlock(s, None) for s in lp.specs)
+    sched = th.SamplingSchedule(3, 4, 2)
+    n_total = 3 + 3 * 2
+    spec = make_rng_spec(blocks, n_total)
+    buf = generate_bulk_rng_for_schedule(0, spec, sched, 6, "cpu", n_chains=2, source=_NumpySource())
+    assert buf.spin_threshold_logits[0].shape == (n_total, 1, 1, 2)
+    assert buf.categorical_gumbel[1].shape == (n_total, 1, 3, 2)
+    assert buf.gaussian_noise[2].shape == (n_total, 1, 1, 2)
+    assert isinstance(buf.spin_threshold_logits[0], torch.Tensor)

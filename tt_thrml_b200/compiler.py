@@ -1,0 +1,649 @@
+"""Program compilation: thrml program -> per-group device plans.
+
+The reference lowers each sampling group to a TT-MLIR flatbuffer with every
+weight and gather index baked in as IR constants (tt_thrml/compiler.py:1-7,
+453-521).  Here each group lowers to static device tables plus a block
+descriptor, and runs as one precompiled sm_100a kernel per sweep:
+
+* the lowering of a thrml `BlockSamplingProgram` to `FusedBlockSpec`s keeps
+  the reference's semantics (flat block-ordered layout, family inference,
+  interaction lowering, weighted masks; tt_thrml/compiler.py:39-271);
+* each group is then planned onto one of two kernels:
+  - `spin_csr`: blocks of spins whose field is one bias plus one pairwise
+    spin coupling (Ising-type programs), int8 state, CSR neighbour tables;
+  - `generic`: anything else (categorical sources, gaussian blocks, mixed
+    superblocks, multi-source terms), ragged-ELL tables.
+
+Programs may also lower themselves (native table programs such as the
+synthetic workloads in `tt_thrml_b200.workloads`) by providing
+`tt_lower_blocks()`; they skip the per-node thrml layout loop.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+
+from . import _native as nat
+from .core import (
+    CompiledFusedBlock,
+    CompiledProgram,
+    CompiledSamplingGroup,
+    CUDAConfig,
+    Family,
+    FusedBlockSpec,
+    FusedInteractionSpec,
+)
+from .rng import make_rng_spec
+
+# --------------------------------------------------------------------------
+# Lowering of thrml programs (semantics of tt_thrml/compiler.py:39-271).
+# --------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class _GlobalStateLayout:
+    """Flat block-ordered layout (tt_thrml/compiler.py:39-50)."""
+
+    block_starts: tuple[int, ...]
+    global_to_flat: tuple[np.ndarray, ...]
+    total_nodes: int
+
+    def flatten_slices(self, global_inds, global_slices) -> tuple[np.ndarray, ...]:
+        flat = []
+        for global_ind, global_slice in zip(global_inds, global_slices, strict=True):
+            index_map = self.global_to_flat[int(global_ind)]
+            flat.append(index_map[np.asarray(global_slice, dtype=np.int64)].astype(np.int32))
+        return tuple(flat)
+
+
+def _infer_family(block, gibbs_spec) -> Family:
+    """tt_thrml/compiler.py:53-70."""
+    explicit = getattr(block, "family", None)
+    if explicit is not None:
+        return Family(explicit)
+    node_type = type(block.nodes[0]).__name__.lower()
+    if "spin" in node_type or "bool" in node_type:
+        return Family.SPIN
+    if "categorical" in node_type or "discrete" in node_type:
+        return Family.CATEGORICAL
+    if "gaussian" in node_type or "continuous" in node_type:
+        return Family.GAUSSIAN
+    sds = getattr(gibbs_spec, "node_shape_dtypes", None) or {}
+    sd = sds.get(type(block.nodes[0]))
+    if sd is not None:
+        dtype = getattr(sd, "dtype", None)
+        if dtype is None:
+            dtype = sd[0][0].dtype
+        kind = np.dtype(dtype).kind
+        if kind == "b":
+            return Family.SPIN
+        if kind in ("i", "u"):
+            return Family.CATEGORICAL
+        if kind == "f":
+            return Family.GAUSSIAN
+    return Family.SPIN
+
+
+def _get_n_categories(block, family: Family) -> int | None:
+    """tt_thrml/compiler.py:73-79."""
+    if family != Family.CATEGORICAL:
+        return None
+    n = getattr(block.nodes[0], "n_categories", None)
+    return int(n) if n is not None else 2
+
+
+def _lower_interaction(interaction, family: Family) -> dict:
+    """tt_thrml/compiler.py:82-114 (same hook, attribute and error contract)."""
+    hook = getattr(interaction, "tt_interaction_contribution", None)
+    if callable(hook):
+        contrib = hook(parameter_family=family.value)
+        return {
+            "weights": np.asarray(getattr(contrib, "weights")),
+            "n_spin": int(getattr(contrib, "n_spin")),
+            "n_categorical": getattr(contrib, "n_categorical", None),
+            "contribution_kind": str(getattr(contrib, "contribution_kind", "default")),
+        }
+    if hasattr(interaction, "n_spin") and hasattr(interaction, "weights"):
+        return {
+            "weights": np.asarray(interaction.weights),
+            "n_spin": int(interaction.n_spin),
+            "n_categorical": None,
+            "contribution_kind": "default",
+        }
+    if family == Family.GAUSSIAN:
+        if hasattr(interaction, "weights"):
+            return {
+                "weights": np.asarray(interaction.weights),
+                "n_spin": 0,
+                "n_categorical": 0,
+                "contribution_kind": "linear",
+            }
+        if hasattr(interaction, "inverse_weights"):
+            return {
+                "weights": np.reciprocal(np.asarray(interaction.inverse_weights, dtype=np.float32)),
+                "n_spin": 0,
+                "n_categorical": 0,
+                "contribution_kind": "precision",
+            }
+    raise TypeError(f"Cannot lower interaction of type {type(interaction)}")
+
+
+def _build_block_global_starts(gibbs_spec) -> tuple[tuple[int, ...], int]:
+    starts, offset = [], 0
+    for block in gibbs_spec.blocks:
+        starts.append(offset)
+        offset += len(block.nodes)
+    return tuple(starts), offset
+
+
+def _build_global_state_layout(gibbs_spec) -> _GlobalStateLayout:
+    """tt_thrml/compiler.py:126-153: free blocks first, then clamped."""
+    block_starts, total_nodes = _build_block_global_starts(gibbs_spec)
+    loc_map = gibbs_spec.node_global_location_map
+    per_block = []
+    max_gi = -1
+    for bi, block in enumerate(gibbs_spec.blocks):
+        locs = np.asarray([loc_map[node] for node in block.nodes], dtype=np.int64).reshape(-1, 2)
+        per_block.append(locs)
+        if len(locs):
+            max_gi = max(max_gi, int(locs[:, 0].max()))
+    sizes = [0] * (max_gi + 1)
+    for locs in per_block:
+        for gi in np.unique(locs[:, 0]):
+            sizes[gi] = max(sizes[gi], int(locs[locs[:, 0] == gi, 1].max()) + 1)
+    maps = [np.full(s, -1, dtype=np.int64) for s in sizes]
+    for bi, locs in enumerate(per_block):
+        flat = block_starts[bi] + np.arange(len(locs), dtype=np.int64)
+        for gi in np.unique(locs[:, 0]):
+            sel = locs[:, 0] == gi
+            maps[gi][locs[sel, 1]] = flat[sel]
+    for m in maps:
+        if (m < 0).any():
+            raise ValueError("THRML global state map is not dense.")
+    return _GlobalStateLayout(block_starts=block_starts, global_to_flat=tuple(maps), total_nodes=total_nodes)
+
+
+def _build_interaction_spec(
+    interaction, active_mask, global_inds, global_slices, family: Family, n_nodes: int, layout: _GlobalStateLayout
+) -> FusedInteractionSpec:
+    """tt_thrml/compiler.py:156-217."""
+    lowered = _lower_interaction(interaction, family)
+    weights = np.asarray(lowered["weights"], dtype=np.float32)
+    mask = np.asarray(active_mask, dtype=np.float32)
+    if weights.ndim == 1:
+        weights = weights.reshape(n_nodes, -1)
+    if mask.ndim == 1:
+        mask = mask.reshape(n_nodes, -1)
+    if weights.shape[:2] == mask.shape:
+        n_terms = int(mask.shape[1])
+        weighted_mask = (weights * mask.reshape(mask.shape + (1,) * (weights.ndim - 2))).astype(np.float32)
+    elif weights.shape == mask.shape:
+        weighted_mask = (weights * mask).astype(np.float32)
+        n_terms = int(weighted_mask.shape[-1])
+    else:
+        raise ValueError(f"weights shape {weights.shape} does not match mask shape {mask.shape}")
+
+    n_spin = int(lowered["n_spin"])
+    explicit = lowered.get("n_categorical")
+    if explicit is not None:
+        n_cat = int(explicit)
+    elif family == Family.CATEGORICAL:
+        n_cat = max(0, weights.ndim - 3)
+    elif lowered["contribution_kind"] == "default":
+        n_cat = max(0, weights.ndim - 2)
+    else:
+        n_cat = 0
+
+    gathers = []
+    for gslice in layout.flatten_slices(global_inds, global_slices):
+        arr = np.asarray(gslice, dtype=np.int32)
+        if arr.shape != (n_nodes, n_terms):
+            raise ValueError(f"gather slice shape {arr.shape} does not match ({n_nodes}, {n_terms})")
+        gathers.append(arr)
+    if len(gathers) < n_spin + n_cat:
+        raise ValueError(
+            f"too few gather slices: need at least {n_spin + n_cat} "
+            f"(n_spin={n_spin} + n_categorical_sources={n_cat}), got {len(gathers)}"
+        )
+    return FusedInteractionSpec(
+        weighted_mask=weighted_mask,
+        gather_indices=tuple(gathers),
+        n_spin=n_spin,
+        n_categorical=n_cat,
+        n_terms=n_terms,
+        contribution_kind=lowered["contribution_kind"],
+    )
+
+
+def _build_fused_block_spec(program, block_index, block, family, block_global_start, total_nodes, layout):
+    """tt_thrml/compiler.py:220-271."""
+    n_nodes = len(block.nodes)
+    n_categories = _get_n_categories(block, family)
+    interactions = tuple(
+        _build_interaction_spec(inter, active, ginds, gslices, family, n_nodes, layout)
+        for inter, active, ginds, gslices in zip(
+            program.per_block_interactions[block_index],
+            program.per_block_interaction_active[block_index],
+            program.per_block_interaction_global_inds[block_index],
+            program.per_block_interaction_global_slices[block_index],
+            strict=True,
+        )
+    )
+    if family == Family.CATEGORICAL and interactions:
+        n_categories = _infer_n_categories(interactions, n_categories)
+    return FusedBlockSpec(block_index, family, n_nodes, n_categories, block_global_start, total_nodes, interactions)
+
+
+def _infer_n_categories(interactions, default):
+    """Category count from the weight shapes (tt_thrml/compiler.py:252-261)."""
+    q = default
+    for ispec in interactions:
+        wm = ispec.weighted_mask
+        if ispec.row_ptr is None:
+            if wm.ndim >= 3:
+                return int(wm.shape[2])
+            if ispec.n_terms > 0:
+                q = wm.shape[-1] // ispec.n_terms
+        elif wm.ndim >= 2:
+            return int(wm.shape[1])
+    return q
+
+
+@dataclass
+class LoweredProgram:
+    specs: tuple[FusedBlockSpec, ...]
+    sampling_order: tuple[tuple[int, ...], ...]
+    n_free_blocks: int
+    total_nodes: int
+    block_global_starts: tuple[int, ...]
+
+
+def lower_program(program) -> LoweredProgram:
+    """Lowers a thrml program (or a native table program) to block specs."""
+    native = getattr(program, "tt_lower_blocks", None)
+    gibbs_spec = program.gibbs_spec
+    sampling_order = tuple(tuple(int(i) for i in g) for g in gibbs_spec.sampling_order)
+    n_free = len(gibbs_spec.free_blocks)
+    if callable(native):
+        specs = tuple(native())
+        starts = tuple(s.block_global_start for s in specs)
+        total = specs[0].total_nodes if specs else 0
+        return LoweredProgram(specs, sampling_order, n_free, total, starts)
+    layout = _build_global_state_layout(gibbs_spec)
+    specs = []
+    for bi, block in enumerate(gibbs_spec.blocks):
+        family = _infer_family(block, gibbs_spec)
+        if bi < n_free:
+            specs.append(
+                _build_fused_block_spec(
+                    program, bi, block, family, layout.block_starts[bi], layout.total_nodes, layout
+                )
+            )
+        else:
+            specs.append(
+                FusedBlockSpec(bi, family, len(block.nodes), None, layout.block_starts[bi], layout.total_nodes, ())
+            )
+    return LoweredProgram(tuple(specs), sampling_order, n_free, layout.total_nodes, layout.block_starts)
+
+
+# --------------------------------------------------------------------------
+# Planning: block specs -> device tables + kernel choice per group.
+# --------------------------------------------------------------------------
+
+_FAMILY_CODE = {Family.SPIN: nat.SPIN, Family.CATEGORICAL: nat.CATEGORICAL, Family.GAUSSIAN: nat.GAUSSIAN}
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def resolve_torch_device(device):
+    torch = _torch()
+    if device is None:
+        return torch.device("cuda", torch.cuda.current_device() if torch.cuda.is_available() else 0)
+    if isinstance(device, torch.device):
+        return device
+    if isinstance(device, int):
+        return torch.device("cuda", device)
+    if isinstance(device, str):
+        return torch.device(device)
+    td = getattr(device, "torch_device", None)
+    if td is not None:
+        return td
+    devs = getattr(device, "devices", None)
+    if devs:
+        return devs[0].torch_device
+    raise TypeError(f"cannot interpret {device!r} as a CUDA device")
+
+
+def _to_dev(arr: np.ndarray, device):
+    torch = _torch()
+    return torch.from_numpy(np.ascontiguousarray(arr)).to(device)
+
+
+def _cat_axes(spec: FusedBlockSpec, it: FusedInteractionSpec) -> tuple[int, tuple[int, ...]]:
+    """(q_target, categorical source sizes) of an interaction's weight table."""
+    wm = np.asarray(it.weighted_mask)
+    lead = 1 if it.row_ptr is not None else 2
+    trailing = tuple(int(d) for d in wm.shape[lead:])
+    if spec.family == Family.CATEGORICAL:
+        q = int(spec.n_categories or 2)
+        if not trailing or trailing[0] != q:
+            raise ValueError(
+                f"block {spec.block_index}: categorical weights need a category axis of size {q}, got {wm.shape}"
+            )
+        cat = trailing[1:]
+        q_t = q
+    else:
+        cat = trailing
+        q_t = 1
+    if len(cat) != it.n_categorical:
+        raise ValueError(
+            f"block {spec.block_index}: weight shape {wm.shape} has {len(cat)} source axes, "
+            f"n_categorical={it.n_categorical}"
+        )
+    if it.n_categorical > nat.MAX_CAT_SOURCES:
+        raise ValueError(f"at most {nat.MAX_CAT_SOURCES} categorical sources per interaction are supported")
+    return q_t, cat
+
+
+@dataclass
+class GenericGroupPlan:
+    """Device tables of a group run by tthrml_group_step."""
+
+    block_indices: tuple[int, ...]
+    family_label: str
+    in_place: bool
+    group_rows: int
+    interaction_tables: list  # keeps device tensors alive
+    block_fields: list  # (family, q, n_inter, n_nodes, row_start, inter_desc_tensor)
+    device: Any
+    kind: str = "generic"
+    _desc: Any = None
+    _desc_variates: tuple = ()
+
+    def descriptor(self, variates: dict | None, n_sweeps: int):
+        """Device array of block descriptors (rebuilt when the variates change)."""
+        key = tuple(
+            (bi, 0 if variates is None or variates.get(bi) is None else variates[bi].data_ptr())
+            for bi in self.block_indices
+        )
+        if self._desc is not None and self._desc_variates == key:
+            return self._desc
+        arr = (nat.BlockDesc * len(self.block_fields))()
+        for k, (bi, (fam, q, n_inter, n_nodes, row_start, inter_t)) in enumerate(
+            zip(self.block_indices, self.block_fields)
+        ):
+            d = arr[k]
+            d.family, d.n_categories, d.n_interactions = fam, q, n_inter
+            d.n_nodes, d.row_start = n_nodes, row_start
+            d.interactions = inter_t.data_ptr() if inter_t is not None else None
+            v = None if variates is None else variates.get(bi)
+            d.variates = v.data_ptr() if v is not None else None
+            d.variates_sweeps = n_sweeps if v is not None else 0
+        torch = _torch()
+        raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
+        self._desc = raw.to(self.device)
+        torch.cuda.synchronize(self.device)  # visible to kernels on any stream
+        self._desc_variates = key
+        return self._desc
+
+
+@dataclass
+class SpinCSRBlock:
+    block_index: int
+    row_start: int
+    n_rows: int
+    row_ptr: Any
+    cols: Any
+    vals: Any
+    bias: Any
+    nnz: int
+
+
+@dataclass
+class SpinCSRGroupPlan:
+    """Device tables of a group of spin blocks run by tthrml_spin_csr_step."""
+
+    block_indices: tuple[int, ...]
+    blocks: list[SpinCSRBlock]
+    family_label: str = "spin"
+    kind: str = "spin_csr"
+    in_place: bool = True
+    group_rows: int = 0
+    device: Any = None
+
+
+def _ragged_tables(spec: FusedBlockSpec):
+    out = []
+    for it in spec.interactions:
+        rp, w, src = it.ragged(spec.n_nodes)
+        out.append((it, rp, w, src))
+    return out
+
+
+def _validate_sources(spec: FusedBlockSpec, tables, total_nodes: int) -> None:
+    for it, rp, w, src in tables:
+        if rp.shape != (spec.n_nodes + 1,) or rp[0] != 0 or (np.diff(rp) < 0).any():
+            raise ValueError(f"block {spec.block_index}: malformed term offsets")
+        if src.size and (src.min() < 0 or src.max() >= total_nodes):
+            raise ValueError(f"block {spec.block_index}: gather index outside the {total_nodes}-row state")
+        if w.shape[0] != rp[-1]:
+            raise ValueError(f"block {spec.block_index}: {w.shape[0]} weight rows for {rp[-1]} terms")
+
+
+def _group_reads_itself(specs, tables_by_block, total_nodes: int) -> bool:
+    inside = np.zeros(total_nodes, dtype=bool)
+    for s in specs:
+        inside[s.block_global_start : s.block_global_start + s.n_nodes] = True
+    for s in specs:
+        for it, rp, w, src in tables_by_block[s.block_index]:
+            if src.size and inside[src].any():
+                return True
+    return False
+
+
+def _spin_csr_eligible(specs, tables_by_block, state_dtype: str, n_chains: int) -> bool:
+    if state_dtype != "int8" or n_chains % 32:
+        return False
+    for s in specs:
+        if s.family != Family.SPIN:
+            return False
+        n_bias = n_pair = 0
+        for it, rp, w, src in tables_by_block[s.block_index]:
+            if it.n_categorical or w.shape[1] != 1:
+                return False
+            if src.shape[0] == 0:
+                n_bias += 1
+            elif src.shape[0] == 1:
+                n_pair += 1
+            else:
+                return False
+        if n_bias > 1 or n_pair > 1 or n_bias + n_pair == 0:
+            return False
+    return True
+
+
+def _sequential_row_sum(rp: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """Per-row float32 sum of terms in order (the bias of a spin block)."""
+    n = rp.shape[0] - 1
+    counts = np.diff(rp)
+    out = np.zeros(n, dtype=np.float32)
+    if n == 0:
+        return out
+    vals = w[:, 0].astype(np.float32)
+    maxc = int(counts.max()) if n else 0
+    first = True
+    for t in range(maxc):
+        has = counts > t
+        idx = rp[:-1][has] + t
+        if first:
+            out[has] = vals[idx]
+            first = False
+        else:
+            out[has] = (out[has] + vals[idx]).astype(np.float32)
+    return out
+
+
+def _plan_spin_csr(group, specs, tables_by_block, device) -> SpinCSRGroupPlan:
+    blocks = []
+    for s in specs:
+        bias = None
+        pair = None
+        for it, rp, w, src in tables_by_block[s.block_index]:
+            if src.shape[0] == 0:
+                bias = _sequential_row_sum(rp, w)
+            else:
+                pair = (rp, w[:, 0], src[0])
+        if pair is None:
+            rp = np.zeros(s.n_nodes + 1, dtype=np.int64)
+            cols = np.zeros(1, dtype=np.int32)
+            vals = np.zeros(1, dtype=np.float32)
+        else:
+            rp, vals, cols = pair
+            keep = vals != 0.0
+            if not keep.all():
+                # masked terms add +-0 to the field: dropping them is exact
+                row_of_term = np.repeat(np.arange(s.n_nodes, dtype=np.int64), np.diff(rp))
+                counts = np.bincount(row_of_term[keep], minlength=s.n_nodes)
+                rp = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+                vals, cols = vals[keep], cols[keep]
+            if len(vals) == 0:
+                cols = np.zeros(1, dtype=np.int32)
+                vals = np.zeros(1, dtype=np.float32)
+        blocks.append(
+            SpinCSRBlock(
+                block_index=s.block_index,
+                row_start=s.block_global_start,
+                n_rows=s.n_nodes,
+                row_ptr=_to_dev(rp.astype(np.int64), device),
+                cols=_to_dev(cols.astype(np.int32), device),
+                vals=_to_dev(vals.astype(np.float32), device),
+                bias=None if bias is None else _to_dev(bias, device),
+                nnz=int(rp[-1]),
+            )
+        )
+    return SpinCSRGroupPlan(
+        block_indices=tuple(group), blocks=blocks, group_rows=sum(s.n_nodes for s in specs), device=device
+    )
+
+
+def _plan_generic(group, specs, tables_by_block, in_place: bool, device) -> GenericGroupPlan:
+    torch = _torch()
+    keep = []
+    fields = []
+    for s in specs:
+        if s.family == Family.CATEGORICAL and int(s.n_categories or 2) > nat.MAX_CATEGORIES:
+            raise ValueError(f"at most {nat.MAX_CATEGORIES} categories are supported")
+        descs = (nat.Interaction * max(1, len(s.interactions)))()
+        for k, (it, rp, w, src) in enumerate(tables_by_block[s.block_index]):
+            q_t, cat = _cat_axes(s, it)
+            rp_d, w_d, src_d = _to_dev(rp, device), _to_dev(w.astype(np.float32), device), _to_dev(src, device)
+            keep += [rp_d, w_d, src_d]
+            d = descs[k]
+            d.row_ptr, d.weights, d.sources = rp_d.data_ptr(), w_d.data_ptr(), src_d.data_ptr()
+            d.nnz = int(rp[-1])
+            d.n_sources = int(src.shape[0])
+            d.n_categorical = int(it.n_categorical)
+            d.kind = nat.KIND_PRECISION if it.contribution_kind == "precision" else nat.KIND_LINEAR
+            d.w_inner = int(w.shape[1])
+            for j, qj in enumerate(cat):
+                d.cat_q[j] = int(qj)
+            if d.n_sources < d.n_categorical:
+                raise ValueError(f"block {s.block_index}: fewer sources than categorical sources")
+            if d.w_inner != q_t * int(np.prod(cat, dtype=np.int64)):
+                raise ValueError(f"block {s.block_index}: weight inner size mismatch")
+        if s.family in (Family.SPIN, Family.CATEGORICAL) and not s.interactions:
+            raise ValueError("Block has no interactions; cannot build kernel")
+        inter_t = torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).to(device)
+        keep.append(inter_t)
+        q = int(s.n_categories or 2) if s.family == Family.CATEGORICAL else 1
+        fields.append((_FAMILY_CODE[s.family], q, len(s.interactions), s.n_nodes, s.block_global_start, inter_t))
+    label = "+".join(s.family.value for s in specs)
+    return GenericGroupPlan(
+        block_indices=tuple(group),
+        family_label=label,
+        in_place=in_place,
+        group_rows=sum(s.n_nodes for s in specs),
+        interaction_tables=keep,
+        block_fields=fields,
+        device=device,
+    )
+
+
+def choose_state_dtype(specs) -> str:
+    for s in specs:
+        if s.family == Family.GAUSSIAN:
+            return "float32"
+        if s.family == Family.CATEGORICAL and int(s.n_categories or 2) > 127:
+            return "float32"
+    return "int8"
+
+
+def plan_program(lowered: LoweredProgram, n_chains: int, device, *, force_generic: bool = False):
+    """Builds the per-group device plans of a lowered program."""
+    specs = lowered.specs
+    state_dtype = choose_state_dtype(specs[: lowered.n_free_blocks])
+    tables = {}
+    for s in specs[: lowered.n_free_blocks]:
+        t = _ragged_tables(s)
+        _validate_sources(s, t, lowered.total_nodes)
+        tables[s.block_index] = t
+    plans = []
+    for group in lowered.sampling_order:
+        gspecs = [specs[i] for i in group]
+        for s in gspecs:
+            if s.block_index >= lowered.n_free_blocks:
+                raise ValueError(f"sampling group {group} contains clamped block {s.block_index}")
+        reads_itself = _group_reads_itself(gspecs, tables, lowered.total_nodes)
+        if not force_generic and not reads_itself and _spin_csr_eligible(gspecs, tables, state_dtype, n_chains):
+            plans.append(_plan_spin_csr(group, gspecs, tables, device))
+        else:
+            plans.append(_plan_generic(group, gspecs, tables, not reads_itself, device))
+    return state_dtype, plans
+
+
+def compile_program(
+    ttnn,
+    device,
+    program,
+    config: CUDAConfig,
+    *,
+    n_sweeps: int = 100,
+    n_chains: int | None = None,
+    force_generic: bool = False,
+) -> CompiledProgram:
+    """Compile a thrml program for the CUDA executor (tt_thrml/compiler.py:524-592)."""
+    del ttnn
+    n_chains = int(n_chains if n_chains is not None else config.n_chains)
+    tdev = resolve_torch_device(device)
+    lowered = lower_program(program)
+    state_dtype, plans = plan_program(lowered, n_chains, tdev, force_generic=force_generic)
+    _torch().cuda.synchronize(tdev)  # tables uploaded before any stream uses them
+    blocks = tuple(CompiledFusedBlock(spec=s, kernel_artifact=None) for s in lowered.specs)
+    groups = tuple(
+        CompiledSamplingGroup(block_indices=tuple(g), kernel_artifact=p) for g, p in zip(lowered.sampling_order, plans)
+    )
+    rng_spec = make_rng_spec(blocks[: lowered.n_free_blocks], n_sweeps)
+    return CompiledProgram(
+        blocks=blocks,
+        sampling_groups=groups,
+        n_free_blocks=lowered.n_free_blocks,
+        total_nodes=lowered.total_nodes,
+        block_global_starts=lowered.block_global_starts,
+        sampling_order=lowered.sampling_order,
+        state_dtype=state_dtype,
+        index_dtype="int32",
+        layout="rows x chains",
+        rng_spec=rng_spec,
+        n_chains=n_chains,
+        device=tdev,
+    )
+
+
+__all__ = ["compile_program", "lower_program", "plan_program", "LoweredProgram", "GenericGroupPlan", "SpinCSRGroupPlan"]

@@ -1,0 +1,84 @@
+// Shared helpers of the sweep kernels: error reporting, Philox4x32-10 and
+// the uniform / normal / Gumbel transforms every kernel draws from.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/tthrml.h"
+
+namespace tthrml {
+
+// Thread-local last error message (read by tthrml_last_error()).
+void set_error(const char* fmt, ...);
+
+inline int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return TTHRML_OK;
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return TTHRML_ERR_CUDA;
+}
+
+// Checks the launch just made (configuration errors surface here; the kernel
+// itself runs asynchronously).
+inline int launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
+
+// Salts of the Philox counter word 3: one per variate kind so the spin,
+// categorical and gaussian streams of one (chain, row, sweep) never overlap.
+constexpr uint32_t kSaltSpin = 0x5350494eu;      // "SPIN"
+constexpr uint32_t kSaltGauss = 0x47415553u;     // "GAUS"
+constexpr uint32_t kSaltCat = 0x43415400u;       // "CAT\0" + (category / 4)
+
+struct u32x4 {
+  uint32_t x, y, z, w;
+};
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as
+// easy as 1, 2, 3", SC'11): ten rounds of two 32x32->64 multiplies with the
+// published multipliers and Weyl key increments.
+__host__ __device__ __forceinline__ u32x4 philox4x32_10(u32x4 c, uint32_t k0, uint32_t k1) {
+#ifdef __CUDA_ARCH__
+#pragma unroll
+#endif
+  for (int r = 0; r < 10; ++r) {
+#ifdef __CUDA_ARCH__
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+#else
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c.x, p1 = (uint64_t)0xCD9E8D57u * c.z;
+    const uint32_t lo0 = (uint32_t)p0, hi0 = (uint32_t)(p0 >> 32);
+    const uint32_t lo1 = (uint32_t)p1, hi1 = (uint32_t)(p1 >> 32);
+#endif
+    c = u32x4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+__host__ __device__ __forceinline__ uint32_t word_of(const u32x4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// Uniform on the open interval (0, 1): odd multiples of 2^-24 built from the
+// top 23 bits, exact in float32 and identical on host and device.
+__host__ __device__ __forceinline__ float uniform_open(uint32_t bits) {
+  return (float)(((bits >> 9) << 1) | 1u) * 5.9604644775390625e-08f;  // 2^-24
+}
+
+__host__ __device__ __forceinline__ uint32_t seed_lo(uint64_t s) { return (uint32_t)s; }
+__host__ __device__ __forceinline__ uint32_t seed_hi(uint64_t s) { return (uint32_t)(s >> 32); }
+
+#ifdef __CUDACC__
+// Heat-bath spin decision in Philox mode: +1 with probability sigmoid(2*gamma)
+// (thrml's SpinGibbsConditional; tt_thrml/compiler.py:321-324), written as
+// u * (1 + exp(-2 gamma)) < 1 so a single exponential decides it.
+__device__ __forceinline__ bool spin_up_philox(float gamma, uint32_t bits) {
+  const float u = uniform_open(bits);
+  return u * (1.0f + __expf(-2.0f * gamma)) < 1.0f;
+}
+#endif
+
+}  // namespace tthrml

@@ -1,0 +1,563 @@
+"""Executor with device-resident state: one CUDA kernel per sampling group per sweep.
+
+Mirrors tt_thrml/executor.py: the same methods, guards, error messages and
+schedule semantics (load_state, prepare_rng, run_sweep, run_warmup, observe,
+sample_states, sample_with_observation, timing_summary, state_is_loaded,
+make_executor; executor.py:66-450).  What changes underneath:
+
+* the state is one torch CUDA tensor [total_nodes, n_chains], chain
+  innermost, int8 (spin / categorical programs) or float32 (programs with
+  gaussian blocks), and never leaves the GPU mid-sweep;
+* each group runs through libtthrml_b200 (`tthrml_spin_csr_step` or
+  `tthrml_group_step`) on the executor's stream; there is no host dispatch
+  layer, no per-call tensor wrapping and no CPU fallback;
+* Philox-mode variates are drawn inside the kernels; parity-mode variates are
+  uploaded once per run like the reference's bulk buffers;
+* `run_sweeps(n)` replays the sweep loop from a captured CUDA graph.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import time
+from typing import Any, Sequence
+
+import numpy as np
+
+from . import _native as nat
+from .compiler import compile_program, resolve_torch_device
+from .core import BulkRNGBuffers, CompiledProgram, CUDAConfig, Family
+from .observers import StateObserver, tree_expand, tree_stack
+from .rng import (
+    block_variates,
+    generate_bulk_rng,
+    generate_bulk_rng_for_schedule,
+    make_rng_spec,
+    philox_buffers,
+)
+
+_OUT_KIND = {Family.SPIN: 0, Family.CATEGORICAL: 1, Family.GAUSSIAN: 2}
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+class Executor:
+    def __init__(
+        self,
+        ttnn,
+        device,
+        program,
+        config: CUDAConfig,
+        compiled: CompiledProgram | None = None,
+        *,
+        n_sweeps: int = 100,
+        profile: bool = False,
+        n_chains: int | None = None,
+        chain_offset: int = 0,
+    ):
+        torch = _torch()
+        if not torch.cuda.is_available():
+            raise RuntimeError("CUDA is not available: the B200 executor has no CPU fallback")
+        self.ttnn = ttnn
+        self.device = device
+        self.program = program
+        self.config = config
+        self.n_sweeps = n_sweeps
+        self.profile = profile
+        if compiled is not None and n_chains is None:
+            n_chains = compiled.n_chains
+        self.n_chains = int(n_chains if n_chains is not None else config.n_chains)
+        if chain_offset % 4:
+            raise ValueError("chain_offset must be a multiple of 4")
+        self.chain_offset = int(chain_offset)
+        self.compiled = (
+            compiled
+            if compiled is not None
+            else compile_program(ttnn, device, program, config, n_sweeps=n_sweeps, n_chains=self.n_chains)
+        )
+        if self.compiled.n_chains != self.n_chains:
+            raise ValueError(f"compiled for {self.compiled.n_chains} chains, executor has {self.n_chains}")
+        self._tdev = self.compiled.device or resolve_torch_device(device)
+        self._lib = nat.lib()
+        stream = getattr(device, "stream", None)
+        self._stream = stream if stream is not None else torch.cuda.current_stream(self._tdev)
+        self._state_code = nat.STATE_I8 if self.compiled.state_dtype == "int8" else nat.STATE_F32
+        self._torch_state_dtype = torch.int8 if self._state_code == nat.STATE_I8 else torch.float32
+
+        self._global_state = None
+        self._state_loaded = False
+        self._rng_buffers: BulkRNGBuffers | None = None
+        self._sweep_counter = 0
+        self._rng_n_sweeps = 0
+        self._timing_log: list[tuple[str, float, float]] = []
+        self._scratch: dict[int, Any] = {}
+        self._pinned: dict[tuple, Any] = {}
+        self._graphs: dict[int, Any] = {}
+        self._ctl = None  # device tthrml_run_ctl read by graph-captured kernels
+        self._ctl_value = None
+
+    # ------------------------------------------------------------------ state
+
+    @property
+    def state_is_loaded(self) -> bool:
+        return self._state_loaded
+
+    @property
+    def stream(self):
+        return self._stream
+
+    @property
+    def global_state(self):
+        """The device state tensor [total_nodes, n_chains] (chain innermost)."""
+        return self._global_state
+
+    def _ensure_state(self):
+        torch = _torch()
+        if self._global_state is None:
+            self._global_state = torch.empty(
+                (self.compiled.total_nodes, self.n_chains), dtype=self._torch_state_dtype, device=self._tdev
+            )
+        return self._global_state
+
+    def _block_source(self, block_index: int, state):
+        """One block's states as a contiguous device tensor [C or 1, n] of int8 or float32.
+
+        Host data (numpy arrays, or torch CPU tensors, ideally pinned) is
+        copied to the device as is; the spin sign mapping and the transpose to
+        the chain-innermost layout happen in tthrml_encode_rows.
+        """
+        torch = _torch()
+        spec = self.compiled.blocks[block_index].spec
+        n, C = spec.n_nodes, self.n_chains
+        t = state if isinstance(state, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(np.asarray(state)))
+        if t.numel() not in (n, C * n):
+            raise ValueError(
+                f"block {block_index}: expected state of shape ({n},) or ({C}, {n}), got {tuple(t.shape)}"
+            )
+        t = t.reshape(-1, n)
+        if t.dtype in (torch.bool, torch.uint8):
+            t = t.view(torch.int8) if t.dtype == torch.uint8 else t.view(torch.uint8).view(torch.int8)
+        elif t.dtype != torch.int8:
+            if spec.family == Family.GAUSSIAN or self._state_code == nat.STATE_F32 or t.is_floating_point():
+                t = t.to(torch.float32)
+            else:
+                t = t.to(torch.int8)
+        t = t.contiguous().to(self._tdev, non_blocking=True)
+        return t
+
+    def load_state(self, state_free, state_clamp) -> None:
+        """Encode the block states and upload them into the device state (tt_thrml/executor.py:104-127)."""
+        torch = _torch()
+        n_free = self.compiled.n_free_blocks
+        states = list(state_free) + list(state_clamp)
+        if len(state_free) > n_free or len(states) != len(self.compiled.blocks):
+            raise ValueError(f"Expected {len(self.compiled.blocks)} block states, got {len(states)}")
+        self._ensure_state()
+        nat.bind_device(self._tdev.index)
+        with torch.cuda.stream(self._stream):
+            for bi, st in enumerate(states):
+                spec = self.compiled.blocks[bi].spec
+                src = self._block_source(bi, st)
+                if src.shape[0] == 1 and self.n_chains > 1:  # one state for every chain
+                    src = src.expand(self.n_chains, spec.n_nodes).contiguous()
+                in_code = nat.STATE_I8 if src.dtype == torch.int8 else nat.STATE_F32
+                nat.check(
+                    self._lib.tthrml_encode_rows(
+                        src.data_ptr(),
+                        in_code,
+                        1 if spec.family == Family.SPIN else 0,
+                        spec.n_nodes,
+                        self._state_code,
+                        self.n_chains,
+                        spec.block_global_start,
+                        self._global_state.data_ptr(),
+                        nat.stream_handle(self._stream),
+                    ),
+                    "tthrml_encode_rows",
+                )
+                src.record_stream(self._stream)
+        self._state_loaded = True
+
+    # -------------------------------------------------------------------- rng
+
+    def _install_rng(self, buffers: BulkRNGBuffers, n_sweeps: int) -> None:
+        # Philox-mode graphs read seed and sweep from the device run control and
+        # stay valid; parity-mode graphs hold variate pointers and are rebuilt.
+        if buffers.seed is None or (self._rng_buffers is not None and self._rng_buffers.seed is None):
+            self._graphs.clear()
+        self._rng_buffers = buffers
+        self._sweep_counter = 0
+        self._rng_n_sweeps = n_sweeps
+
+    def prepare_rng(self, key) -> None:
+        """Prepare variates for `n_sweeps` sweeps (tt_thrml/executor.py:138-148)."""
+        n = self.compiled.rng_spec.n_sweeps
+        if self.config.rng_mode == "philox":
+            self._install_rng(philox_buffers(key, n), n)
+        else:
+            buffers = generate_bulk_rng(key, self.compiled.rng_spec, self._tdev, n_chains=self.n_chains)
+            self._install_rng(buffers, n)
+
+    def _prepare_rng_for_n_sweeps(self, key, n_sweeps: int) -> None:
+        if self.config.rng_mode == "philox":
+            self._install_rng(philox_buffers(key, n_sweeps), n_sweeps)
+            return
+        spec = make_rng_spec(self.compiled.blocks[: self.compiled.n_free_blocks], n_sweeps)
+        self._install_rng(generate_bulk_rng(key, spec, self._tdev, n_chains=self.n_chains), n_sweeps)
+
+    def _prepare_rng_thrml_compat(self, key, schedule, n_total: int) -> None:
+        if self.config.rng_mode == "philox":
+            self._install_rng(philox_buffers(key, n_total), n_total)
+            return
+        spec = make_rng_spec(self.compiled.blocks[: self.compiled.n_free_blocks], n_total)
+        buffers = generate_bulk_rng_for_schedule(
+            key, spec, schedule, self.compiled.n_free_blocks, self._tdev, n_chains=self.n_chains
+        )
+        self._install_rng(buffers, n_total)
+
+    # ------------------------------------------------------------------ sweeps
+
+    def _check_ready(self, n: int = 1) -> None:
+        if not self._state_loaded:
+            raise RuntimeError("State must be loaded before running sweep")
+        if self._rng_buffers is None:
+            raise RuntimeError("RNG must be prepared before running sweep")
+        if self._sweep_counter + n > self._rng_n_sweeps:
+            raise RuntimeError("RNG buffer exhausted - call prepare_rng again")
+
+    def run_sweep(self) -> None:
+        """One sweep: every sampling group in order (tt_thrml/executor.py:150-163)."""
+        self._check_ready()
+        sweep_idx = self._sweep_counter
+        for group in self.compiled.sampling_groups:
+            self._run_sampling_group(group, sweep_idx)
+        self._sweep_counter += 1
+
+    def run_warmup(self, n_warmup: int) -> None:
+        self.run_sweeps(n_warmup)
+
+    def run_sweeps(self, n: int) -> None:
+        """n sweeps; replayed from a CUDA graph when config.cuda_graphs is set."""
+        if n <= 0:
+            return
+        self._check_ready(n)
+        if not self.config.cuda_graphs or self.profile or n < 4:
+            for _ in range(n):
+                self.run_sweep()
+            return
+        self._run_sweeps_graph(n)
+
+    def _run_sweeps_graph(self, n: int) -> None:
+        """Replays a captured graph of n sweeps.
+
+        Captured kernels read the sweep index as `k + ctl.sweep` (k = 0..n-1
+        baked into the graph) and the Philox seed from `ctl.seed`; the graph's
+        last node adds n to ctl.sweep.  One graph per n therefore serves every
+        position of every run; the host only rewrites ctl when it drifts.
+        """
+        torch = _torch()
+        if self._ctl is None:
+            self._ctl = torch.zeros(2, dtype=torch.int64, device=self._tdev)  # tthrml_run_ctl
+            self._ctl_host = torch.zeros(2, dtype=torch.int64, pin_memory=True)
+            self._ctl_value = None
+        g = self._graphs.get(n)
+        if g is None:
+            self._prepare_launch_state()
+            nat.bind_device(self._tdev.index)
+            g = torch.cuda.CUDAGraph()
+            self._stream.synchronize()
+            with torch.cuda.graph(g, stream=self._stream):
+                for k in range(n):
+                    for group in self.compiled.sampling_groups:
+                        self._run_sampling_group(group, k, capturing=True)
+                nat.check(
+                    self._lib.tthrml_ctl_advance(
+                        self._ctl.data_ptr(), n, nat.stream_handle(torch.cuda.current_stream(self._tdev))
+                    ),
+                    "tthrml_ctl_advance",
+                )
+            self._graphs[n] = g
+        seed = self._rng_buffers.seed if self._rng_buffers.seed is not None else 0
+        want = (self._sweep_counter, seed)
+        with torch.cuda.stream(self._stream):
+            if self._ctl_value != want:
+                self._stream.synchronize()  # the pinned staging word may still be in flight
+                lo = seed & 0xFFFFFFFFFFFFFFFF
+                self._ctl_host[0] = self._sweep_counter
+                self._ctl_host[1] = lo - (1 << 64) if lo >= (1 << 63) else lo
+                self._ctl.copy_(self._ctl_host, non_blocking=True)
+            g.replay()
+        self._sweep_counter += n
+        self._ctl_value = (self._sweep_counter, seed)
+
+    def _prepare_launch_state(self) -> None:
+        """Uploads descriptors and allocates scratch ahead of a graph capture."""
+        rng = self._rng_buffers
+        for group in self.compiled.sampling_groups:
+            plan = group.kernel_artifact
+            if plan.kind != "generic":
+                continue
+            variates = None if rng.seed is not None else {bi: self._variates(bi) for bi in plan.block_indices}
+            plan.descriptor(variates, self._rng_n_sweeps)
+            if not plan.in_place:
+                self._scratch_for(id(plan), plan.group_rows)
+        self._stream.synchronize()
+
+    def _scratch_for(self, gi: int, rows: int):
+        torch = _torch()
+        buf = self._scratch.get(gi)
+        if buf is None:
+            buf = torch.empty((max(1, rows), self.n_chains), dtype=self._torch_state_dtype, device=self._tdev)
+            self._scratch[gi] = buf
+        return buf
+
+    def _variates(self, block_index: int):
+        spec = self.compiled.blocks[block_index].spec
+        return block_variates(self._rng_buffers, block_index, spec.family)
+
+    def _run_sampling_group(self, group, sweep_idx: int, capturing: bool = False) -> None:
+        rng = self._rng_buffers
+        if rng is None:
+            raise RuntimeError("RNG must be prepared before running sweep")
+        plan = group.kernel_artifact
+        torch = _torch()
+        stream = nat.stream_handle(torch.cuda.current_stream(self._tdev) if capturing else self._stream)
+        seed = rng.seed if rng.seed is not None else 0
+        ctl = self._ctl.data_ptr() if capturing else None
+        nat.bind_device(self._tdev.index)
+        t0 = time.perf_counter()
+        if self.profile:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(self._stream)
+        if plan.kind == "spin_csr":
+            for blk in plan.blocks:
+                v = self._variates(blk.block_index)
+                vptr = None if v is None else v.data_ptr()
+                nat.check(
+                    self._lib.tthrml_spin_csr_step(
+                        blk.row_ptr.data_ptr(),
+                        blk.cols.data_ptr(),
+                        blk.vals.data_ptr(),
+                        None if blk.bias is None else blk.bias.data_ptr(),
+                        blk.row_start,
+                        blk.n_rows,
+                        self._global_state.data_ptr(),
+                        self.n_chains,
+                        self.chain_offset,
+                        vptr,
+                        self._rng_n_sweeps if v is not None else 0,
+                        seed,
+                        sweep_idx,
+                        ctl,
+                        stream,
+                    ),
+                    "tthrml_spin_csr_step",
+                )
+        else:
+            variates = None
+            if rng.seed is None:
+                variates = {bi: self._variates(bi) for bi in plan.block_indices}
+                missing = [bi for bi, v in variates.items() if v is None]
+                if missing:
+                    raise RuntimeError(f"RNG buffers hold no variates for blocks {missing}")
+            desc = plan.descriptor(variates, self._rng_n_sweeps)
+            gi = id(plan)
+            g = nat.GroupDesc()
+            g.blocks = desc.data_ptr()
+            g.n_blocks = len(plan.block_indices)
+            g.state_dtype = self._state_code
+            g.group_rows = plan.group_rows
+            g.n_chains = self.n_chains
+            g.chain_offset = self.chain_offset
+            g.state = self._global_state.data_ptr()
+            g.scratch = None if plan.in_place else self._scratch_for(gi, plan.group_rows).data_ptr()
+            g.in_place = 1 if plan.in_place else 0
+            g.use_variates = 0 if rng.seed is not None else 1
+            g.seed = seed
+            g.sweep = sweep_idx
+            g.ctl = ctl
+            nat.check(self._lib.tthrml_group_step(ctypes.byref(g), stream), "tthrml_group_step")
+        if self.profile:
+            t1 = time.perf_counter()
+            ev1.record(self._stream)
+            ev1.synchronize()
+            self._timing_log.append((plan.family_label, (t1 - t0) * 1000.0, ev0.elapsed_time(ev1)))
+
+    # ------------------------------------------------------------- read-back
+
+    def _pinned_buffer(self, key, shape, dtype):
+        torch = _torch()
+        buf = self._pinned.get(key)
+        if buf is None or tuple(buf.shape) != tuple(shape) or buf.dtype != dtype:
+            buf = torch.empty(shape, dtype=dtype, pin_memory=True)
+            self._pinned[key] = buf
+        return buf
+
+    def _decode_block(self, block_index: int, *, to_host: bool = True):
+        """One block as chain-major (C, n) bool / int32 / float32 (tt_thrml/executor.py:433-438)."""
+        torch = _torch()
+        spec = self.compiled.blocks[block_index].spec
+        kind = _OUT_KIND[spec.family]
+        dtype = (torch.uint8, torch.int32, torch.float32)[kind]
+        with torch.cuda.stream(self._stream):
+            dev = torch.empty((self.n_chains, spec.n_nodes), dtype=dtype, device=self._tdev)
+        nat.bind_device(self._tdev.index)
+        nat.check(
+            self._lib.tthrml_decode_rows(
+                self._global_state.data_ptr(),
+                self._state_code,
+                self.n_chains,
+                spec.block_global_start,
+                spec.n_nodes,
+                kind,
+                dev.data_ptr(),
+                nat.stream_handle(self._stream),
+            ),
+            "tthrml_decode_rows",
+        )
+        if not to_host:
+            return dev
+        host = self._pinned_buffer(("blk", block_index), dev.shape, dtype)
+        with torch.cuda.stream(self._stream):
+            host.copy_(dev, non_blocking=True)
+        dev.record_stream(self._stream)
+        return host
+
+    def _block_states_host(self, block_indices) -> list[np.ndarray]:
+        hosts = [self._decode_block(bi) for bi in block_indices]
+        self._stream.synchronize()
+        out = []
+        for bi, h in zip(block_indices, hosts):
+            spec = self.compiled.blocks[bi].spec
+            a = h.numpy().copy()
+            if spec.family == Family.SPIN:
+                a = a.astype(bool)
+            out.append(a.reshape(spec.n_nodes) if self.n_chains == 1 else a)
+        return out
+
+    def observe(self, blocks: Sequence) -> dict:
+        """Block states keyed by block (tt_thrml/executor.py:277-292)."""
+        if self._global_state is None:
+            return {}
+        lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
+        wanted = [(b, lookup.get(id(b))) for b in blocks]
+        idx = [bi for _, bi in wanted if bi is not None]
+        states = dict(zip(idx, self._block_states_host(idx)))
+        return {b: states[bi] for b, bi in wanted if bi is not None}
+
+    def _read_state_lists(self) -> tuple[list, list]:
+        """(state_free, state_clamped) as host arrays (tt_thrml/executor.py:297-312)."""
+        n_free = self.compiled.n_free_blocks
+        all_states = self._block_states_host(range(len(self.compiled.blocks)))
+        return all_states[:n_free], all_states[n_free:]
+
+    def block_sums(self, blocks: Sequence) -> np.ndarray:
+        """Per-chain sum over the listed blocks' rows, on device; returns (n_chains,) float64."""
+        torch = _torch()
+        lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
+        with torch.cuda.stream(self._stream):
+            out = torch.zeros(self.n_chains, dtype=torch.float64, device=self._tdev)
+        nat.bind_device(self._tdev.index)
+        for b in blocks:
+            bi = lookup[id(b)] if not isinstance(b, int) else b
+            spec = self.compiled.blocks[bi].spec
+            nat.check(
+                self._lib.tthrml_sum_rows(
+                    self._global_state.data_ptr(),
+                    self._state_code,
+                    self.n_chains,
+                    spec.block_global_start,
+                    spec.n_nodes,
+                    out.data_ptr(),
+                    nat.stream_handle(self._stream),
+                ),
+                "tthrml_sum_rows",
+            )
+        with torch.cuda.stream(self._stream):
+            host = out.cpu()
+        return host.numpy()
+
+    # --------------------------------------------------------------- schedule
+
+    def sample_states(self, key, schedule, nodes_to_sample: Sequence, *, init_state_free, state_clamp=()):
+        """thrml.sample_states over the schedule (tt_thrml/executor.py:342-365)."""
+        try:
+            from thrml.observers import StateObserver as _ThrmlStateObserver  # type: ignore
+
+            f_observe = _ThrmlStateObserver(list(nodes_to_sample))
+        except ImportError:
+            f_observe = StateObserver(list(nodes_to_sample))
+        _, results = self.sample_with_observation(
+            key, schedule, f_observe, init_state_free=init_state_free, state_clamp=state_clamp
+        )
+        return results
+
+    def sample_with_observation(
+        self, key, schedule, f_observe, *, init_state_free, state_clamp=(), observation_carry_init=None
+    ):
+        """thrml.sample_with_observation semantics (tt_thrml/executor.py:367-409).
+
+        Sample 0 is taken after warmup, samples 1..n_samples-1 after each
+        group of steps_per_sample sweeps.  Returns (carry, stacked observations).
+        """
+        n_total = schedule.n_warmup + max(0, schedule.n_samples - 1) * schedule.steps_per_sample
+        self.load_state(list(init_state_free), list(state_clamp))
+        self._prepare_rng_thrml_compat(key, schedule, n_total)
+        self.run_warmup(schedule.n_warmup)
+
+        carry = f_observe.init() if observation_carry_init is None else observation_carry_init
+        device_side = getattr(f_observe, "device_side", False)
+
+        def observe(carry, i):
+            if device_side:
+                return f_observe.observe_device(self, carry, i)
+            state_free, state_clamped = self._read_state_lists()
+            return f_observe(self.program, state_free, state_clamped, carry, np.asarray(i))
+
+        carry, obs = observe(carry, 0)
+        if schedule.n_samples <= 1:
+            return carry, tree_expand(obs)
+        all_obs = [obs]
+        for i in range(1, schedule.n_samples):
+            self.run_sweeps(schedule.steps_per_sample)
+            carry, obs = observe(carry, i)
+            all_obs.append(obs)
+        if all(o is None for o in all_obs):
+            return carry, None
+        return carry, tree_stack(all_obs)
+
+    def timing_summary(self) -> dict:
+        """Per-family dispatch and kernel ms of profiled runs (tt_thrml/executor.py:411-431)."""
+        groups: dict[str, list[tuple[float, float]]] = {}
+        for label, d, k in self._timing_log:
+            groups.setdefault(label, []).append((d, k))
+        summary = {}
+        for label, entries in sorted(groups.items()):
+            ds = [d for d, _ in entries]
+            ks = [k for _, k in entries]
+            summary[label] = {
+                "n": len(entries),
+                "dispatch_mean_ms": sum(ds) / len(ds),
+                "dispatch_total_ms": sum(ds),
+                "kernel_mean_ms": sum(ks) / len(ks),
+                "kernel_total_ms": sum(ks),
+            }
+        return summary
+
+
+def make_executor(
+    ttnn,
+    device,
+    program,
+    config: CUDAConfig,
+    *,
+    n_sweeps: int = 100,
+    profile: bool = False,
+    n_chains: int | None = None,
+) -> Executor:
+    return Executor(ttnn, device, program, config, n_sweeps=n_sweeps, profile=profile, n_chains=n_chains)
