@@ -7,14 +7,17 @@ each), 256 chains per GPU, seeded synthetic data.  One bench step = one run of
 200 sweeps over all k groups for all chains of every GPU.
 
 * `value`: steps on device-resident state (CUDA-graph replay of 200 sweeps),
-  CUDA events on the executor's stream, barrier + synchronize on both sides,
-  max over ranks; state (256 MiB int8) is larger than L2, so no flush is done.
+  one CUDA event pair per step on the executor's stream, barrier + synchronize
+  on both sides, max over ranks.  The bit-packed state (32 MiB) and the CSR
+  tables fit in L2, so L2 is flushed (256 MiB write) before every step,
+  outside the timed windows.
 * `e2e`: the same metric through the public API: each step is one
   `Executor.sample_states` call (pinned host initial state -> 200 sweeps ->
   final state back on the host), wall clock with synchronize on both sides.
-* `roofline`: the spin_csr kernel, algorithmic bytes per launch (neighbour
-  state rows read, own row written, CSR tables read once) over the CUDA-event
-  duration of each launch, against the measured HBM copy bandwidth.
+* `roofline`: the sparse spin kernel, algorithmic bytes per launch (neighbour
+  state rows read, own row written, CSR tables read once; a row is 32 B
+  bit-packed or 256 B as int8) over the CUDA-event duration of each launch,
+  against the measured HBM copy bandwidth.
 * `cpu_baseline`: the CPU oracle (C restatement of the reference's group
   math) on this host's cores over a bounded sample of the same workload.
 
@@ -136,13 +139,16 @@ def build_workload():
     return workloads.erdos_renyi_ising(N_NODES, MEAN_DEGREE, seed=SEED)
 
 
-def algorithmic_bytes(prog, n_chains: int):
-    """Per block: int8 state bytes (neighbour rows read + own row written) + CSR tables read once."""
+def algorithmic_bytes(prog, n_chains: int, layout: str):
+    """Per block launch: state bytes (each neighbour row read once, own row written once) plus the
+    CSR tables read once (8 B per edge: column + weight; 4 B bias and 8 B offset per row).
+    A state row is n_chains bytes in the int8 layout and n_chains/8 bytes bit-packed."""
+    row_bytes = n_chains // 8 if layout == "bits" else n_chains
     out = []
     for s in prog.specs:
         n = s.n_nodes
         nnz = int(s.interactions[1].row_ptr[-1])
-        out.append(n_chains * (nnz + n) + 8 * nnz + 4 * n + 8 * (n + 1))
+        out.append(row_bytes * (nnz + n) + 8 * nnz + 4 * n + 8 * (n + 1))
     return out
 
 
@@ -234,7 +240,7 @@ def run_ours(args):
     total_sweeps = SWEEPS_PER_STEP * (args.steps + args.warmup) + 16
     ex = Executor(None, device, prog, cfg, n_sweeps=total_sweeps, n_chains=C, chain_offset=rank * C)
     kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
-    assert kinds == {"spin_csr"}, kinds
+    assert kinds <= {"spin_csr", "spin_bits"}, kinds
     rng = np.random.default_rng(100 + rank)
     init = [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
     ex.load_state(init, [])
@@ -250,14 +256,21 @@ def run_ours(args):
     for _ in range(args.warmup):
         ex.run_sweeps(SWEEPS_PER_STEP)
     barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # Each step is timed by its own event pair; between steps a 256 MiB buffer is
+    # written so every step starts with a cold L2 (the bit-packed state and the
+    # CSR tables together fit in the 126 MB L2).
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
+        for e0, e1 in events:
+            with torch.cuda.stream(stream):
+                flush.fill_(1)
+            e0.record(stream)
             ex.run_sweeps(SWEEPS_PER_STEP)
-        ev1.record(stream)
+            e1.record(stream)
         barrier()
-    dt_ms = ev0.elapsed_time(ev1)
+    dt_ms = sum(e0.elapsed_time(e1) for e0, e1 in events)
+    del flush
     if dist is not None:
         t = torch.tensor([dt_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -267,7 +280,8 @@ def run_ours(args):
     gpu_launches = args.steps * (SWEEPS_PER_STEP * k + 1)
 
     # ---- roofline: per-launch CUDA events on the launch stream (eager sweeps)
-    per_block_bytes = algorithmic_bytes(prog, C)
+    layout = ex.compiled.state_dtype
+    per_block_bytes = algorithmic_bytes(prog, C, layout)
     ex.profile = True
     ex._timing_log.clear()
     n_prof = 5
@@ -332,7 +346,7 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "int8",
+            "dtype": "u32 bit-packed spins, f32 fields" if ex.compiled.state_dtype == "bits" else "int8 spins, f32 fields",
             "data": "synthetic (seeded Erdos-Renyi graph, random init)",
             "config": {
                 "workload": WORKLOAD,
@@ -342,11 +356,12 @@ def run_ours(args):
                 "chains_per_gpu": C,
                 "sweeps_per_step": SWEEPS_PER_STEP,
                 "rng": "philox4x32-10 on device",
-                "l2": "state 256 MiB > 126 MB L2 (no flush)",
+                "state_layout": ex.compiled.state_dtype,
+                "l2": "flushed before every timed step (256 MiB write)",
                 "parallelism": f"chain-sharded x{world}",
             },
             "roofline": {
-                "kernel": "k_spin_csr",
+                "kernel": "k_spin_bits" if layout == "bits" else "k_spin_csr_async",
                 "bound": "hbm",
                 "achieved": achieved,
                 "peak": peak,
@@ -380,12 +395,35 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-sweeps", type=int, default=0,
+                    help="run this many eager sweeps of the workload and exit (profiler target, no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_sweeps:
+        return run_profile_target(args.profile_sweeps)
     return run_ours(args)
+
+
+def run_profile_target(n_sweeps: int) -> int:
+    """Eager sweeps of the bench workload: one kernel launch per colour block per sweep."""
+    import torch
+
+    from tt_thrml_b200 import Executor, make_cuda_config
+
+    prog = build_workload()
+    C = CHAINS_PER_GPU
+    ex = Executor(None, 0, prog, make_cuda_config(n_chains=C, cuda_graphs=False), n_sweeps=n_sweeps, n_chains=C)
+    rng = np.random.default_rng(100)
+    ex.load_state([rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks], [])
+    ex.prepare_rng(SEED)
+    for _ in range(n_sweeps):
+        ex.run_sweep()
+    torch.cuda.synchronize()
+    print(f"profile target: {n_sweeps} sweeps x {len(prog.specs)} blocks", flush=True)
+    return 0
 
 
 if __name__ == "__main__":

@@ -59,6 +59,8 @@ extern "C" {
 /* state element types */
 #define TTHRML_STATE_F32 0 /* float32: spin ±1.0, categorical index, gaussian value */
 #define TTHRML_STATE_I8 1  /* int8:    spin ±1, categorical index (no gaussian) */
+#define TTHRML_STATE_BITS 2 /* spin only: row = n_chains bits in uint32 words,
+                               bit c set = chain c is -1 (n_chains % 32 == 0) */
 
 #define TTHRML_MAX_CAT_SOURCES 4
 #define TTHRML_MAX_CATEGORIES 64
@@ -155,6 +157,20 @@ int tthrml_spin_csr_step(const int64_t* row_ptr_dev, /* [n_rows + 1] */
                          uint64_t seed, uint32_t sweep,
                          const tthrml_run_ctl* ctl_dev, /* device run control, or NULL */
                          void* stream);
+
+/*
+ * The same block update on bit-packed state (TTHRML_STATE_BITS):
+ * state_dev is [rows][n_chains/32] uint32, bit c of a row = 1 when chain c
+ * is -1.  Same arguments, arithmetic and Philox stream as
+ * tthrml_spin_csr_step, so both layouts produce identical samples.
+ * Requires n_chains % 256 == 0 and chain_offset % 4 == 0.
+ */
+int tthrml_spin_bits_step(const int64_t* row_ptr_dev, const int32_t* cols_dev, const float* vals_dev,
+                          const float* bias_dev, int64_t row_start, int64_t n_rows,
+                          uint32_t* state_dev, int64_t n_chains, int64_t chain_offset,
+                          const float* variates_dev, int64_t variates_sweeps,
+                          uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl_dev,
+                          void* stream);
 
 /*
  * Adds `delta` to ctl->sweep on `stream` (the last node of a captured

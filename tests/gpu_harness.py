@@ -64,16 +64,12 @@ def make_variates(executor: Executor, n_sweeps: int, seed: int = 7):
 
 
 def gpu_state(executor: Executor) -> np.ndarray:
-    executor.stream.synchronize()
-    return executor.global_state.float().cpu().numpy()
+    """Device state decoded to float32 [rows, chains] (any layout)."""
+    return executor.raw_state()
 
 
 def set_gpu_state(executor: Executor, state: np.ndarray) -> None:
-    import torch
-
-    t = torch.from_numpy(np.ascontiguousarray(state)).to(executor.global_state.device)
-    executor.global_state.copy_(t.to(executor.global_state.dtype))
-    torch.cuda.synchronize()
+    executor.set_raw_state(state)
 
 
 def compare_group(report: ParityReport, ex: Executor, o: orc.OracleSampler, gi: int, margin: np.ndarray) -> None:

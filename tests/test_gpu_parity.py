@@ -69,7 +69,8 @@ def test_clamped_program_matches_oracle(cuda_device, mode):
 def test_spin_csr_kernel_matches_oracle_on_random_graph(cuda_device, mode, C):
     prog = workloads.erdos_renyi_ising(3000, 8.0, seed=3)
     rep, ex, _ = gh.run_parity(prog, C, 4, mode=mode)
-    assert all(g.kernel_artifact.kind == "spin_csr" for g in ex.compiled.sampling_groups)
+    kind = "spin_bits" if C % 256 == 0 else "spin_csr"
+    assert all(g.kernel_artifact.kind == kind for g in ex.compiled.sampling_groups)
     _assert_parity(rep)
 
 
@@ -95,6 +96,23 @@ def test_generic_and_spin_csr_paths_agree_bit_for_bit(cuda_device):
         for _ in range(8):
             ex.run_sweep()
         outs.append(gh.gpu_state(ex))
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("C", [256, 512])
+def test_bit_packed_and_int8_layouts_agree_bit_for_bit(cuda_device, C):
+    prog = workloads.erdos_renyi_ising(3000, 9.0, seed=8)
+    outs = []
+    for layout in ("int8", "bits"):
+        cfg = make_cuda_config(n_chains=C, cuda_graphs=True, spin_layout=layout)
+        ex = Executor(None, 0, prog, cfg, n_sweeps=12, n_chains=C)
+        assert ex.compiled.state_dtype == layout
+        ex.load_state(gh.random_init(prog, C, 2), [])
+        ex.prepare_rng(31)
+        ex.run_sweeps(12)
+        outs.append(gh.gpu_state(ex))
+        sums = ex.block_sums(prog.gibbs_spec.free_blocks)
+        np.testing.assert_array_equal(sums, outs[-1].sum(0))
     np.testing.assert_array_equal(outs[0], outs[1])
 
 

@@ -18,7 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 OK = 0
 SPIN, CATEGORICAL, GAUSSIAN = 0, 1, 2
 KIND_LINEAR, KIND_PRECISION = 0, 1
-STATE_F32, STATE_I8 = 0, 1
+STATE_F32, STATE_I8, STATE_BITS = 0, 1, 2
 MAX_CAT_SOURCES = 4
 MAX_CATEGORIES = 64
 
@@ -80,6 +80,10 @@ class GroupDesc(ctypes.Structure):
 _SIGNATURES = {
     "tthrml_group_step": (c_i32, [ctypes.POINTER(GroupDesc), c_vp]),
     "tthrml_spin_csr_step": (
+        c_i32,
+        [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp, c_vp],
+    ),
+    "tthrml_spin_bits_step": (
         c_i32,
         [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp, c_vp],
     ),

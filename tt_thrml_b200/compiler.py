@@ -585,8 +585,15 @@ def choose_state_dtype(specs) -> str:
     return "int8"
 
 
-def plan_program(lowered: LoweredProgram, n_chains: int, device, *, force_generic: bool = False):
-    """Builds the per-group device plans of a lowered program."""
+def plan_program(
+    lowered: LoweredProgram, n_chains: int, device, *, force_generic: bool = False, spin_layout: str = "auto"
+):
+    """Builds the per-group device plans of a lowered program.
+
+    Returns (state dtype, plans).  Programs whose every group runs on the
+    sparse spin kernel keep their state bit-packed ("bits") when the chain
+    count is a multiple of 256 and spin_layout allows it.
+    """
     specs = lowered.specs
     state_dtype = choose_state_dtype(specs[: lowered.n_free_blocks])
     tables = {}
@@ -605,6 +612,17 @@ def plan_program(lowered: LoweredProgram, n_chains: int, device, *, force_generi
             plans.append(_plan_spin_csr(group, gspecs, tables, device))
         else:
             plans.append(_plan_generic(group, gspecs, tables, not reads_itself, device))
+    if (
+        spin_layout in ("auto", "bits")
+        and plans
+        and all(p.kind == "spin_csr" for p in plans)
+        and n_chains % 256 == 0
+    ):
+        state_dtype = "bits"
+        for p in plans:
+            p.kind = "spin_bits"
+    elif spin_layout == "bits":
+        raise ValueError("spin_layout='bits' needs an all-spin program on the sparse kernel and n_chains % 256 == 0")
     return state_dtype, plans
 
 
@@ -623,7 +641,9 @@ def compile_program(
     n_chains = int(n_chains if n_chains is not None else config.n_chains)
     tdev = resolve_torch_device(device)
     lowered = lower_program(program)
-    state_dtype, plans = plan_program(lowered, n_chains, tdev, force_generic=force_generic)
+    state_dtype, plans = plan_program(
+        lowered, n_chains, tdev, force_generic=force_generic, spin_layout=config.spin_layout
+    )
     _torch().cuda.synchronize(tdev)  # tables uploaded before any stream uses them
     blocks = tuple(CompiledFusedBlock(spec=s, kernel_artifact=None) for s in lowered.specs)
     groups = tuple(

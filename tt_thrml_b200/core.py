@@ -30,6 +30,10 @@ class Family(str, Enum):
 
 
 RNG_MODES = ("philox", "parity")
+# State layout of all-spin programs: "bits" packs one bit per chain (needs a
+# multiple of 256 chains), "int8" one byte per chain; "auto" picks bits when
+# the chain count allows.
+SPIN_LAYOUTS = ("auto", "bits", "int8")
 
 
 @dataclass(frozen=True)
@@ -41,6 +45,7 @@ class CUDAConfig:
       variates following thrml's key tree (tt_thrml/rng.py:132-200).
     n_chains: independent chains per executor (the reference has one).
     cuda_graphs: capture multi-sweep runs in CUDA graphs.
+    spin_layout: state layout of all-spin programs ("auto", "bits", "int8").
     """
 
     artifact_root: Path
@@ -48,6 +53,7 @@ class CUDAConfig:
     rng_mode: str = "philox"
     n_chains: int = 1
     cuda_graphs: bool = True
+    spin_layout: str = "auto"
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "artifact_root", Path(self.artifact_root).resolve())
@@ -57,6 +63,8 @@ class CUDAConfig:
             raise ValueError("n_chains must be >= 1")
         if self.arch != "sm_100a":
             raise ValueError(f"only sm_100a is supported, got {self.arch!r}")
+        if self.spin_layout not in SPIN_LAYOUTS:
+            raise ValueError(f"spin_layout must be one of {SPIN_LAYOUTS}, got {self.spin_layout!r}")
 
     def cache_key(self) -> str:
         payload = {"arch": self.arch, "rng_mode": self.rng_mode}
@@ -200,10 +208,18 @@ def make_cuda_config(
     rng_mode: str = "philox",
     n_chains: int = 1,
     cuda_graphs: bool = True,
+    spin_layout: str = "auto",
 ) -> CUDAConfig:
     """Create a CUDA configuration (the CUDA counterpart of make_ttmlir_config)."""
     root = Path(artifact_root if artifact_root is not None else Path(tempfile.gettempdir()) / "tt-thrml-b200")
-    return CUDAConfig(artifact_root=root, arch=arch, rng_mode=rng_mode, n_chains=int(n_chains), cuda_graphs=cuda_graphs)
+    return CUDAConfig(
+        artifact_root=root,
+        arch=arch,
+        rng_mode=rng_mode,
+        n_chains=int(n_chains),
+        cuda_graphs=cuda_graphs,
+        spin_layout=spin_layout,
+    )
 
 
 def make_ttmlir_config(

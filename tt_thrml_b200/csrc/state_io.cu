@@ -100,6 +100,51 @@ __global__ void k_sum_rows(const S* __restrict__ state, int64_t C, int64_t row_s
 
 __global__ void k_ctl_advance(tthrml_run_ctl* c, uint32_t d) { c->sweep += d; }
 
+// Bit-packed spin state (TTHRML_STATE_BITS): row r = W words, bit c set = chain c is -1.
+template <typename I>
+__global__ void k_encode_bits(const I* __restrict__ in, int64_t n_rows, int64_t W, int64_t row_start,
+                              uint32_t* __restrict__ state) {
+  __shared__ float tile[32][33];  // [chain][row]
+  const int64_t r0 = (int64_t)blockIdx.x * 32, w = blockIdx.y;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t c = w * 32 + k, r = r0 + threadIdx.x;
+    tile[k][threadIdx.x] = r < n_rows ? (float)in[c * n_rows + r] : 1.0f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {  // warp y packs row r0 + k
+    const unsigned down = __ballot_sync(0xffffffffu, !(tile[threadIdx.x][k] > 0.0f));
+    if (threadIdx.x == 0 && r0 + k < n_rows) state[(row_start + r0 + k) * W + w] = down;
+  }
+}
+
+__global__ void k_decode_bits(const uint32_t* __restrict__ state, int64_t W, int64_t row_start, int64_t n_rows,
+                              int out_kind, void* __restrict__ out) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t C = W * 32;
+  if (r >= n_rows) return;
+  for (int64_t c = blockIdx.y; c < C; c += gridDim.y) {
+    const bool up = ((state[(row_start + r) * W + (c >> 5)] >> (c & 31)) & 1u) == 0u;
+    const int64_t o = c * n_rows + r;
+    if (out_kind == 0)
+      ((uint8_t*)out)[o] = up ? 1 : 0;
+    else if (out_kind == 1)
+      ((int32_t*)out)[o] = up ? 1 : -1;
+    else
+      ((float*)out)[o] = up ? 1.0f : -1.0f;
+  }
+}
+
+__global__ void k_sum_rows_bits(const uint32_t* __restrict__ state, int64_t W, int64_t row_start, int64_t n_rows,
+                                int64_t rows_per_strip, double* __restrict__ out) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= W * 32) return;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_strip;
+  const int64_t r1 = min(n_rows, r0 + rows_per_strip);
+  int64_t down = 0;
+  for (int64_t r = r0; r < r1; ++r) down += (state[(row_start + r) * W + (c >> 5)] >> (c & 31)) & 1u;
+  if (r1 > r0) atomicAdd(out + c, (double)((r1 - r0) - 2 * down));
+}
+
 }  // namespace
 }  // namespace tthrml
 
@@ -127,6 +172,15 @@ extern "C" int tthrml_decode_rows(const void* state, int32_t dtype, int64_t C, i
     return TTHRML_ERR_ARG;
   }
   cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == TTHRML_STATE_BITS) {
+    if (C % 32) {
+      set_error("tthrml_decode_rows: bit-packed state needs n_chains %% 32 == 0");
+      return TTHRML_ERR_ARG;
+    }
+    dim3 g((unsigned)((n_rows + 255) / 256), (unsigned)(C < 1024 ? C : 1024));
+    k_decode_bits<<<g, 256, 0, s>>>((const uint32_t*)state, C / 32, row_start, n_rows, out_kind, out);
+    return launch_status("k_decode_bits launch");
+  }
   if (dtype == TTHRML_STATE_F32)
     k_decode<float><<<grid, block, 0, s>>>((const float*)state, C, row_start, n_rows, out_kind, out);
   else if (dtype == TTHRML_STATE_I8)
@@ -155,6 +209,18 @@ extern "C" int tthrml_encode_rows(const void* in, int32_t in_dtype, int32_t as_s
   if (!in_f32 && in_dtype != TTHRML_STATE_I8) {
     set_error("tthrml_encode_rows: unknown input dtype %d", in_dtype);
     return TTHRML_ERR_ARG;
+  }
+  if (dtype == TTHRML_STATE_BITS) {
+    if (C % 32 || !as_spin) {
+      set_error("tthrml_encode_rows: bit-packed state holds spins only and needs n_chains %% 32 == 0");
+      return TTHRML_ERR_ARG;
+    }
+    dim3 g((unsigned)((n_rows + 31) / 32), (unsigned)(C / 32));
+    if (in_f32)
+      k_encode_bits<float><<<g, block, 0, s>>>((const float*)in, n_rows, C / 32, row_start, (uint32_t*)state);
+    else
+      k_encode_bits<int8_t><<<g, block, 0, s>>>((const int8_t*)in, n_rows, C / 32, row_start, (uint32_t*)state);
+    return launch_status("k_encode_bits launch");
   }
   if (dtype == TTHRML_STATE_F32) {
     if (in_f32)
@@ -191,6 +257,14 @@ extern "C" int tthrml_sum_rows(const void* state, int32_t dtype, int64_t C, int6
     return TTHRML_ERR_ARG;
   }
   cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == TTHRML_STATE_BITS) {
+    if (C % 32) {
+      set_error("tthrml_sum_rows: bit-packed state needs n_chains %% 32 == 0");
+      return TTHRML_ERR_ARG;
+    }
+    k_sum_rows_bits<<<grid, threads, 0, s>>>((const uint32_t*)state, C / 32, row_start, n_rows, rows_per_strip, out);
+    return launch_status("k_sum_rows_bits launch");
+  }
   if (dtype == TTHRML_STATE_F32)
     k_sum_rows<float><<<grid, threads, 0, s>>>((const float*)state, C, row_start, n_rows, rows_per_strip, out);
   else if (dtype == TTHRML_STATE_I8)

@@ -5,12 +5,15 @@ schedule semantics (load_state, prepare_rng, run_sweep, run_warmup, observe,
 sample_states, sample_with_observation, timing_summary, state_is_loaded,
 make_executor; executor.py:66-450).  What changes underneath:
 
-* the state is one torch CUDA tensor [total_nodes, n_chains], chain
-  innermost, int8 (spin / categorical programs) or float32 (programs with
-  gaussian blocks), and never leaves the GPU mid-sweep;
-* each group runs through libtthrml_b200 (`tthrml_spin_csr_step` or
-  `tthrml_group_step`) on the executor's stream; there is no host dispatch
-  layer, no per-call tensor wrapping and no CPU fallback;
+* the state is one torch CUDA tensor per executor, chain innermost, that
+  never leaves the GPU mid-sweep: bit-packed uint32 words [total_nodes,
+  n_chains/32] for all-spin programs with a multiple of 256 chains, int8
+  [total_nodes, n_chains] for other spin / categorical programs, float32 for
+  programs with gaussian blocks;
+* each group runs through libtthrml_b200 (`tthrml_spin_bits_step`,
+  `tthrml_spin_csr_step` or `tthrml_group_step`) on the executor's stream;
+  there is no host dispatch layer, no per-call tensor wrapping and no CPU
+  fallback;
 * Philox-mode variates are drawn inside the kernels; parity-mode variates are
   uploaded once per run like the reference's bulk buffers;
 * `run_sweeps(n)` replays the sweep loop from a captured CUDA graph.
@@ -83,10 +86,15 @@ class Executor:
             raise ValueError(f"compiled for {self.compiled.n_chains} chains, executor has {self.n_chains}")
         self._tdev = self.compiled.device or resolve_torch_device(device)
         self._lib = nat.lib()
+        # a stream of its own (CUDA graphs cannot be captured on the default stream)
         stream = getattr(device, "stream", None)
-        self._stream = stream if stream is not None else torch.cuda.current_stream(self._tdev)
-        self._state_code = nat.STATE_I8 if self.compiled.state_dtype == "int8" else nat.STATE_F32
-        self._torch_state_dtype = torch.int8 if self._state_code == nat.STATE_I8 else torch.float32
+        self._stream = stream if stream is not None else torch.cuda.Stream(device=self._tdev)
+        self._state_code = {"int8": nat.STATE_I8, "bits": nat.STATE_BITS}.get(self.compiled.state_dtype, nat.STATE_F32)
+        self._torch_state_dtype = {nat.STATE_I8: torch.int8, nat.STATE_BITS: torch.int32}.get(
+            self._state_code, torch.float32
+        )
+        # elements per state row: chains, or 32-chain words when bit-packed
+        self._row_len = self.n_chains // 32 if self._state_code == nat.STATE_BITS else self.n_chains
 
         self._global_state = None
         self._state_loaded = False
@@ -119,7 +127,7 @@ class Executor:
         torch = _torch()
         if self._global_state is None:
             self._global_state = torch.empty(
-                (self.compiled.total_nodes, self.n_chains), dtype=self._torch_state_dtype, device=self._tdev
+                (self.compiled.total_nodes, self._row_len), dtype=self._torch_state_dtype, device=self._tdev
             )
         return self._global_state
 
@@ -334,12 +342,13 @@ class Executor:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record(self._stream)
-        if plan.kind == "spin_csr":
+        if plan.kind in ("spin_csr", "spin_bits"):
+            step = self._lib.tthrml_spin_bits_step if plan.kind == "spin_bits" else self._lib.tthrml_spin_csr_step
             for blk in plan.blocks:
                 v = self._variates(blk.block_index)
                 vptr = None if v is None else v.data_ptr()
                 nat.check(
-                    self._lib.tthrml_spin_csr_step(
+                    step(
                         blk.row_ptr.data_ptr(),
                         blk.cols.data_ptr(),
                         blk.vals.data_ptr(),
@@ -356,7 +365,7 @@ class Executor:
                         ctl,
                         stream,
                     ),
-                    "tthrml_spin_csr_step",
+                    plan.kind,
                 )
         else:
             variates = None
@@ -389,6 +398,45 @@ class Executor:
             self._timing_log.append((plan.family_label, (t1 - t0) * 1000.0, ev0.elapsed_time(ev1)))
 
     # ------------------------------------------------------------- read-back
+
+    def raw_state(self) -> np.ndarray:
+        """The whole state as host float32 [total_nodes, n_chains] values (spins +-1)."""
+        torch = _torch()
+        out = torch.empty((self.n_chains, self.compiled.total_nodes), dtype=torch.float32, device=self._tdev)
+        nat.bind_device(self._tdev.index)
+        nat.check(
+            self._lib.tthrml_decode_rows(
+                self._global_state.data_ptr(), self._state_code, self.n_chains, 0, self.compiled.total_nodes, 2,
+                out.data_ptr(), nat.stream_handle(self._stream),
+            ),
+            "tthrml_decode_rows",
+        )
+        self._stream.synchronize()
+        return out.cpu().numpy().T.copy()
+
+    def set_raw_state(self, values: np.ndarray) -> None:
+        """Overwrites the whole state from host float32 [total_nodes, n_chains] values."""
+        torch = _torch()
+        src = torch.from_numpy(np.ascontiguousarray(np.asarray(values, np.float32).T)).to(self._tdev)
+        self._ensure_state()
+        nat.bind_device(self._tdev.index)
+        with torch.cuda.stream(self._stream):
+            pos = 0
+            for cb in self.compiled.blocks:
+                s = cb.spec
+                part = src[:, pos : pos + s.n_nodes].contiguous()
+                nat.check(
+                    self._lib.tthrml_encode_rows(
+                        part.data_ptr(), nat.STATE_F32, 1 if s.family == Family.SPIN else 0, s.n_nodes,
+                        self._state_code, self.n_chains, s.block_global_start, self._global_state.data_ptr(),
+                        nat.stream_handle(self._stream),
+                    ),
+                    "tthrml_encode_rows",
+                )
+                part.record_stream(self._stream)
+                pos += s.n_nodes
+        self._stream.synchronize()
+        self._state_loaded = True
 
     def _pinned_buffer(self, key, shape, dtype):
         torch = _torch()
