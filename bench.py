@@ -58,18 +58,26 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _traffic_per_launch():
-    """DRAM bytes per spin_csr launch from the committed ncu summary, when present."""
-    f = ROOT / "profiles" / "spin_csr_er1m_c256.md"
+def _traffic_per_launch(avg_algorithmic_bytes: float):
+    """DRAM bytes of an average sparse-spin launch, from the committed ncu summary.
+
+    The summary holds one captured launch (DRAM read + write bytes and its
+    algorithmic bytes); the figure is scaled to the average launch of a sweep
+    by algorithmic bytes.  None when no summary is committed.
+    """
+    f = ROOT / "profiles" / "spin_bits_er1m_c256.md"
     if not f.exists():
         return None
+    vals = {}
     for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if ":" in line and line.split(":", 1)[0] in ("traffic_bytes_per_launch", "algorithmic_bytes_captured_launch"):
             try:
-                return float(line.split(":", 1)[1].strip())
+                vals[line.split(":", 1)[0]] = float(line.split(":", 1)[1].strip())
             except ValueError:
                 return None
-    return None
+    if len(vals) != 2:
+        return None
+    return vals["traffic_bytes_per_launch"] * avg_algorithmic_bytes / vals["algorithmic_bytes_captured_launch"]
 
 
 class ClockSampler:
@@ -292,7 +300,7 @@ def run_ours(args):
     launch_bytes = per_block_bytes * n_prof
     achieved = sum(launch_bytes) / (sum(kernel_ms) / 1000.0) / 1e9
     peak, peak_kind = _peaks()
-    traffic = _traffic_per_launch()
+    traffic = _traffic_per_launch(sum(per_block_bytes) / len(per_block_bytes)) if layout == "bits" else None
 
     # ---- end to end through the public API (pinned host state in, final state out)
     from tt_thrml_b200.observers import StateObserver
