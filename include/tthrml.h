@@ -137,6 +137,31 @@ typedef struct tthrml_group {
 int tthrml_group_step(const tthrml_group* group_host, void* stream);
 
 /*
+ * Allocation-free tthrml_group_step.  It has no counterpart in the reference.
+ *
+ * tthrml_group_step wants a caller buffer for `scratch` whenever a group
+ * reads its own rows.  Callers that cannot provide one, such as a plugin or
+ * FFI host that owns every buffer it passes and has no device allocator to
+ * lend, or a running control loop that must not call cudaMalloc (it can
+ * synchronise the whole device), use this entry point instead: `scratch` in
+ * the descriptor is ignored and the staging area is a device array inside
+ * this library of TTHRML_STATIC_SCRATCH_BYTES, which every GPU that loads the
+ * library holds until the process exits.  Groups needing more
+ * (group_rows * n_chains * element size) are rejected with TTHRML_ERR_ARG.
+ * No memory is allocated and no allocating routine is called.
+ *
+ * The first call on a device looks up the array's device address there
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  Every call shares the one array and the array
+ * keeps the last call's contents; nothing has to start at zero because the
+ * step writes every scratch element before it reads it back.  Calls whose
+ * kernels overlap on the GPU race on the array: serialise them (one stream,
+ * or events) per device.
+ */
+#define TTHRML_STATIC_SCRATCH_BYTES (16u << 20)
+int tthrml_group_step_static_scratch(const tthrml_group* group_host, void* stream);
+
+/*
  * Sparse spin block (pairwise spin couplings + bias) on int8 ±1 state:
  * gamma = bias + sum_e w_e * s[col_e], s = +1 where 2*gamma > logit(u).
  * Reference: _accumulate_gamma + _sample_spin_block

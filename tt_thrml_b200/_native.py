@@ -79,6 +79,7 @@ class GroupDesc(ctypes.Structure):
 # (name, restype, argtypes) of every exported entry point.
 _SIGNATURES = {
     "tthrml_group_step": (c_i32, [ctypes.POINTER(GroupDesc), c_vp]),
+    "tthrml_group_step_static_scratch": (c_i32, [ctypes.POINTER(GroupDesc), c_vp]),
     "tthrml_spin_csr_step": (
         c_i32,
         [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp, c_vp],

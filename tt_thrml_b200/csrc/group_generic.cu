@@ -264,3 +264,89 @@ extern "C" int tthrml_group_step(const tthrml_group* g, void* stream) {
   set_error("tthrml_group_step: unknown state dtype %d", g->state_dtype);
   return TTHRML_ERR_ARG;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free group step.
+//
+// tthrml_group_step needs a caller-provided scratch buffer whenever a group
+// reads its own rows: every block samples from the pre-group state, so new
+// values are staged and committed afterwards.  Some hosts cannot hand one over:
+// a plugin or FFI host that gives the library only the buffers it owns and has
+// no device allocator to lend, or a control loop that must not call cudaMalloc
+// (which can synchronise the whole device) once it is running.  For them the
+// staging area is this library's own file-scope device array, reserved on
+// every GPU when the library's device code is loaded and kept until exit.
+// Each call resolves the array's device address for the current device (once
+// per device, on the first call there) and runs the same kernels as
+// tthrml_group_step with it.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace tthrml {
+namespace {
+
+__device__ __align__(256) unsigned char g_static_scratch[TTHRML_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxScratchDevices = 256;
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_addr[kMaxScratchDevices];  // device address per device ordinal, resolved once
+
+// Device address of g_static_scratch on the current device.  Host code only
+// sees a host-side stand-in under the array's name, so the address must come
+// from cudaGetSymbolAddress with that device current.
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "tthrml_group_step_static_scratch: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxScratchDevices) {
+    set_error("tthrml_group_step_static_scratch: device ordinal %d is beyond the %d supported", dev,
+              kMaxScratchDevices);
+    return TTHRML_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (!g_static_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "tthrml_group_step_static_scratch: cudaGetSymbolAddress");
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = g_static_scratch_addr[dev];
+  return TTHRML_OK;
+}
+
+}  // namespace
+}  // namespace tthrml
+
+extern "C" int tthrml_group_step_static_scratch(const tthrml_group* g, void* stream) {
+  using namespace tthrml;
+  if (!g || !g->blocks || !g->state || g->n_blocks <= 0 || g->n_chains <= 0 || g->group_rows < 0) {
+    set_error("tthrml_group_step_static_scratch: invalid group descriptor");
+    return TTHRML_ERR_ARG;
+  }
+  if (g->chain_offset % 4) {
+    set_error("tthrml_group_step_static_scratch: chain_offset must be a multiple of 4");
+    return TTHRML_ERR_ARG;
+  }
+  int64_t elem = 0;
+  if (g->state_dtype == TTHRML_STATE_F32) elem = 4;
+  if (g->state_dtype == TTHRML_STATE_I8) elem = 1;
+  if (!elem) {
+    set_error("tthrml_group_step_static_scratch: unknown state dtype %d", g->state_dtype);
+    return TTHRML_ERR_ARG;
+  }
+  const int64_t need = g->group_rows * g->n_chains * elem;
+  if (g->group_rows > 0 && (need / g->group_rows / g->n_chains != elem || need > (int64_t)TTHRML_STATIC_SCRATCH_BYTES)) {
+    set_error("tthrml_group_step_static_scratch: the group needs %lld bytes of scratch (%lld rows x %lld chains x "
+              "%lld B) but the static scratch holds %lld bytes; use tthrml_group_step with a caller buffer",
+              (long long)need, (long long)g->group_rows, (long long)g->n_chains, (long long)elem,
+              (long long)TTHRML_STATIC_SCRATCH_BYTES);
+    return TTHRML_ERR_ARG;
+  }
+  void* scratch = nullptr;
+  const int rc = static_scratch_address(&scratch);
+  if (rc) return rc;
+  tthrml_group local = *g;
+  local.scratch = scratch;
+  cudaStream_t s = (cudaStream_t)stream;
+  return elem == 4 ? launch_group<float>(local, s) : launch_group<int8_t>(local, s);
+}
