@@ -198,6 +198,32 @@ int tthrml_spin_bits_step(const int64_t* row_ptr_dev, const int32_t* cols_dev, c
                           void* stream);
 
 /*
+ * Dense bipartite block update on the tensor cores (tcgen05, bf16 operands,
+ * fp32 accumulation in TMEM).  Replaces the group kernel of a block whose
+ * interaction with another block is a dense weight matrix (the RBM case:
+ * per-node weight rows over every source unit, tt_thrml/compiler.py:173-176,
+ * 303-365):
+ *   field[m][n] = sum_k source_state[m][k] * weights_nk[n][k] + bias[n]
+ * source_state: bf16 [n_chains][n_sources] (chain-major), weights_nk: bf16
+ * [n_units][n_sources]; the target block's new state is written to out_state
+ * (bf16 [n_chains][n_units]) and, when out_state_f32 is not NULL, to float32.
+ * family TTHRML_SPIN draws +1 with probability sigmoid(2*field) (variates:
+ * 2*field > logit); TTHRML_GAUSSIAN draws field*var + sqrt(var)*xi with
+ * var = 1/(precision + 1e-6).  Philox counters: (chain/4, row0 + unit, sweep)
+ * for spins, (chain, row0 + unit, sweep) for gaussians, as in the other
+ * kernels.  variates: [variates_sweeps][n_units][n_chains] or NULL.
+ * Requires n_chains % 128 == 0, n_units % 256 == 0, n_sources % 64 == 0 and
+ * 16-byte aligned buffers.  Waits inside the kernel are bounded: a device
+ * error word (*error, zero on entry) receives a non-zero code if one expired.
+ */
+int tthrml_dense_field_sample(const void* source_state, const void* weights_nk, int64_t n_chains,
+                              int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
+                              float precision, void* out_state, float* out_state_f32, int64_t row0,
+                              int64_t chain_offset, const float* variates, int64_t variates_sweeps,
+                              uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int32_t* error,
+                              void* stream);
+
+/*
  * Adds `delta` to ctl->sweep on `stream` (the last node of a captured
  * multi-sweep CUDA graph, so each replay continues the run).
  */

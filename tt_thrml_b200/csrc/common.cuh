@@ -30,6 +30,11 @@ inline int launch_status(const char* what) { return cuda_status(cudaGetLastError
 constexpr uint32_t kSaltSpin = 0x5350494eu;      // "SPIN"
 constexpr uint32_t kSaltGauss = 0x47415553u;     // "GAUS"
 constexpr uint32_t kSaltCat = 0x43415400u;       // "CAT\0" + (category / 4)
+// Dense (tensor-core) blocks draw along the unit axis of one chain: counter
+// (chain, row/4, sweep, salt) gives the spins of four consecutive rows,
+// (chain, row/2, sweep, salt) the two uniforms of two gaussian rows.
+constexpr uint32_t kSaltDenseSpin = 0x44535049u;   // "DSPI"
+constexpr uint32_t kSaltDenseGauss = 0x44474155u;  // "DGAU"
 
 struct u32x4 {
   uint32_t x, y, z, w;
