@@ -1,23 +1,29 @@
 """Benchmark of the block-Gibbs sweep path (node-updates/s).
 
-Workload (the sparse random-graph Ising configuration): Erdos-Renyi graph
-with N = 2^20 nodes and mean degree 8, J_ij ~ N(0, 1/8) symmetric, h_i ~ N(0,
-0.1) (variances), beta = 1, greedy colouring into k blocks (one sampling group
-each), 256 chains per GPU, seeded synthetic data.  One bench step = one run of
-200 sweeps over all k groups for all chains of every GPU.
+Default workload (`--workload er`, the headline: the sparse random-graph
+Ising configuration): Erdos-Renyi graph with N = 2^20 nodes and mean degree 8,
+J_ij ~ N(0, 1/8) symmetric, h_i ~ N(0, 0.1) (variances), beta = 1, greedy
+colouring into k blocks (one sampling group each), 256 chains per GPU, seeded
+synthetic data.  One bench step = one run of 200 sweeps over all k groups for
+all chains of every GPU.  Other workloads: `--workload rbm` (Gauss-Bernoulli
+RBM, 4096 gaussian visible x 8192 spin hidden, 8192 chains, 100 sweeps per
+step; tensor-core roofline) and `--workload lattice` (64x64 Ising, 1024
+chains, the schedule n_warmup=32 n_samples=64 steps_per_sample=2 per step).
 
-* `value`: steps on device-resident state (CUDA-graph replay of 200 sweeps),
-  one CUDA event pair per step on the executor's stream, barrier + synchronize
-  on both sides, max over ranks.  The bit-packed state (32 MiB) and the CSR
-  tables fit in L2, so L2 is flushed (256 MiB write) before every step,
-  outside the timed windows.
+* `value`: steps on device-resident state (CUDA-graph replay of the step's
+  sweeps), one CUDA event pair per step on the executor's stream, barrier +
+  synchronize on both sides, max over ranks.  L2 is flushed (256 MiB write)
+  before every step, outside the timed windows.
 * `e2e`: the same metric through the public API: each step is one
-  `Executor.sample_states` call (pinned host initial state -> 200 sweeps ->
-  final state back on the host), wall clock with synchronize on both sides.
-* `roofline`: the sparse spin kernel, algorithmic bytes per launch (neighbour
-  state rows read, own row written, CSR tables read once; a row is 32 B
-  bit-packed or 256 B as int8) over the CUDA-event duration of each launch,
-  against the measured HBM copy bandwidth.
+  `Executor.sample_states` call (pinned host initial state -> the sweeps ->
+  final state back on the host; for the lattice, `sample_with_observation`
+  with the magnetisation observed on device), wall clock with synchronize on
+  both sides.
+* `roofline`: the step's dominant kernel over per-launch CUDA events of eager
+  sweeps: algorithmic bytes (sparse spin kernel: neighbour state rows read,
+  own row written, CSR tables read once) against the measured HBM copy
+  bandwidth, or algorithmic FLOPs (dense kernel: 2 x chains x visible x
+  hidden per GEMM, two per sweep) against the measured bf16 GEMM peak.
 * `cpu_baseline`: the CPU oracle (C restatement of the reference's group
   math) on this host's cores over a bounded sample of the same workload.
 
@@ -41,21 +47,222 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parent
-N_NODES = 1 << 20
-MEAN_DEGREE = 8.0
-CHAINS_PER_GPU = 256
-SWEEPS_PER_STEP = 200
 SEED = 0
-WORKLOAD = "er-ising-n1048576-deg8-c256pergpu-s200"
-METRIC = "node-updates/sec (sites x chains x sweeps / s)"
+
+
+class ErIsing:
+    """Sparse random-graph Ising: N = 2^20, Erdos-Renyi mean degree 8, greedy colouring, 256 chains/GPU, 200 sweeps."""
+
+    name = "er"
+    workload = "er-ising-n1048576-deg8-c256pergpu-s200"
+    metric = "node-updates/sec (sites x chains x sweeps / s)"
+    chains = 256
+    sweeps = 200
+    data = "synthetic (seeded Erdos-Renyi graph, random init)"
+    cpu_chains, cpu_sweeps = 32, 1
+
+    def build(self):
+        from tt_thrml_b200 import workloads
+
+        return workloads.erdos_renyi_ising(1 << 20, 8.0, seed=SEED)
+
+    def init(self, prog, C, seed):
+        rng = np.random.default_rng(seed)
+        return [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
+
+    def host_inputs(self, init):
+        import torch
+
+        return [torch.from_numpy(s.astype(np.int8) * 2 - 1).pin_memory() for s in init]
+
+    def check(self, ex):
+        kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
+        assert kinds <= {"spin_csr", "spin_bits"}, kinds
+
+    def config(self, prog, ex, world):
+        return {
+            "workload": self.workload,
+            "n_nodes": _n_nodes(prog),
+            "mean_degree": 8.0,
+            "colour_blocks": len(prog.specs),
+            "chains_per_gpu": self.chains,
+            "sweeps_per_step": self.sweeps,
+            "rng": "philox4x32-10 on device",
+            "state_layout": ex.compiled.state_dtype,
+            "l2": "flushed before every timed step (256 MiB write)",
+            "parallelism": f"chain-sharded x{world}",
+        }
+
+    def dtype(self, ex):
+        return "u32 bit-packed spins, f32 fields" if ex.compiled.state_dtype == "bits" else "int8 spins, f32 fields"
+
+    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof):
+        layout = ex.compiled.state_dtype
+        per_block = algorithmic_bytes(prog, C, layout)
+        achieved = sum(per_block) * n_prof / (sum(kernel_ms_per_group) / 1000.0) / 1e9
+        peak, kind = _peaks()["hbm"]
+        traffic = _traffic_per_launch(sum(per_block) / len(per_block)) if layout == "bits" else None
+        return {
+            "kernel": "k_spin_bits" if layout == "bits" else "k_spin_csr_async",
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_source": kind,
+            "traffic": traffic,
+            "algorithmic_bytes_per_update": sum(per_block) / (_n_nodes(prog) * C),
+        }
+
+
+class GaussBernoulliRBM:
+    """Gauss-Bernoulli RBM: 4096 gaussian visible x 8192 spin hidden, W ~ N(0, 0.01^2), 8192 chains, 100 sweeps."""
+
+    name = "rbm"
+    workload = "gauss-bernoulli-rbm-v4096-h8192-c8192-s100"
+    metric = "node-updates/sec (sites x chains x sweeps / s)"
+    chains = 8192
+    sweeps = 100
+    data = "synthetic (seeded RBM weights rounded to bf16, random init)"
+    cpu_chains, cpu_sweeps = 8, 1
+    V, H = 4096, 8192
+
+    def build(self):
+        from tt_thrml_b200 import workloads
+
+        return workloads.gaussian_bernoulli_rbm(self.V, self.H, seed=SEED)
+
+    def init(self, prog, C, seed):
+        rng = np.random.default_rng(seed)
+        return [rng.standard_normal((C, self.V)).astype(np.float32), rng.integers(0, 2, (C, self.H)).astype(bool)]
+
+    def host_inputs(self, init):
+        import torch
+
+        return [torch.from_numpy(init[0]).pin_memory(), torch.from_numpy(init[1]).pin_memory()]
+
+    def check(self, ex):
+        kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
+        assert kinds == {"dense"}, kinds
+
+    def config(self, prog, ex, world):
+        return {
+            "workload": self.workload,
+            "n_visible": self.V,
+            "n_hidden": self.H,
+            "chains_per_gpu": self.chains,
+            "sweeps_per_step": self.sweeps,
+            "rng": "philox4x32-10 on device",
+            "state_layout": "bf16 chain-major blocks (tcgen05 GEMM operands)",
+            "l2": "operands (64-128 MiB per launch) exceed L2; flushed before every timed step (256 MiB write)",
+            "parallelism": f"chain-sharded x{world}",
+        }
+
+    def dtype(self, ex):
+        return "bf16 operands, f32 accumulate (tcgen05)"
+
+    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof):
+        flops = 2.0 * 2.0 * C * self.V * self.H * n_prof  # two GEMMs per sweep
+        achieved = flops / (sum(kernel_ms_per_group) / 1000.0) / 1e12
+        peaks = _peaks()
+        peak, kind = peaks["bf16"]
+        return {
+            "kernel": "k_dense_field_sample",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": achieved / peak,
+            "peak_source": kind + " burst (kernels timed launch by launch)",
+            "frac_of_sustained": achieved / peaks["bf16_sustained"][0],
+            "traffic": _dense_traffic_per_launch(),
+            "algorithmic_flops_per_update": 2.0 * 2.0 * self.V * self.H / (self.V + self.H),
+        }
+
+
+class Lattice2D:
+    """2-D Ising 64x64 periodic, J=1, h=0, beta=0.44, 1024 chains; one step = the sampling schedule
+    n_warmup=32, n_samples=64, steps_per_sample=2 with the per-chain magnetisation observed on device."""
+
+    name = "lattice"
+    workload = "ising2d-64x64-c1024-w32-n64-s2"
+    metric = "node-updates/sec (sites x chains x sweeps / s)"
+    chains = 1024
+    sweeps = 32 + 63 * 2
+    data = "synthetic (uniform +-1 init from seed 0)"
+    cpu_chains, cpu_sweeps = 1024, 4
+
+    def build(self):
+        from tt_thrml_b200 import workloads
+
+        return workloads.ising_lattice_2d(64, 64, J=1.0, h=0.0, beta=0.44)
+
+    def init(self, prog, C, seed):
+        rng = np.random.default_rng(seed)
+        return [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
+
+    def host_inputs(self, init):
+        import torch
+
+        return [torch.from_numpy(s.astype(np.int8) * 2 - 1).pin_memory() for s in init]
+
+    def check(self, ex):
+        kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
+        assert kinds <= {"spin_csr", "spin_bits"}, kinds
+
+    def config(self, prog, ex, world):
+        return {
+            "workload": self.workload,
+            "lattice": "64x64 periodic",
+            "chains_per_gpu": self.chains,
+            "sweeps_per_step": self.sweeps,
+            "observable": "per-chain magnetisation, 64 samples, summed on device",
+            "state_layout": ex.compiled.state_dtype,
+            "l2": "state (512 KiB) is L2-resident by design; flushed before every timed step (256 MiB write)",
+            "parallelism": f"chain-sharded x{world}",
+        }
+
+    def dtype(self, ex):
+        return ErIsing.dtype(self, ex)
+
+    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof):
+        return ErIsing.roofline(self, ex, prog, C, kernel_ms_per_group, n_prof) | {"traffic": None}
+
+
+WORKLOADS = {w.name: w for w in (ErIsing(), GaussBernoulliRBM(), Lattice2D())}
+
+
+def _n_nodes(prog):
+    return sum(len(b.nodes) for b in prog.gibbs_spec.blocks)
 
 
 def _peaks():
+    """Roofline denominators: (value, "measured" | "fallback") per kind."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return {
+            "hbm": (float(d["hbm_gbs"]), "measured"),
+            "bf16": (float(d["bf16_tflops"]), "measured"),
+            "bf16_sustained": (float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"),
+        }
+    return {"hbm": (6650.0, "fallback"), "bf16": (1590.0, "fallback"), "bf16_sustained": (1400.0, "fallback")}
+
+
+def _profile_figures(name: str, keys):
+    """Machine-readable `key: value` lines of a committed ncu summary, or None."""
+    f = ROOT / "profiles" / name
+    if not f.exists():
+        return None
+    vals = {}
+    for line in f.read_text().splitlines():
+        k = line.split(":", 1)[0]
+        if ":" in line and k in keys:
+            try:
+                vals[k] = float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return vals if len(vals) == len(keys) else None
 
 
 def _traffic_per_launch(avg_algorithmic_bytes: float):
@@ -65,19 +272,18 @@ def _traffic_per_launch(avg_algorithmic_bytes: float):
     algorithmic bytes); the figure is scaled to the average launch of a sweep
     by algorithmic bytes.  None when no summary is committed.
     """
-    f = ROOT / "profiles" / "spin_bits_er1m_c256.md"
-    if not f.exists():
-        return None
-    vals = {}
-    for line in f.read_text().splitlines():
-        if ":" in line and line.split(":", 1)[0] in ("traffic_bytes_per_launch", "algorithmic_bytes_captured_launch"):
-            try:
-                vals[line.split(":", 1)[0]] = float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    if len(vals) != 2:
+    vals = _profile_figures(
+        "spin_bits_er1m_c256.md", ("traffic_bytes_per_launch", "algorithmic_bytes_captured_launch")
+    )
+    if vals is None:
         return None
     return vals["traffic_bytes_per_launch"] * avg_algorithmic_bytes / vals["algorithmic_bytes_captured_launch"]
+
+
+def _dense_traffic_per_launch():
+    """DRAM bytes of an average dense launch of the RBM sweep, from the committed ncu summary (None if absent)."""
+    vals = _profile_figures("dense_tc_rbm.md", ("traffic_bytes_per_launch_full_size",))
+    return None if vals is None else vals["traffic_bytes_per_launch_full_size"]
 
 
 class ClockSampler:
@@ -141,12 +347,6 @@ class ClockSampler:
         }
 
 
-def build_workload():
-    from tt_thrml_b200 import workloads
-
-    return workloads.erdos_renyi_ising(N_NODES, MEAN_DEGREE, seed=SEED)
-
-
 def algorithmic_bytes(prog, n_chains: int, layout: str):
     """Per block launch: state bytes (each neighbour row read once, own row written once) plus the
     CSR tables read once (8 B per edge: column + weight; 4 B bias and 8 B offset per row).
@@ -160,41 +360,45 @@ def algorithmic_bytes(prog, n_chains: int, layout: str):
     return out
 
 
-def cpu_oracle_sample(prog, n_chains: int, n_sweeps: int, threads: int):
+def cpu_oracle_sample(W, prog, n_chains: int, n_sweeps: int, threads: int):
     """Times the CPU oracle on `n_sweeps` full sweeps of `n_chains` chains; returns (updates/s, seconds)."""
     sys.path.insert(0, str(ROOT))
     from oracle import oracle as orc
 
     o = orc.OracleSampler(prog, n_chains=n_chains, n_threads=threads)
-    rng = np.random.default_rng(1)
-    o.load_state([rng.integers(0, 2, (n_chains, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks])
+    o.load_state(W.init(prog, n_chains, 1))
     o.sweep(0, seed=7)  # warm
     t0 = time.perf_counter()
     for s in range(n_sweeps):
         o.sweep(1 + s, seed=7)
     dt = time.perf_counter() - t0
-    return N_NODES * n_chains * n_sweeps / dt, dt
+    return _n_nodes(prog) * n_chains * n_sweeps / dt, dt
 
 
-def run_reference(args):
+def _cpu_sample_text(W, prog, chains, sweeps):
+    return (f"CPU oracle (C restatement, float32 state), {_n_nodes(prog)} nodes x {chains} chains x "
+            f"{sweeps} sweep(s) per sample")
+
+
+def run_reference(args, W):
     """CPU arm: the oracle restatement of the reference's group kernel on all host cores."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    prog = build_workload()
-    chains = 32  # bounded sample: all 2^20 nodes, 32 chains, one sweep per step
+    prog = W.build()
+    chains, sweeps = W.cpu_chains, W.cpu_sweeps  # bounded sample of the workload per step
     for _ in range(args.warmup):
-        cpu_oracle_sample(prog, chains, 1, threads)
+        cpu_oracle_sample(W, prog, chains, sweeps, threads)
     times = []
     for _ in range(args.steps):
-        _, dt = cpu_oracle_sample(prog, chains, 1, threads)
+        _, dt = cpu_oracle_sample(W, prog, chains, sweeps, threads)
         times.append(dt)
     tot = sum(times)
-    value = N_NODES * chains * args.steps / tot
+    value = _n_nodes(prog) * chains * sweeps * args.steps / tot
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": W.metric,
         "value": value,
         "unit": "node-updates/s",
         "n_gpus": args.gpus,
@@ -205,14 +409,15 @@ def run_reference(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic (seeded Erdos-Renyi graph, random init)",
-        "config": {"workload": WORKLOAD, "sample": f"all {N_NODES} nodes x {chains} chains x 1 sweep per step"},
+        "data": W.data,
+        "config": {"workload": W.workload, "sample": f"all {_n_nodes(prog)} nodes x {chains} chains x {sweeps} "
+                                                      "sweep(s) per step"},
         "cpu_baseline": {
             "value": value,
             "unit": "node-updates/s",
             "cores": threads,
             "kind": "port",
-            "sample": f"CPU oracle (C restatement, float32 state), {N_NODES} nodes x {chains} chains, 1 sweep/step",
+            "sample": _cpu_sample_text(W, prog, chains, sweeps),
         },
         "e2e": {"value": value, "unit": "node-updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -220,7 +425,7 @@ def run_reference(args):
     return 0
 
 
-def run_ours(args):
+def run_ours(args, W):
     import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -239,18 +444,18 @@ def run_ours(args):
 
     from tt_thrml_b200 import Executor, make_cuda_config
     from tt_thrml_b200.backend import CudaDevice
+    from tt_thrml_b200.observers import MagnetizationObserver
 
-    prog = build_workload()
-    k = len(prog.specs)
-    C = CHAINS_PER_GPU
+    prog = W.build()
+    n_nodes = _n_nodes(prog)
+    C, S = W.chains, W.sweeps
     device = CudaDevice(local)
     cfg = make_cuda_config(n_chains=C, cuda_graphs=True)
-    total_sweeps = SWEEPS_PER_STEP * (args.steps + args.warmup) + 16
+    total_sweeps = S * (args.steps + args.warmup) + 16
     ex = Executor(None, device, prog, cfg, n_sweeps=total_sweeps, n_chains=C, chain_offset=rank * C)
-    kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
-    assert kinds <= {"spin_csr", "spin_bits"}, kinds
-    rng = np.random.default_rng(100 + rank)
-    init = [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
+    W.check(ex)
+    n_groups = len(ex.compiled.sampling_groups)
+    init = W.init(prog, C, 100 + rank)
     ex.load_state(init, [])
     ex.prepare_rng(SEED)
     stream = ex.stream
@@ -262,11 +467,10 @@ def run_ours(args):
 
     # ---- device-resident steps: warmup, then K timed steps
     for _ in range(args.warmup):
-        ex.run_sweeps(SWEEPS_PER_STEP)
+        ex.run_sweeps(S)
     barrier()
     # Each step is timed by its own event pair; between steps a 256 MiB buffer is
-    # written so every step starts with a cold L2 (the bit-packed state and the
-    # CSR tables together fit in the 126 MB L2).
+    # written so every step starts with a cold L2 (126 MB).
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
@@ -274,22 +478,21 @@ def run_ours(args):
             with torch.cuda.stream(stream):
                 flush.fill_(1)
             e0.record(stream)
-            ex.run_sweeps(SWEEPS_PER_STEP)
+            ex.run_sweeps(S)
             e1.record(stream)
         barrier()
+    ex.check_device_errors()
     dt_ms = sum(e0.elapsed_time(e1) for e0, e1 in events)
     del flush
     if dist is not None:
         t = torch.tensor([dt_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt_ms = float(t.item())
-    updates = world * N_NODES * C * SWEEPS_PER_STEP * args.steps
+    updates = world * n_nodes * C * S * args.steps
     value = updates / (dt_ms / 1000.0)
-    gpu_launches = args.steps * (SWEEPS_PER_STEP * k + 1)
+    gpu_launches = args.steps * (S * n_groups + 1)  # group kernels + the run-control advance of each graph
 
     # ---- roofline: per-launch CUDA events on the launch stream (eager sweeps)
-    layout = ex.compiled.state_dtype
-    per_block_bytes = algorithmic_bytes(prog, C, layout)
     ex.profile = True
     ex._timing_log.clear()
     n_prof = 5
@@ -297,54 +500,61 @@ def run_ours(args):
         ex.run_sweep()
     ex.profile = False
     kernel_ms = [kms for _, _, kms in ex._timing_log]
-    launch_bytes = per_block_bytes * n_prof
-    achieved = sum(launch_bytes) / (sum(kernel_ms) / 1000.0) / 1e9
-    peak, peak_kind = _peaks()
-    traffic = _traffic_per_launch(sum(per_block_bytes) / len(per_block_bytes)) if layout == "bits" else None
+    roofline = W.roofline(ex, prog, C, kernel_ms, n_prof)
 
-    # ---- end to end through the public API (pinned host state in, final state out)
-    from tt_thrml_b200.observers import StateObserver
-
-    pinned = [torch.from_numpy(s.astype(np.int8) * 2 - 1).pin_memory() for s in init]
-
-    class _Sched:
-        n_warmup, n_samples, steps_per_sample = SWEEPS_PER_STEP, 1, 1
-
+    # ---- end to end through the public API (pinned host state in, results out)
+    host_init = W.host_inputs(init)
+    h2d = sum(t.numel() * t.element_size() for t in host_init)
     nodes = prog.gibbs_spec.free_blocks
-    ex.sample_states(SEED + 1, _Sched, nodes, init_state_free=pinned)  # warm the graph for this schedule
+    from types import SimpleNamespace
+
+    if W.name == "lattice":
+        sched = SimpleNamespace(n_warmup=32, n_samples=64, steps_per_sample=2)
+        obs = MagnetizationObserver(nodes)
+
+        def e2e_call(key):
+            _, m = ex.sample_with_observation(key, sched, obs, init_state_free=host_init)
+            return [m]  # float64 magnetisation per chain per sample
+    else:
+        sched = SimpleNamespace(n_warmup=S, n_samples=1, steps_per_sample=1)
+
+        def e2e_call(key):
+            return ex.sample_states(key, sched, nodes, init_state_free=host_init)
+
+    e2e_call(SEED + 1)  # warm the graph for this schedule
     barrier()
     e2e_times = []
     for s in range(args.steps):
         barrier()
         t0 = time.perf_counter()
-        out = ex.sample_states(SEED + 2 + s, _Sched, nodes, init_state_free=pinned)
+        out = e2e_call(SEED + 2 + s)
         torch.cuda.synchronize(dev)
         e2e_times.append(time.perf_counter() - t0)
-    assert out[0].shape == (1, C, len(nodes[0].nodes))
+    d2h = int(sum(np.asarray(a).nbytes for a in out))  # bytes the call returned to the host
+    del out
+    ex.check_device_errors()
     e2e_s = sum(e2e_times)
     if dist is not None:
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e_value = updates / e2e_s
-    h2d = N_NODES * C  # int8 ±1 initial state
-    d2h = N_NODES * C  # bool final state
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        v, _ = cpu_oracle_sample(prog, 32, 1, threads)
+        v, _ = cpu_oracle_sample(W, prog, W.cpu_chains, W.cpu_sweeps, threads)
         cpu = {
             "value": v,
             "unit": "node-updates/s",
             "cores": threads,
             "kind": "port",
-            "sample": f"CPU oracle (C restatement, float32 state), {N_NODES} nodes x 32 chains x 1 sweep",
+            "sample": _cpu_sample_text(W, prog, W.cpu_chains, W.cpu_sweeps),
         }
 
     if rank == 0:
         line = {
-            "metric": METRIC,
+            "metric": W.metric,
             "value": value,
             "unit": "node-updates/s",
             "n_gpus": world,
@@ -354,31 +564,10 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "u32 bit-packed spins, f32 fields" if ex.compiled.state_dtype == "bits" else "int8 spins, f32 fields",
-            "data": "synthetic (seeded Erdos-Renyi graph, random init)",
-            "config": {
-                "workload": WORKLOAD,
-                "n_nodes": N_NODES,
-                "mean_degree": MEAN_DEGREE,
-                "colour_blocks": k,
-                "chains_per_gpu": C,
-                "sweeps_per_step": SWEEPS_PER_STEP,
-                "rng": "philox4x32-10 on device",
-                "state_layout": ex.compiled.state_dtype,
-                "l2": "flushed before every timed step (256 MiB write)",
-                "parallelism": f"chain-sharded x{world}",
-            },
-            "roofline": {
-                "kernel": "k_spin_bits" if layout == "bits" else "k_spin_csr_async",
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "peak_source": peak_kind,
-                "traffic": traffic,
-                "algorithmic_bytes_per_update": sum(per_block_bytes) / (N_NODES * C),
-            },
+            "dtype": W.dtype(ex),
+            "data": W.data,
+            "config": W.config(prog, ex, world),
+            "roofline": roofline,
             "e2e": {
                 "value": e2e_value,
                 "unit": "node-updates/s",
@@ -402,35 +591,41 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="er",
+                    help="er: sparse random-graph Ising (default, the headline); rbm: Gauss-Bernoulli RBM; "
+                         "lattice: 64x64 Ising with magnetisation samples")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-sweeps", type=int, default=0,
                     help="run this many eager sweeps of the workload and exit (profiler target, no timing)")
+    ap.add_argument("--chains", type=int, default=0, help="profiler target only: chains (default: the workload's)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    W = WORKLOADS[args.workload]
     if args.impl == "reference":
-        return run_reference(args)
+        return run_reference(args, W)
     if args.profile_sweeps:
-        return run_profile_target(args.profile_sweeps)
-    return run_ours(args)
+        return run_profile_target(args, W)
+    return run_ours(args, W)
 
 
-def run_profile_target(n_sweeps: int) -> int:
-    """Eager sweeps of the bench workload: one kernel launch per colour block per sweep."""
+def run_profile_target(args, W) -> int:
+    """Eager sweeps of the workload: one kernel launch per sampling group per sweep."""
     import torch
 
     from tt_thrml_b200 import Executor, make_cuda_config
 
-    prog = build_workload()
-    C = CHAINS_PER_GPU
-    ex = Executor(None, 0, prog, make_cuda_config(n_chains=C, cuda_graphs=False), n_sweeps=n_sweeps, n_chains=C)
-    rng = np.random.default_rng(100)
-    ex.load_state([rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks], [])
+    prog = W.build()
+    C = args.chains or W.chains
+    n = args.profile_sweeps
+    ex = Executor(None, 0, prog, make_cuda_config(n_chains=C, cuda_graphs=False), n_sweeps=n, n_chains=C)
+    ex.load_state(W.init(prog, C, 100), [])
     ex.prepare_rng(SEED)
-    for _ in range(n_sweeps):
+    for _ in range(n):
         ex.run_sweep()
     torch.cuda.synchronize()
-    print(f"profile target: {n_sweeps} sweeps x {len(prog.specs)} blocks", flush=True)
+    ex.check_device_errors()
+    print(f"profile target: {W.workload}, {C} chains, {n} sweeps x {len(ex.compiled.sampling_groups)} groups", flush=True)
     return 0
 
 

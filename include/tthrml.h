@@ -206,19 +206,27 @@ int tthrml_spin_bits_step(const int64_t* row_ptr_dev, const int32_t* cols_dev, c
  *   field[m][n] = sum_k source_state[m][k] * weights_nk[n][k] + bias[n]
  * source_state: bf16 [n_chains][n_sources] (chain-major), weights_nk: bf16
  * [n_units][n_sources]; the target block's new state is written to out_state
- * (bf16 [n_chains][n_units]) and, when out_state_f32 is not NULL, to float32.
+ * as `out_pieces` bf16 pieces per value (bf16 [n_chains][out_pieces *
+ * n_units]; piece p, at column p * n_units + unit, is the bf16 rounding of
+ * the value minus pieces 0..p-1, so 3 pieces hold a float32 exactly and a
+ * source operand built from them with the weights repeated along K gives the
+ * float32 field) and, when out_state_f32 is not NULL, to float32.
  * family TTHRML_SPIN draws +1 with probability sigmoid(2*field) (variates:
  * 2*field > logit); TTHRML_GAUSSIAN draws field*var + sqrt(var)*xi with
- * var = 1/(precision + 1e-6).  Philox counters: (chain/4, row0 + unit, sweep)
- * for spins, (chain, row0 + unit, sweep) for gaussians, as in the other
- * kernels.  variates: [variates_sweeps][n_units][n_chains] or NULL.
+ * var = 1/(precision + 1e-6).  Philox counters run along the unit axis of a
+ * chain: spins of units 4j..4j+3 take the four words of
+ * (chain_offset + chain, (row0 + unit) / 4, sweep, "DSPI"); gaussian units
+ * 2j, 2j+1 the word pairs of (chain_offset + chain, (row0 + unit) / 2, sweep,
+ * "DGAU") through Box-Muller.  variates: [variates_sweeps][n_units][n_chains]
+ * or NULL.
  * Requires n_chains % 128 == 0, n_units % 256 == 0, n_sources % 64 == 0 and
  * 16-byte aligned buffers.  Waits inside the kernel are bounded: a device
  * error word (*error, zero on entry) receives a non-zero code if one expired.
  */
 int tthrml_dense_field_sample(const void* source_state, const void* weights_nk, int64_t n_chains,
                               int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
-                              float precision, void* out_state, float* out_state_f32, int64_t row0,
+                              float precision, void* out_state, float* out_state_f32, int32_t out_pieces,
+                              int64_t row0,
                               int64_t chain_offset, const float* variates, int64_t variates_sweeps,
                               uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int32_t* error,
                               void* stream);

@@ -47,8 +47,11 @@ typedef struct {
   int32_t cat_q[4];
 } or_interaction;
 
+/* rng_layout 0: one Philox counter per (site, chain group), as the sparse and
+ * generic kernels draw; 1: counters along the unit axis of one chain, as the
+ * dense tensor-core kernel draws (tt_thrml_b200/csrc/dense_tc.cu draw_chunk) */
 typedef struct {
-  int32_t family, q, n_interactions, pad;
+  int32_t family, q, n_interactions, rng_layout;
   int64_t n_nodes, row_start;
   const or_interaction* inter;
   const float* variates; /* this sweep: [n_nodes][qv][C], or NULL */
@@ -80,6 +83,7 @@ void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t
 }
 
 static const uint32_t SALT_SPIN = 0x5350494eu, SALT_GAUSS = 0x47415553u, SALT_CAT = 0x43415400u;
+static const uint32_t SALT_DENSE_SPIN = 0x44535049u, SALT_DENSE_GAUSS = 0x44474155u;
 
 static double or_uniform(uint32_t bits) { return (double)((((bits >> 9) << 1) | 1u)) * 5.9604644775390625e-08; }
 
@@ -198,8 +202,10 @@ static void* run_rows(void* arg) {
           v = two_g > l ? 1.0f : -1.0f;
           m = (double)two_g - (double)l;
         } else {
-          const or_u32x4 r = or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_SPIN, t->k0, t->k1);
-          const double u = or_uniform(r.v[gc & 3]);
+          const int dense = B->rng_layout == 1;
+          const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 2), t->sweep, SALT_DENSE_SPIN, t->k0, t->k1)
+                                   : or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_SPIN, t->k0, t->k1);
+          const double u = or_uniform(r.v[dense ? (row & 3) : (gc & 3)]);
           const double l = log(u) - log1p(-u);
           m = (double)two_g - l;
           v = m > 0.0 ? 1.0f : -1.0f;
@@ -244,8 +250,11 @@ static void* run_rows(void* arg) {
           const float tt = sd * B->variates[i * C + c];
           v = mean + tt;
         } else {
-          const or_u32x4 r = or_philox((uint32_t)gc, (uint32_t)row, t->sweep, SALT_GAUSS, t->k0, t->k1);
-          const double xi = sqrt(-2.0 * log(or_uniform(r.v[0]))) * cos(2.0 * M_PI * or_uniform(r.v[1]));
+          const int dense = B->rng_layout == 1;
+          const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 1), t->sweep, SALT_DENSE_GAUSS, t->k0, t->k1)
+                                   : or_philox((uint32_t)gc, (uint32_t)row, t->sweep, SALT_GAUSS, t->k0, t->k1);
+          const int w = dense ? (int)(row & 1) * 2 : 0;
+          const double xi = sqrt(-2.0 * log(or_uniform(r.v[w]))) * cos(2.0 * M_PI * or_uniform(r.v[w + 1]));
           v = (float)((double)mean + (double)sd * xi);
         }
       }

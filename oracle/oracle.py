@@ -56,7 +56,7 @@ class _Block(ctypes.Structure):
         ("family", ctypes.c_int32),
         ("q", ctypes.c_int32),
         ("n_interactions", ctypes.c_int32),
-        ("pad", ctypes.c_int32),
+        ("rng_layout", ctypes.c_int32),
         ("n_nodes", ctypes.c_int64),
         ("row_start", ctypes.c_int64),
         ("inter", ctypes.c_void_p),
@@ -310,7 +310,14 @@ def lower_program(program) -> OProgram:
 class OracleSampler:
     """Runs lowered programs on the CPU over a float32 [rows, chains] state."""
 
-    def __init__(self, program, n_chains: int = 1, chain_offset: int = 0, n_threads: int | None = None):
+    def __init__(self, program, n_chains: int = 1, chain_offset: int = 0, n_threads: int | None = None,
+                 rng_layout: str = "site"):
+        """rng_layout: "site" (Philox counter per site and chain group, the sparse and
+        generic kernels) or "dense" (counters along one chain's unit axis, the
+        tensor-core dense kernel)."""
+        if rng_layout not in ("site", "dense"):
+            raise ValueError(f"rng_layout must be 'site' or 'dense', got {rng_layout!r}")
+        self.rng_layout = 1 if rng_layout == "dense" else 0
         self.prog = program if isinstance(program, OProgram) else lower_program(program)
         self.program = program
         self.C = int(n_chains)
@@ -372,6 +379,7 @@ class OracleSampler:
             d.n_interactions = len(b.interactions)
             d.n_nodes = b.n_nodes
             d.row_start = b.start
+            d.rng_layout = self.rng_layout
             d.inter = ctypes.addressof(self._inter_structs[bi])
             if variates is not None:
                 v = np.ascontiguousarray(variates[bi], dtype=np.float32)

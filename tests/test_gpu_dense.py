@@ -18,7 +18,7 @@ from tt_thrml_b200 import _native as nat
 pytestmark = pytest.mark.gpu
 
 
-def _call(A, Bt, bias, family, precision, out, out32, *, row0=0, variates=None, seed=1, sweep=0, chain_offset=0):
+def _call(A, Bt, bias, family, precision, out, out32, *, pieces=1, row0=0, variates=None, seed=1, sweep=0, chain_offset=0):
     import torch
 
     lib = nat.lib()
@@ -28,7 +28,7 @@ def _call(A, Bt, bias, family, precision, out, out32, *, row0=0, variates=None, 
     N = Bt.shape[0]
     rc = lib.tthrml_dense_field_sample(
         A.data_ptr(), Bt.data_ptr(), M, N, K, None if bias is None else bias.data_ptr(), family, ctypes.c_float(precision),
-        out.data_ptr(), None if out32 is None else out32.data_ptr(), row0, chain_offset,
+        out.data_ptr(), None if out32 is None else out32.data_ptr(), pieces, row0, chain_offset,
         None if variates is None else variates.data_ptr(), 0 if variates is None else variates.shape[0],
         seed, sweep, None, err.data_ptr(), torch.cuda.current_stream().cuda_stream,
     )

@@ -151,3 +151,23 @@ def test_oracle_runs_multichain_philox_deterministically():
         for sweep in range(5):
             s.sweep(sweep, seed=1234)
     np.testing.assert_array_equal(a.state, b.state)
+
+
+def test_oracle_dense_rng_layout_differs_from_site_layout():
+    """The dense (unit-axis) Philox counter layout gives different draws from the site layout."""
+    import numpy as np
+
+    from tt_thrml_b200 import workloads
+
+    prog = workloads.gaussian_bernoulli_rbm(256, 256, seed=0, w_std=0.05)
+    rng = np.random.default_rng(13)
+    init = [rng.standard_normal((8, 256)).astype(np.float32), rng.integers(0, 2, (8, 256)).astype(bool)]
+    res = []
+    for layout in ("site", "dense"):
+        o = orc.OracleSampler(prog, n_chains=8, rng_layout=layout)
+        o.load_state(init)
+        o.group_step(0, 0, seed=99)
+        res.append(o.state.copy())
+    assert not np.array_equal(res[0], res[1])
+    with pytest.raises(ValueError):
+        orc.OracleSampler(prog, n_chains=8, rng_layout="tiles")

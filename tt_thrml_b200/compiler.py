@@ -626,6 +626,105 @@ def plan_program(
     return state_dtype, plans
 
 
+@dataclass
+class DenseGroupPlan:
+    """A block whose field is one dense GEMM over the chain batch (tthrml_dense_field_sample)."""
+
+    block_indices: tuple[int, ...]
+    source: int
+    family: Family
+    n_units: int
+    n_sources: int
+    row0: int
+    precision: float
+    weights_nk: Any  # bf16 [n_units][source_pieces * n_sources] device tensor (K-repeated per piece)
+    bias: Any  # float32 [n_units] device tensor
+    source_pieces: int = 1  # bf16 pieces per source value in the source block's state
+    out_pieces: int = 1  # bf16 pieces per value written for the target block
+    family_label: str = ""
+    kind: str = "dense"
+    in_place: bool = True
+    group_rows: int = 0
+    device: Any = None
+
+
+DENSE_CHAIN_MULTIPLE = 128
+DENSE_UNIT_MULTIPLE = 256
+
+
+def dense_eligible(program, n_chains: int) -> bool:
+    """True when the program lowers to the tensor-core dense plan at this chain count."""
+    couplings = getattr(program, "tt_dense_couplings", None)
+    if not callable(couplings) or n_chains % DENSE_CHAIN_MULTIPLE:
+        return False
+    gs = program.gibbs_spec
+    if gs.clamped_blocks or any(len(g) != 1 for g in gs.sampling_order):
+        return False
+    for bi, c in couplings().items():
+        if c["n_units"] % DENSE_UNIT_MULTIPLE or Family(c["family"]) not in (Family.SPIN, Family.GAUSSIAN):
+            return False
+    return True
+
+
+def dense_pieces(program, precision: str) -> dict[int, int]:
+    """bf16 pieces per value of each block's state: 3 for gaussian blocks at fp32, else 1."""
+    couplings = program.tt_dense_couplings()
+    return {
+        bi: 3 if precision == "fp32" and Family(c["family"]) == Family.GAUSSIAN else 1 for bi, c in couplings.items()
+    }
+
+
+def _plan_dense(program, device, precision: str = "bf16"):
+    torch = _torch()
+    couplings = program.tt_dense_couplings()
+    pieces = dense_pieces(program, precision)
+    plans = []
+    for group in program.gibbs_spec.sampling_order:
+        bi = int(group[0])
+        c = couplings[bi]
+        w = np.ascontiguousarray(c["weights_nk"], dtype=np.float32)
+        wt = torch.from_numpy(w).to(device=device, dtype=torch.bfloat16).contiguous()
+        if not torch.equal(wt.float().cpu(), torch.from_numpy(w)):
+            raise ValueError(
+                f"block {bi}: dense couplings must be bf16-representable (round them with "
+                "workloads.bf16_representable) so the tensor-core operands are the model's weights"
+            )
+        fam = Family(c["family"])
+        src_pieces = pieces[int(c["source"])]
+        if src_pieces > 1:
+            wt = wt.repeat(1, src_pieces).contiguous()
+        plans.append(
+            DenseGroupPlan(
+                block_indices=(bi,),
+                source=int(c["source"]),
+                family=fam,
+                n_units=int(c["n_units"]),
+                n_sources=int(w.shape[1]) * src_pieces,
+                row0=int(c["row0"]),
+                precision=float(c.get("precision", 1.0)),
+                weights_nk=wt,
+                source_pieces=src_pieces,
+                out_pieces=pieces[bi],
+                bias=torch.from_numpy(np.asarray(c["bias"], np.float32)).to(device),
+                family_label=fam.value,
+                group_rows=int(c["n_units"]),
+                device=device,
+            )
+        )
+    return plans
+
+
+def _dense_specs(program):
+    """Light block specs (no tables) of a dense program: family, size, flat start."""
+    couplings = program.tt_dense_couplings()
+    blocks = program.gibbs_spec.blocks
+    total = sum(len(b.nodes) for b in blocks)
+    return tuple(
+        FusedBlockSpec(bi, Family(couplings[bi]["family"]), len(b.nodes), None, int(couplings[bi]["row0"]), total, ())
+        for bi, b in enumerate(blocks)
+    )
+
+
 def compile_program(
     ttnn,
     device,
@@ -640,10 +739,17 @@ def compile_program(
     del ttnn
     n_chains = int(n_chains if n_chains is not None else config.n_chains)
     tdev = resolve_torch_device(device)
-    lowered = lower_program(program)
-    state_dtype, plans = plan_program(
-        lowered, n_chains, tdev, force_generic=force_generic, spin_layout=config.spin_layout
-    )
+    if not force_generic and dense_eligible(program, n_chains):
+        specs = _dense_specs(program)
+        order = tuple(tuple(int(i) for i in g) for g in program.gibbs_spec.sampling_order)
+        lowered = LoweredProgram(specs, order, len(program.gibbs_spec.free_blocks), specs[0].total_nodes,
+                                 tuple(s.block_global_start for s in specs))
+        state_dtype, plans = "dense_bf16", _plan_dense(program, tdev, config.resolved_dense_precision)
+    else:
+        lowered = lower_program(program)
+        state_dtype, plans = plan_program(
+            lowered, n_chains, tdev, force_generic=force_generic, spin_layout=config.spin_layout
+        )
     _torch().cuda.synchronize(tdev)  # tables uploaded before any stream uses them
     blocks = tuple(CompiledFusedBlock(spec=s, kernel_artifact=None) for s in lowered.specs)
     groups = tuple(
@@ -666,4 +772,12 @@ def compile_program(
     )
 
 
-__all__ = ["compile_program", "lower_program", "plan_program", "LoweredProgram", "GenericGroupPlan", "SpinCSRGroupPlan"]
+__all__ = [
+    "compile_program",
+    "lower_program",
+    "plan_program",
+    "LoweredProgram",
+    "GenericGroupPlan",
+    "SpinCSRGroupPlan",
+    "DenseGroupPlan",
+]

@@ -34,6 +34,7 @@ RNG_MODES = ("philox", "parity")
 # multiple of 256 chains), "int8" one byte per chain; "auto" picks bits when
 # the chain count allows.
 SPIN_LAYOUTS = ("auto", "bits", "int8")
+DENSE_PRECISIONS = ("auto", "bf16", "fp32")
 
 
 @dataclass(frozen=True)
@@ -46,6 +47,11 @@ class CUDAConfig:
     n_chains: independent chains per executor (the reference has one).
     cuda_graphs: capture multi-sweep runs in CUDA graphs.
     spin_layout: state layout of all-spin programs ("auto", "bits", "int8").
+    dense_precision: tensor-core path of dense bipartite programs. "bf16"
+      keeps gaussian block states as bf16 GEMM operands; "fp32" keeps them
+      float32, fed to the GEMM as three bf16 pieces against the weights
+      repeated along K (the float32 field up to summation order); "auto" is
+      "fp32" in parity mode and "bf16" in Philox mode.
     """
 
     artifact_root: Path
@@ -54,6 +60,7 @@ class CUDAConfig:
     n_chains: int = 1
     cuda_graphs: bool = True
     spin_layout: str = "auto"
+    dense_precision: str = "auto"
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "artifact_root", Path(self.artifact_root).resolve())
@@ -65,6 +72,14 @@ class CUDAConfig:
             raise ValueError(f"only sm_100a is supported, got {self.arch!r}")
         if self.spin_layout not in SPIN_LAYOUTS:
             raise ValueError(f"spin_layout must be one of {SPIN_LAYOUTS}, got {self.spin_layout!r}")
+        if self.dense_precision not in DENSE_PRECISIONS:
+            raise ValueError(f"dense_precision must be one of {DENSE_PRECISIONS}, got {self.dense_precision!r}")
+
+    @property
+    def resolved_dense_precision(self) -> str:
+        if self.dense_precision != "auto":
+            return self.dense_precision
+        return "fp32" if self.rng_mode == "parity" else "bf16"
 
     def cache_key(self) -> str:
         payload = {"arch": self.arch, "rng_mode": self.rng_mode}
@@ -209,6 +224,7 @@ def make_cuda_config(
     n_chains: int = 1,
     cuda_graphs: bool = True,
     spin_layout: str = "auto",
+    dense_precision: str = "auto",
 ) -> CUDAConfig:
     """Create a CUDA configuration (the CUDA counterpart of make_ttmlir_config)."""
     root = Path(artifact_root if artifact_root is not None else Path(tempfile.gettempdir()) / "tt-thrml-b200")
@@ -219,6 +235,7 @@ def make_cuda_config(
         n_chains=int(n_chains),
         cuda_graphs=cuda_graphs,
         spin_layout=spin_layout,
+        dense_precision=dense_precision,
     )
 
 

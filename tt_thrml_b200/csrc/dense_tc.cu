@@ -124,8 +124,9 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
 
 struct DenseArgs {
   const float* bias;       // [N] or NULL
-  __nv_bfloat16* out;      // [M][N] new target state (bf16)
+  __nv_bfloat16* out;      // [M][pieces * N] new target state: bf16 pieces, value = sum over pieces
   float* out_f32;          // [M][N] same values in float32, or NULL
+  int32_t pieces;          // 1: bf16 value; 2-3: successive bf16 remainders (3 is exact for float32)
   const float* variates;   // [variates_sweeps][N][M] (unit-major, chains innermost) or NULL
   int64_t variates_sweeps;
   int64_t M, N, K;
@@ -157,7 +158,6 @@ __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc
                                            uint32_t sweep, uint32_t k0, uint32_t k1, float inv, float sd_g,
                                            int64_t vs) {
   const int64_t gchain = a.chain_offset + m;
-  __align__(16) __nv_bfloat16 outv[32];
   float outf[32];
   u32x4 r{0u, 0u, 0u, 0u};
 #pragma unroll
@@ -189,16 +189,26 @@ __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc
       v = __fadd_rn(__fmul_rn(field, inv), __fmul_rn(sd_g, xi));
     }
     outf[j] = v;
-    outv[j] = __float2bfloat16_rn(v);
   }
-  uint4* dst = reinterpret_cast<uint4*>(a.out + m * a.N + n_first);
-  const uint4* srcv = reinterpret_cast<const uint4*>(outv);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) dst[q] = srcv[q];
   if (a.out_f32) {
     float4* df = reinterpret_cast<float4*>(a.out_f32 + m * a.N + n_first);
 #pragma unroll
     for (int q = 0; q < 8; ++q) df[q] = make_float4(outf[4 * q], outf[4 * q + 1], outf[4 * q + 2], outf[4 * q + 3]);
+  }
+  // piece p = bf16(v - pieces 0..p-1); each remainder is exact in float32, so
+  // three pieces carry all 24 significand bits
+  __nv_bfloat16* row = a.out + m * (a.N * a.pieces) + n_first;
+  for (int p = 0; p < a.pieces; ++p) {
+    __align__(16) __nv_bfloat16 outv[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      outv[j] = __float2bfloat16_rn(outf[j]);
+      outf[j] = __fsub_rn(outf[j], __bfloat162float(outv[j]));
+    }
+    uint4* dst = reinterpret_cast<uint4*>(row + p * a.N);
+    const uint4* srcv = reinterpret_cast<const uint4*>(outv);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = srcv[q];
   }
 }
 
@@ -404,7 +414,8 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, uin
 
 extern "C" int tthrml_dense_field_sample(const void* source_state, const void* weights_nk, int64_t n_chains,
                                          int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
-                                         float precision, void* out_state, float* out_state_f32, int64_t row0,
+                                         float precision, void* out_state, float* out_state_f32,
+                                         int32_t out_pieces, int64_t row0,
                                          int64_t chain_offset, const float* variates, int64_t variates_sweeps,
                                          uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int32_t* error,
                                          void* stream) {
@@ -424,6 +435,10 @@ extern "C" int tthrml_dense_field_sample(const void* source_state, const void* w
   }
   if (family != TTHRML_SPIN && family != TTHRML_GAUSSIAN) {
     set_error("tthrml_dense_field_sample: family must be spin or gaussian");
+    return TTHRML_ERR_ARG;
+  }
+  if (out_pieces < 1 || out_pieces > 3) {
+    set_error("tthrml_dense_field_sample: out_pieces must be 1, 2 or 3 (got %d)", (int)out_pieces);
     return TTHRML_ERR_ARG;
   }
   if (chain_offset % 4 || ((uintptr_t)source_state % 16) || ((uintptr_t)weights_nk % 16) || ((uintptr_t)out_state % 16) ||
@@ -463,6 +478,7 @@ extern "C" int tthrml_dense_field_sample(const void* source_state, const void* w
   a.bias = bias;
   a.out = reinterpret_cast<__nv_bfloat16*>(out_state);
   a.out_f32 = out_state_f32;
+  a.pieces = out_pieces;
   a.variates = variates;
   a.variates_sweeps = variates_sweeps;
   a.M = n_chains;

@@ -95,6 +95,10 @@ class Executor:
         )
         # elements per state row: chains, or 32-chain words when bit-packed
         self._row_len = self.n_chains // 32 if self._state_code == nat.STATE_BITS else self.n_chains
+        # dense (tensor-core) programs keep one bf16 [n_chains, n_units] tensor per block
+        self._dense = self.compiled.state_dtype == "dense_bf16"
+        self._block_states: list | None = None
+        self._error_word = None
 
         self._global_state = None
         self._state_loaded = False
@@ -125,11 +129,51 @@ class Executor:
 
     def _ensure_state(self):
         torch = _torch()
+        if self._dense:
+            if self._block_states is None:
+                pieces = {plan.block_indices[0]: plan.out_pieces for plan in self._plans()}
+                self._dense_pieces = [pieces.get(bi, 1) for bi in range(len(self.compiled.blocks))]
+                self._block_states = [
+                    torch.empty((self.n_chains, p * cb.spec.n_nodes), dtype=torch.bfloat16, device=self._tdev)
+                    for p, cb in zip(self._dense_pieces, self.compiled.blocks)
+                ]
+                # float32 copies of the blocks held in several pieces (the readable state)
+                self._block_f32 = [
+                    torch.empty((self.n_chains, cb.spec.n_nodes), dtype=torch.float32, device=self._tdev)
+                    if p > 1
+                    else None
+                    for p, cb in zip(self._dense_pieces, self.compiled.blocks)
+                ]
+                self._error_word = torch.zeros(1, dtype=torch.int32, device=self._tdev)
+            return self._block_states
         if self._global_state is None:
             self._global_state = torch.empty(
                 (self.compiled.total_nodes, self._row_len), dtype=self._torch_state_dtype, device=self._tdev
             )
         return self._global_state
+
+    def _plans(self):
+        return [g.kernel_artifact for g in self.compiled.sampling_groups]
+
+    def _dense_write_block(self, block_index: int, values) -> None:
+        """Stores float32 values [C or 1, n] into a dense block (bf16 pieces + float32 copy)."""
+        torch = _torch()
+        n = self.compiled.blocks[block_index].spec.n_nodes
+        rem = values.to(torch.float32).expand(self.n_chains, n)
+        if self._block_f32[block_index] is not None:
+            self._block_f32[block_index].copy_(rem)
+        dst = self._block_states[block_index]
+        for p in range(self._dense_pieces[block_index]):
+            piece = rem.to(torch.bfloat16)
+            dst[:, p * n : (p + 1) * n].copy_(piece)
+            rem = rem - piece.float()
+
+    def _dense_block_values(self, block_index: int):
+        """A dense block's float32 values [C, n] (device)."""
+        f32 = self._block_f32[block_index]
+        if f32 is not None:
+            return f32
+        return self._block_states[block_index].float()
 
     def _block_source(self, block_index: int, state):
         """One block's states as a contiguous device tensor [C or 1, n] of int8 or float32.
@@ -166,6 +210,16 @@ class Executor:
             raise ValueError(f"Expected {len(self.compiled.blocks)} block states, got {len(states)}")
         self._ensure_state()
         nat.bind_device(self._tdev.index)
+        if self._dense:
+            with torch.cuda.stream(self._stream):
+                for bi, st in enumerate(states):
+                    spec = self.compiled.blocks[bi].spec
+                    src = self._block_source(bi, st)
+                    if spec.family == Family.SPIN:
+                        src = torch.where(src > 0, 1.0, -1.0)
+                    self._dense_write_block(bi, src)
+            self._state_loaded = True
+            return
         with torch.cuda.stream(self._stream):
             for bi, st in enumerate(states):
                 spec = self.compiled.blocks[bi].spec
@@ -342,7 +396,35 @@ class Executor:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev1 = torch.cuda.Event(enable_timing=True)
             ev0.record(self._stream)
-        if plan.kind in ("spin_csr", "spin_bits"):
+        if plan.kind == "dense":
+            bi = plan.block_indices[0]
+            v = self._variates(bi)
+            nat.check(
+                self._lib.tthrml_dense_field_sample(
+                    self._block_states[plan.source].data_ptr(),
+                    plan.weights_nk.data_ptr(),
+                    self.n_chains,
+                    plan.n_units,
+                    plan.n_sources,
+                    plan.bias.data_ptr(),
+                    nat.SPIN if plan.family == Family.SPIN else nat.GAUSSIAN,
+                    ctypes.c_float(plan.precision),
+                    self._block_states[bi].data_ptr(),
+                    None if self._block_f32[bi] is None else self._block_f32[bi].data_ptr(),
+                    plan.out_pieces,
+                    plan.row0,
+                    self.chain_offset,
+                    None if v is None else v.data_ptr(),
+                    self._rng_n_sweeps if v is not None else 0,
+                    seed,
+                    sweep_idx,
+                    ctl,
+                    self._error_word.data_ptr(),
+                    stream,
+                ),
+                "tthrml_dense_field_sample",
+            )
+        elif plan.kind in ("spin_csr", "spin_bits"):
             step = self._lib.tthrml_spin_bits_step if plan.kind == "spin_bits" else self._lib.tthrml_spin_csr_step
             for blk in plan.blocks:
                 v = self._variates(blk.block_index)
@@ -399,9 +481,21 @@ class Executor:
 
     # ------------------------------------------------------------- read-back
 
+    def check_device_errors(self) -> None:
+        """Raises if a kernel recorded an expired in-kernel wait (dense programs)."""
+        if self._error_word is not None:
+            self._stream.synchronize()
+            code = int(self._error_word.item())
+            if code:
+                raise RuntimeError(f"tensor-core kernel reported an expired wait (code {code})")
+
     def raw_state(self) -> np.ndarray:
         """The whole state as host float32 [total_nodes, n_chains] values (spins +-1)."""
         torch = _torch()
+        if self._dense:
+            self._stream.synchronize()
+            vals = [self._dense_block_values(bi) for bi in range(len(self._block_states))]
+            return torch.cat(vals, dim=1).cpu().numpy().T.copy()
         out = torch.empty((self.n_chains, self.compiled.total_nodes), dtype=torch.float32, device=self._tdev)
         nat.bind_device(self._tdev.index)
         nat.check(
@@ -417,6 +511,16 @@ class Executor:
     def set_raw_state(self, values: np.ndarray) -> None:
         """Overwrites the whole state from host float32 [total_nodes, n_chains] values."""
         torch = _torch()
+        if self._dense:
+            self._ensure_state()
+            vals = torch.from_numpy(np.ascontiguousarray(np.asarray(values, np.float32).T)).to(self._tdev)
+            pos = 0
+            for bi, cb in enumerate(self.compiled.blocks):
+                self._dense_write_block(bi, vals[:, pos : pos + cb.spec.n_nodes])
+                pos += cb.spec.n_nodes
+            torch.cuda.synchronize(self._tdev)
+            self._state_loaded = True
+            return
         src = torch.from_numpy(np.ascontiguousarray(np.asarray(values, np.float32).T)).to(self._tdev)
         self._ensure_state()
         nat.bind_device(self._tdev.index)
@@ -452,6 +556,17 @@ class Executor:
         spec = self.compiled.blocks[block_index].spec
         kind = _OUT_KIND[spec.family]
         dtype = (torch.uint8, torch.int32, torch.float32)[kind]
+        if self._dense:
+            self.check_device_errors()
+            with torch.cuda.stream(self._stream):
+                b = self._dense_block_values(block_index)
+                dev = (b > 0).to(torch.uint8) if spec.family == Family.SPIN else b.contiguous()
+            if not to_host:
+                return dev
+            host = self._pinned_buffer(("blk", block_index), dev.shape, dtype)
+            with torch.cuda.stream(self._stream):
+                host.copy_(dev, non_blocking=True)
+            return host
         with torch.cuda.stream(self._stream):
             dev = torch.empty((self.n_chains, spec.n_nodes), dtype=dtype, device=self._tdev)
         nat.bind_device(self._tdev.index)
@@ -490,7 +605,7 @@ class Executor:
 
     def observe(self, blocks: Sequence) -> dict:
         """Block states keyed by block (tt_thrml/executor.py:277-292)."""
-        if self._global_state is None:
+        if self._global_state is None and self._block_states is None:
             return {}
         lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
         wanted = [(b, lookup.get(id(b))) for b in blocks]
@@ -511,6 +626,14 @@ class Executor:
         with torch.cuda.stream(self._stream):
             out = torch.zeros(self.n_chains, dtype=torch.float64, device=self._tdev)
         nat.bind_device(self._tdev.index)
+        if self._dense:
+            lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
+            with torch.cuda.stream(self._stream):
+                for b in blocks:
+                    bi = lookup[id(b)] if not isinstance(b, int) else b
+                    out += self._dense_block_values(bi).double().sum(1)
+                host = out.cpu()
+            return host.numpy()
         for b in blocks:
             bi = lookup[id(b)] if not isinstance(b, int) else b
             spec = self.compiled.blocks[bi].spec

@@ -237,3 +237,99 @@ def random_spin_state(program: TableProgram, n_chains: int, seed: int = 0) -> li
     rng = np.random.default_rng(seed)
     return [rng.integers(0, 2, size=(n_chains, len(b.nodes)), dtype=np.int8).astype(bool)
             for b in program.gibbs_spec.free_blocks]
+
+
+def bf16_representable(x: np.ndarray) -> np.ndarray:
+    """float32 values rounded to the nearest bfloat16 (ties to even), kept as float32."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rounded = ((b + np.uint32(0x7FFF) + ((b >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)).astype(np.uint32)
+    return rounded.view(np.float32)
+
+
+class DenseBipartiteProgram(TableProgram):
+    """Two blocks coupled through a dense weight matrix (a restricted Boltzmann machine).
+
+    Block 0: `n_visible` units (gaussian with unit precision, or spins), flat
+    rows [0, n_visible); block 1: `n_hidden` spins, rows [n_visible, n_visible
+    + n_hidden).  Field of visible unit i: b_v[i] + sum_j W[i, j] h_j; of hidden
+    unit j: b_h[j] + sum_i W[i, j] v_i.  The tensor-core plan reads W directly
+    (`tt_dense_couplings`); `tt_lower_blocks` builds the equivalent per-node
+    tables (every unit has one term per unit of the other block) for the
+    generic kernel and the oracle.
+    """
+
+    def __init__(self, W, b_v, b_h, *, visible_family: Family = Family.GAUSSIAN, sampling_order=((1,), (0,)),
+                 name: str = "rbm"):
+        W = np.ascontiguousarray(W, dtype=np.float32)
+        V, H = W.shape
+        blocks = [IndexBlock(V, visible_family, name="visible:"), IndexBlock(H, Family.SPIN, name="hidden:")]
+        gspec = TableGibbsSpec(free_blocks=blocks, clamped_blocks=[], sampling_order=[list(g) for g in sampling_order])
+        super().__init__(gspec, [], {"name": name, "n_visible": V, "n_hidden": H})
+        self.W = W
+        self.b_v = np.asarray(b_v, dtype=np.float32).reshape(V)
+        self.b_h = np.asarray(b_h, dtype=np.float32).reshape(H)
+        self.visible_family = Family(visible_family)
+        self._specs = None
+
+    def tt_dense_couplings(self) -> dict:
+        V, H = self.W.shape
+        return {
+            0: {"family": self.visible_family, "row0": 0, "n_units": V, "source": 1, "weights_nk": self.W,
+                "bias": self.b_v, "precision": 1.0},
+            1: {"family": Family.SPIN, "row0": V, "n_units": H, "source": 0, "weights_nk": self.W.T,
+                "bias": self.b_h, "precision": 1.0},
+        }
+
+    def tt_lower_blocks(self):
+        if self._specs is None:
+            V, H = self.W.shape
+            total = V + H
+
+            def block(bi, family, n, start, bias, w_nk, src0, n_src):
+                rp = np.arange(n + 1, dtype=np.int64) * n_src
+                cols = np.tile(np.arange(src0, src0 + n_src, dtype=np.int32), n)
+                pair = FusedInteractionSpec(
+                    weighted_mask=np.ascontiguousarray(w_nk, dtype=np.float32).reshape(-1),
+                    gather_indices=(cols,),
+                    n_spin=1,
+                    n_categorical=0,
+                    n_terms=n_src,
+                    contribution_kind="default" if family == Family.SPIN else "linear",
+                    row_ptr=rp,
+                )
+                b = FusedInteractionSpec(
+                    weighted_mask=np.asarray(bias, np.float32).reshape(n, 1),
+                    gather_indices=(),
+                    n_spin=0,
+                    n_categorical=0,
+                    n_terms=1,
+                    contribution_kind="default" if family == Family.SPIN else "linear",
+                )
+                return FusedBlockSpec(bi, family, n, None, start, total, (b, pair))
+
+            self._specs = [
+                block(0, self.visible_family, V, 0, self.b_v, self.W, V, H),
+                block(1, Family.SPIN, H, V, self.b_h, self.W.T, 0, V),
+            ]
+        return list(self._specs)
+
+
+def gaussian_bernoulli_rbm(
+    n_visible: int = 4096,
+    n_hidden: int = 8192,
+    *,
+    seed: int = 0,
+    w_std: float = 0.01,
+    visible_bias_variance: float = 0.1,
+) -> DenseBipartiteProgram:
+    """Gauss-Bernoulli RBM: unit-precision gaussian visible units with bias ~
+    N(0, visible_bias_variance), +-1 hidden spins without bias, couplings
+    W ~ N(0, w_std^2) rounded to bf16-representable values (the tensor cores
+    then multiply the model's exact weights)."""
+    rng = np.random.default_rng(seed)
+    W = bf16_representable((rng.standard_normal((n_visible, n_hidden)) * w_std).astype(np.float32))
+    b_v = (rng.standard_normal(n_visible) * np.sqrt(visible_bias_variance)).astype(np.float32)
+    b_h = np.zeros(n_hidden, dtype=np.float32)
+    prog = DenseBipartiteProgram(W, b_v, b_h, name=f"gb-rbm-{n_visible}x{n_hidden}")
+    prog.meta.update(seed=seed, w_std=w_std, visible_bias_variance=visible_bias_variance)
+    return prog
