@@ -198,6 +198,27 @@ int tthrml_spin_bits_step(const int64_t* row_ptr_dev, const int32_t* cols_dev, c
                           void* stream);
 
 /*
+ * Checkerboard colour block of a q-state Potts model on a periodic X x Y x Z
+ * lattice (q <= 8; one q x q matrix per axis).  Replaces the group kernel of
+ * the categorical block (tt_thrml/compiler.py:289-344) for lattice programs:
+ * the neighbour gather is computed from the site coordinates instead of read
+ * from tables.  state_dev: int8 [rows][n_chains] categories; colour-c site
+ * (x, y, z) sits at row target_row0 + L/2 with L = (z*Y + y)*X + x, its
+ * neighbours at source_row0 + L'/2.  J: float [3][q][q] (axis, target
+ * category, neighbour category); bias: float [X*Y*Z/2][q] per target row.
+ * theta_k = ((b_k + (Jx[k][s_x-] + Jx[k][s_x+])) + (Jy..)) + (Jz..), each sum
+ * rounded in float32.  variates: [variates_sweeps][X*Y*Z/2][q][n_chains]
+ * Gumbels (argmax(theta + g)) or NULL (Philox: one uniform per update from
+ * counter (chain/4, row, sweep, "CAT"), inverse-CDF draw, identical to the
+ * generic kernel).  Requires even X, Y, Z, n_chains % 4 == 0, chain_offset %
+ * 4 == 0 and 16-byte aligned buffers.
+ */
+int tthrml_potts3d_step(int8_t* state_dev, int64_t n_chains, int32_t X, int32_t Y, int32_t Z, int32_t colour,
+                        int64_t target_row0, int64_t source_row0, const float* J_dev, const float* bias_dev,
+                        int32_t q, int64_t chain_offset, const float* variates_dev, int64_t variates_sweeps,
+                        uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl_dev, void* stream);
+
+/*
  * Dense bipartite block update on the tensor cores (tcgen05, bf16 operands,
  * fp32 accumulation in TMEM).  Replaces the group kernel of a block whose
  * interaction with another block is a dense weight matrix (the RBM case:

@@ -16,7 +16,8 @@
  *     categorical sources select the weight slice of their value
  *     (tt_thrml/compiler.py:289-300);
  *   - spin: +1 where 2*gamma > l (compiler.py:321-324); categorical:
- *     argmax(theta + g), first maximum (compiler.py:327-344); gaussian:
+ *     argmax(theta + g), first maximum (compiler.py:327-344), or in Philox
+ *     mode the inverse-CDF draw of softmax(theta) from one uniform; gaussian:
  *     mean + sqrt(var)*xi with var = 1/(precision + 1e-6) (compiler.py:347-365).
  *
  * Variates: either given per block (the reference's uploaded slices,
@@ -86,6 +87,41 @@ static const uint32_t SALT_SPIN = 0x5350494eu, SALT_GAUSS = 0x47415553u, SALT_CA
 static const uint32_t SALT_DENSE_SPIN = 0x44535049u, SALT_DENSE_GAUSS = 0x44474155u;
 
 static double or_uniform(uint32_t bits) { return (double)((((bits >> 9) << 1) | 1u)) * 5.9604644775390625e-08; }
+
+static double or_logit(double p) { return log(p) - log1p(-p); }
+
+/* Categorical draw of the kernels' Philox mode, decided exactly: e_k =
+ * exp(theta_k - max) in double, C_k = e_0 + ... + e_k, T_(k+1) = e_(k+1) +
+ * ... (summed from the end), draw = number of k < q-1 with u >= C_k / S (the
+ * inverse CDF of softmax(theta) at u).  margin: the smallest |logit(u) -
+ * log(C_k / T_(k+1))| over the q-1 boundaries; the kernels' float32 decision
+ * can differ from this one only inside the threshold band. */
+static int or_categorical_icdf(const float* theta, int q, double u, double* margin) {
+  double mx = theta[0];
+  for (int k = 1; k < q; ++k) mx = fmax(mx, (double)theta[k]);
+  double e[OR_MAXQ], head[OR_MAXQ], tail[OR_MAXQ + 1];
+  double s = 0.0;
+  for (int k = 0; k < q; ++k) {
+    e[k] = exp((double)theta[k] - mx);
+    s += e[k];
+    head[k] = s;
+  }
+  tail[q] = 0.0;
+  for (int k = q - 1; k >= 0; --k) tail[k] = tail[k + 1] + e[k];
+  const double lu = or_logit(u);
+  int cat = 0;
+  double mg = INFINITY;
+  for (int k = 0; k < q - 1; ++k) {
+    const int reached = head[k] <= tail[k + 1] ? head[k] <= u * s : (1.0 - u) * s <= tail[k + 1];
+    cat += reached;
+    if (head[k] > 0.0 && tail[k + 1] > 0.0) {
+      const double d = fabs(lu - (log(head[k]) - log(tail[k + 1])));
+      if (d < mg) mg = d;
+    }
+  }
+  *margin = mg;
+  return cat;
+}
 
 /* ---- field ---- */
 
@@ -213,29 +249,26 @@ static void* run_rows(void* arg) {
       } else if (B->family == OR_CATEGORICAL) {
         float theta[OR_MAXQ];
         theta_of(B, state, C, c, i, theta);
-        int best = 0;
         const int q = B->q;
-        double bv = 0.0, second = -INFINITY;
-        for (int k = 0; k < q; ++k) {
-          double pk;
-          if (t->use_variates) {
-            const float f = theta[k] + B->variates[((int64_t)i * q + k) * C + c];
-            pk = f;
-          } else {
-            const or_u32x4 r =
-                or_philox((uint32_t)gc, (uint32_t)row, t->sweep, SALT_CAT + (uint32_t)(k >> 2), t->k0, t->k1);
-            pk = (double)theta[k] - log(-log(or_uniform(r.v[k & 3])));
+        if (t->use_variates) {
+          int best = 0;
+          double bv = 0.0, second = -INFINITY;
+          for (int k = 0; k < q; ++k) {
+            const double pk = (float)(theta[k] + B->variates[((int64_t)i * q + k) * C + c]);
+            if (k == 0 || pk > bv) {
+              if (k) second = bv;
+              bv = pk;
+              best = k;
+            } else if (pk > second) {
+              second = pk;
+            }
           }
-          if (k == 0 || pk > bv) {
-            if (k) second = bv;
-            bv = pk;
-            best = k;
-          } else if (pk > second) {
-            second = pk;
-          }
+          v = (float)best;
+          m = q > 1 ? bv - second : INFINITY;
+        } else {
+          const or_u32x4 r = or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_CAT, t->k0, t->k1);
+          v = (float)or_categorical_icdf(theta, q, or_uniform(r.v[gc & 3]), &m);
         }
-        v = (float)best;
-        m = q > 1 ? bv - second : INFINITY;
       } else {
         int any_l, any_p;
         const float lin = scalar_field(B, 0, state, C, c, i, &any_l);

@@ -725,6 +725,73 @@ def _dense_specs(program):
     )
 
 
+@dataclass
+class PottsStencilGroupPlan:
+    """One checkerboard colour of a 3-D Potts lattice (tthrml_potts3d_step)."""
+
+    block_indices: tuple[int, ...]
+    dims: tuple[int, int, int]
+    colour: int
+    q: int
+    target_row0: int
+    source_row0: int
+    J: Any  # float32 [3][q][q] device tensor
+    bias: Any  # float32 [n_rows][q] device tensor (target block rows)
+    family: Family = Family.CATEGORICAL
+    family_label: str = "categorical"
+    kind: str = "potts3d"
+    in_place: bool = True
+    group_rows: int = 0
+    device: Any = None
+
+
+POTTS_MAX_Q = 8
+
+
+def stencil_eligible(program, n_chains: int) -> bool:
+    """True when the program is a lattice the stencil kernels run at this chain count."""
+    stencil = getattr(program, "tt_stencil", None)
+    if not callable(stencil):
+        return False
+    st = stencil()
+    if st.get("kind") == "potts3d":
+        return 1 <= int(st["q"]) <= POTTS_MAX_Q and n_chains % 4 == 0
+    return False
+
+
+def _plan_stencil(program, device):
+    torch = _torch()
+    st = program.tt_stencil()
+    if st["kind"] != "potts3d":
+        raise ValueError(f"unknown stencil kind {st['kind']!r}")
+    J = torch.from_numpy(np.ascontiguousarray(st["J"], dtype=np.float32)).to(device)
+    rows = st["block_rows"]
+    plans = []
+    for group in program.gibbs_spec.sampling_order:
+        c = int(group[0])
+        bias = torch.from_numpy(np.ascontiguousarray(st["bias"][c], dtype=np.float32)).to(device)
+        plans.append(
+            PottsStencilGroupPlan(
+                block_indices=(c,), dims=tuple(int(d) for d in st["dims"]), colour=c, q=int(st["q"]),
+                target_row0=int(rows[c]), source_row0=int(rows[1 - c]), J=J, bias=bias,
+                group_rows=int(bias.shape[0]), device=device,
+            )
+        )
+    return plans
+
+
+def _stencil_specs(program):
+    """Light block specs (no tables) of a stencil program: family, size, flat start."""
+    st = program.tt_stencil()
+    blocks = program.gibbs_spec.blocks
+    total = sum(len(b.nodes) for b in blocks)
+    q = int(st["q"])
+    return tuple(
+        FusedBlockSpec(bi, Family.CATEGORICAL, len(b.nodes), q, int(st["block_rows"][bi]), total, ())
+        for bi, b in enumerate(blocks)
+    )
+
+
 def compile_program(
     ttnn,
     device,
@@ -739,7 +806,13 @@ def compile_program(
     del ttnn
     n_chains = int(n_chains if n_chains is not None else config.n_chains)
     tdev = resolve_torch_device(device)
-    if not force_generic and dense_eligible(program, n_chains):
+    if not force_generic and stencil_eligible(program, n_chains):
+        specs = _stencil_specs(program)
+        order = tuple(tuple(int(i) for i in g) for g in program.gibbs_spec.sampling_order)
+        lowered = LoweredProgram(specs, order, len(program.gibbs_spec.free_blocks), specs[0].total_nodes,
+                                 tuple(s.block_global_start for s in specs))
+        state_dtype, plans = "int8", _plan_stencil(program, tdev)
+    elif not force_generic and dense_eligible(program, n_chains):
         specs = _dense_specs(program)
         order = tuple(tuple(int(i) for i in g) for g in program.gibbs_spec.sampling_order)
         lowered = LoweredProgram(specs, order, len(program.gibbs_spec.free_blocks), specs[0].total_nodes,
@@ -780,4 +853,5 @@ __all__ = [
     "GenericGroupPlan",
     "SpinCSRGroupPlan",
     "DenseGroupPlan",
+    "PottsStencilGroupPlan",
 ]

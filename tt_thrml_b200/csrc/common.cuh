@@ -29,7 +29,7 @@ inline int launch_status(const char* what) { return cuda_status(cudaGetLastError
 // categorical and gaussian streams of one (chain, row, sweep) never overlap.
 constexpr uint32_t kSaltSpin = 0x5350494eu;      // "SPIN"
 constexpr uint32_t kSaltGauss = 0x47415553u;     // "GAUS"
-constexpr uint32_t kSaltCat = 0x43415400u;       // "CAT\0" + (category / 4)
+constexpr uint32_t kSaltCat = 0x43415400u;       // "CAT\0"
 // Dense (tensor-core) blocks draw along the unit axis of one chain: counter
 // (chain, row/4, sweep, salt) gives the spins of four consecutive rows,
 // (chain, row/2, sweep, salt) the two uniforms of two gaussian rows.
@@ -77,6 +77,49 @@ __host__ __device__ __forceinline__ uint32_t seed_lo(uint64_t s) { return (uint3
 __host__ __device__ __forceinline__ uint32_t seed_hi(uint64_t s) { return (uint32_t)(s >> 32); }
 
 #ifdef __CUDACC__
+// Categorical draw in Philox mode by inverse CDF from one uniform u, a sample
+// of softmax(theta): e_k = 2^((theta_k - max theta) * log2 e) (ex2.approx),
+// and the draw is the number of boundaries k < q - 1 that u reaches,
+// u >= C_k / S with C_k = e_0 + ... + e_k and S = C_(q-1).  Each boundary is
+// decided on the side where its mass is small: the head sum C_k against u*S
+// where C_k <= T_(k+1), else the tail sum T_(k+1) = e_(k+1) + ... + e_(q-1)
+// (summed from the end) against (1 - u)*S, which is exact in float32.  The
+// float32 error of a decision then stays near 1e-6 in logit units, inside the
+// 1e-5 threshold band of the parity criteria, at either end of the CDF.
+template <int QMAX>
+__device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int q, float u) {
+  constexpr bool kUnroll = QMAX <= 16;  // small bounds stay in registers
+  float m = theta[0];
+#pragma unroll(kUnroll ? QMAX : 1)
+  for (int k = 1; k < QMAX; ++k)
+    if (k < q) m = fmaxf(m, theta[k]);
+  const float ml = m * 1.44269502162933349609375f;
+  float e[QMAX], head[QMAX];
+  float s = 0.0f;
+#pragma unroll(kUnroll ? QMAX : 1)
+  for (int k = 0; k < QMAX; ++k) {
+    if (k < q) {
+      float v;
+      asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(__fmaf_rn(theta[k], 1.44269502162933349609375f, -ml)));
+      e[k] = v;
+      s = k == 0 ? v : __fadd_rn(s, v);
+      head[k] = s;
+    }
+  }
+  const float us = __fmul_rn(u, s), vs = __fmul_rn(1.0f - u, s);
+  int cat = 0;
+  float tail = 0.0f;  // T_(k+1) while boundary k is decided, walking down from the top
+#pragma unroll(kUnroll ? QMAX : 1)
+  for (int k = QMAX - 2; k >= 0; --k) {
+    if (k < q - 1) {
+      tail = k == q - 2 ? e[k + 1] : __fadd_rn(tail, e[k + 1]);
+      const bool reached = head[k] <= tail ? head[k] <= us : vs <= tail;
+      cat += reached ? 1 : 0;
+    }
+  }
+  return cat;
+}
+
 // Heat-bath spin decision in Philox mode: +1 with probability sigmoid(2*gamma)
 // (thrml's SpinGibbsConditional; tt_thrml/compiler.py:321-324), written as
 // u * (1 + exp(-2 gamma)) < 1 so a single exponential decides it.

@@ -160,22 +160,21 @@ __global__ void __launch_bounds__(256) k_group_generic(tthrml_group g) {
       for (int k = 0; k < q; ++k) theta[k] = seen ? __fadd_rn(theta[k], contrib[k]) : contrib[k];
       seen = true;
     }
-    // argmax(theta + g), first maximum wins (jnp.argmax; tt_thrml/compiler.py:343-344)
     int best = 0;
-    float best_v = 0.0f;
-    for (int k = 0; k < q; ++k) {
-      float gk;
-      if (VARIATES) {
-        gk = B.variates[((vsweep * B.n_nodes + i) * q + k) * C + chain];
-      } else {
-        const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)row, sweep, kSaltCat + (uint32_t)(k >> 2)}, k0, k1);
-        gk = -logf(-logf(uniform_open(word_of(r, k & 3))));
+    if (VARIATES) {
+      // argmax(theta + g), first maximum wins (jnp.argmax; tt_thrml/compiler.py:343-344)
+      float best_v = 0.0f;
+      for (int k = 0; k < q; ++k) {
+        const float v = __fadd_rn(theta[k], B.variates[((vsweep * B.n_nodes + i) * q + k) * C + chain]);
+        if (k == 0 || v > best_v) {
+          best_v = v;
+          best = k;
+        }
       }
-      const float v = __fadd_rn(theta[k], gk);
-      if (k == 0 || v > best_v) {
-        best_v = v;
-        best = k;
-      }
+    } else {
+      // one uniform per update: counter (chain / 4, row, sweep), word chain % 4
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)(gchain >> 2), (uint32_t)row, sweep, kSaltCat}, k0, k1);
+      best = categorical_icdf(theta, q, uniform_open(word_of(r, (int)(gchain & 3))));
     }
     store_value(out, out_idx, (float)best);
   } else {

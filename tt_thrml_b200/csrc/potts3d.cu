@@ -1,0 +1,213 @@
+// 3-D q-state Potts stencil kernel (checkerboard colour block of a periodic
+// X x Y x Z lattice).
+//
+// State layout: the flat int8 state [rows][n_chains] (chain innermost) of the
+// executor; colour block c holds the colour-c sites in increasing linear index
+// L = (z*Y + y)*X + x, so site L sits at block row L/2.  One thread updates
+// one 32-bit word of a row, i.e. four chains of one site: it loads the
+// matching word of its six neighbour rows (x-, x+, y-, y+, z-, z+, all of the
+// other colour), forms the q category fields
+//   theta_k = ((b_k + (Jx[k][s_x-] + Jx[k][s_x+])) + (Jy[k][s_y-] + Jy[k][s_y+]))
+//             + (Jz[k][s_z-] + Jz[k][s_z+])
+// (interactions summed over their terms first, then accumulated in program
+// order: tt_thrml/compiler.py:289-318), draws, and writes the word back.  Each
+// CTA first tabulates the rounded pair sums P_a[s0][s1][k] = J_a[k][s0] +
+// J_a[k][s1] in shared memory, so an axis costs one 32-byte lookup and q adds
+// per chain; categories outside [0, q) select all-zero matrix rows, as the
+// reference's one-hot selection gives them no weight.  Site coordinates come
+// from 32-bit divisions by invariant integers (multiply-high and shift).
+//
+// Draws: variates mode takes argmax(theta + g) over uploaded Gumbels
+// (tt_thrml/compiler.py:327-344, first maximum wins); Philox mode takes one
+// uniform from counter (chain/4, row, sweep, "CAT") and draws by inverse CDF
+// (categorical_icdf), exactly as the generic kernel does, so both kernels give
+// identical states.
+#include "common.cuh"
+
+namespace tthrml {
+namespace {
+
+constexpr int kPottsThreads = 256;
+constexpr int kPottsQ = 8;  // categories handled by this kernel
+constexpr int kRows = kPottsQ + 1;  // matrix rows per neighbour category, the last one all zero
+
+// n / d for 0 <= n < 2^31 as (umulhi(n, m) + n) >> l (Granlund and Montgomery,
+// "Division by invariant integers using multiplication", PLDI 1994).
+struct FastDiv {
+  uint32_t d, m, l;
+};
+FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, l};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return (__umulhi(n, f.m) + n) >> f.l; }
+
+template <bool VARIATES>
+__global__ void __launch_bounds__(kPottsThreads) k_potts3d(
+    int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
+    int32_t colour, int64_t target_row0, int64_t source_row0, const float* __restrict__ J,
+    const float* __restrict__ bias, int32_t q, int64_t chain_offset, const float* __restrict__ variates,
+    int64_t variates_sweeps, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl) {
+  // P[a][s0][s1][k] = J[a][k][s0] + J[a][k][s1] (float32), with J[a][k][s] = 0
+  // for s >= q (rows kPottsQ: categories out of range) and for k >= q
+  __shared__ __align__(16) float P[3][kRows][kRows][kPottsQ];
+  for (int i = threadIdx.x; i < 3 * kRows * kRows * kPottsQ; i += blockDim.x) {
+    const int k = i % kPottsQ, s1 = (i / kPottsQ) % kRows, s0 = (i / (kPottsQ * kRows)) % kRows;
+    const int a = i / (kPottsQ * kRows * kRows);
+    const float j0 = (s0 < q && k < q) ? J[((int64_t)a * q + k) * q + s0] : 0.0f;
+    const float j1 = (s1 < q && k < q) ? J[((int64_t)a * q + k) * q + s1] : 0.0f;
+    (&P[0][0][0][0])[i] = __fadd_rn(j0, j1);
+  }
+  __syncthreads();
+
+  const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
+  const uint64_t sd = ctl ? ctl->seed : seed;
+  const uint32_t k0 = seed_lo(sd), k1 = seed_hi(sd);
+  const uint32_t words = div_words.d;
+  const int64_t half = (int64_t)X * Y * Z / 2;
+  const uint32_t items = (uint32_t)(half * words);  // < 2^31, checked by the host
+  const int64_t XY = (int64_t)X * Y;
+  const int64_t vs = VARIATES ? (int64_t)(sweep % (uint32_t)(variates_sweeps > 0 ? variates_sweeps : 1)) : 0;
+
+  for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+    const uint32_t r = fdiv(it, div_words);
+    const uint32_t w = it - r * words;
+    const uint32_t even = 2 * r;
+    const uint32_t yz = fdiv(even, div_x);
+    const int32_t z = (int32_t)fdiv(yz, div_y);
+    const int32_t y = (int32_t)yz - z * Y;
+    const int32_t x = (int32_t)(even - yz * (uint32_t)X) + ((y + z + colour) & 1);
+    const int32_t xm = x == 0 ? X - 1 : x - 1, xp = x == X - 1 ? 0 : x + 1;
+    const int32_t ym = y == 0 ? Y - 1 : y - 1, yp = y == Y - 1 ? 0 : y + 1;
+    const int32_t zm = z == 0 ? Z - 1 : z - 1, zp = z == Z - 1 ? 0 : z + 1;
+    const int64_t zy = (int64_t)z * XY + (int64_t)y * X;
+    int64_t nb[6];
+    nb[0] = (zy + xm) >> 1;
+    nb[1] = (zy + xp) >> 1;
+    nb[2] = ((int64_t)z * XY + (int64_t)ym * X + x) >> 1;
+    nb[3] = ((int64_t)z * XY + (int64_t)yp * X + x) >> 1;
+    nb[4] = ((int64_t)zm * XY + (int64_t)y * X + x) >> 1;
+    nb[5] = ((int64_t)zp * XY + (int64_t)y * X + x) >> 1;
+    uint32_t nw[6];
+#pragma unroll
+    for (int j = 0; j < 6; ++j)
+      nw[j] = __ldg(reinterpret_cast<const uint32_t*>(state + (source_row0 + nb[j]) * C) + w);
+
+    float b[kPottsQ];
+#pragma unroll
+    for (int k = 0; k < kPottsQ; ++k) b[k] = k < q ? __ldg(bias + r * q + k) : 0.0f;
+
+    const int64_t row = target_row0 + r;
+    uint32_t out = 0u;
+    u32x4 rr{0u, 0u, 0u, 0u};
+    if (!VARIATES)
+      rr = philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w), (uint32_t)row, sweep, kSaltCat}, k0, k1);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      float theta[kPottsQ];
+#pragma unroll
+      for (int k = 0; k < kPottsQ; ++k) theta[k] = b[k];
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const uint32_t s0 = min(__byte_perm(nw[2 * a], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+        const uint32_t s1 = min(__byte_perm(nw[2 * a + 1], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+        const float4* pp = reinterpret_cast<const float4*>(&P[a][s0][s1][0]);
+        const float4 p0 = pp[0], p1 = pp[1];
+        theta[0] = __fadd_rn(theta[0], p0.x);
+        theta[1] = __fadd_rn(theta[1], p0.y);
+        theta[2] = __fadd_rn(theta[2], p0.z);
+        theta[3] = __fadd_rn(theta[3], p0.w);
+        theta[4] = __fadd_rn(theta[4], p1.x);
+        theta[5] = __fadd_rn(theta[5], p1.y);
+        theta[6] = __fadd_rn(theta[6], p1.z);
+        theta[7] = __fadd_rn(theta[7], p1.w);
+      }
+      int cat;
+      if (VARIATES) {
+        const float* g = variates + ((vs * half + r) * q) * C + 4 * w + v;
+        cat = 0;
+        float best = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kPottsQ; ++k) {
+          if (k < q) {
+            const float val = __fadd_rn(theta[k], __ldg(g + (int64_t)k * C));
+            if (k == 0 || val > best) {
+              best = val;
+              cat = k;
+            }
+          }
+        }
+      } else {
+        cat = categorical_icdf(theta, q, uniform_open(word_of(rr, v)));
+      }
+      out |= (uint32_t)cat << (8 * v);
+    }
+    reinterpret_cast<uint32_t*>(state + row * C)[w] = out;
+  }
+}
+
+template <bool VARIATES>
+int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int32_t colour, int64_t target_row0,
+                 int64_t source_row0, const float* J, const float* bias, int32_t q, int64_t chain_offset,
+                 const float* variates, int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                 const tthrml_run_ctl* ctl, cudaStream_t s) {
+  static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
+  if (!per_sm) {
+    int dev = 0, n = 0, b = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_potts3d<VARIATES>, kPottsThreads, 0);
+    if (e != cudaSuccess) return cuda_status(e, "k_potts3d set-up");
+    sms = n;
+    per_sm = b > 0 ? b : 1;
+  }
+  const int64_t items = (int64_t)X * Y * Z / 2 * (C / 4);
+  const int64_t need = (items + kPottsThreads - 1) / kPottsThreads;
+  const int64_t full = (int64_t)sms * per_sm;
+  const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
+  k_potts3d<VARIATES><<<grid, kPottsThreads, 0, s>>>(state, C, X, Y, Z, make_fastdiv((uint32_t)(C / 4)),
+                                                     make_fastdiv((uint32_t)X), make_fastdiv((uint32_t)Y), colour,
+                                                     target_row0, source_row0, J, bias, q, chain_offset, variates,
+                                                     variates_sweeps, seed, sweep, ctl);
+  return launch_status("k_potts3d launch");
+}
+
+}  // namespace
+}  // namespace tthrml
+
+extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, int32_t Y, int32_t Z, int32_t colour,
+                                   int64_t target_row0, int64_t source_row0, const float* J, const float* bias,
+                                   int32_t q, int64_t chain_offset, const float* variates, int64_t variates_sweeps,
+                                   uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, void* stream) {
+  using namespace tthrml;
+  if (!state || !J || !bias || X <= 0 || Y <= 0 || Z <= 0 || (X | Y | Z) & 1 || (colour != 0 && colour != 1)) {
+    set_error("tthrml_potts3d_step: invalid arguments (dimensions must be positive and even, colour 0 or 1)");
+    return TTHRML_ERR_ARG;
+  }
+  if (q < 1 || q > kPottsQ) {
+    set_error("tthrml_potts3d_step: q must be in [1, %d] (got %d)", kPottsQ, (int)q);
+    return TTHRML_ERR_ARG;
+  }
+  if (n_chains <= 0 || n_chains % 4 || chain_offset % 4 || ((uintptr_t)state % 16) ||
+      (variates && ((uintptr_t)variates % 16))) {
+    set_error("tthrml_potts3d_step: n_chains and chain_offset must be multiples of 4 and buffers 16-byte aligned");
+    return TTHRML_ERR_ARG;
+  }
+  const int64_t half = (int64_t)X * Y * Z / 2;
+  if (half * (n_chains / 4) >= (1ll << 31) || (int64_t)X * Y * Z >= (1ll << 31)) {
+    set_error("tthrml_potts3d_step: sites x chain words must stay below 2^31 per launch");
+    return TTHRML_ERR_UNSUPPORTED;
+  }
+  if (target_row0 < 0 || source_row0 < 0 || (target_row0 < source_row0 + half && source_row0 < target_row0 + half)) {
+    set_error("tthrml_potts3d_step: target and source blocks must be disjoint row ranges");
+    return TTHRML_ERR_ARG;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  if (variates)
+    return launch_potts<true>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset,
+                              variates, variates_sweeps, seed, sweep, ctl, s);
+  return launch_potts<false>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset,
+                             variates, variates_sweeps, seed, sweep, ctl, s);
+}

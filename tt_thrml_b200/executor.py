@@ -107,7 +107,6 @@ class Executor:
         self._rng_n_sweeps = 0
         self._timing_log: list[tuple[str, float, float]] = []
         self._scratch: dict[int, Any] = {}
-        self._pinned: dict[tuple, Any] = {}
         self._graphs: dict[int, Any] = {}
         self._ctl = None  # device tthrml_run_ctl read by graph-captured kernels
         self._ctl_value = None
@@ -307,7 +306,7 @@ class Executor:
         if n <= 0:
             return
         self._check_ready(n)
-        if not self.config.cuda_graphs or self.profile or n < 4:
+        if not self.config.cuda_graphs or self.profile or n < 2:
             for _ in range(n):
                 self.run_sweep()
             return
@@ -423,6 +422,19 @@ class Executor:
                     stream,
                 ),
                 "tthrml_dense_field_sample",
+            )
+        elif plan.kind == "potts3d":
+            bi = plan.block_indices[0]
+            v = self._variates(bi)
+            X, Y, Z = plan.dims
+            nat.check(
+                self._lib.tthrml_potts3d_step(
+                    self._global_state.data_ptr(), self.n_chains, X, Y, Z, plan.colour, plan.target_row0,
+                    plan.source_row0, plan.J.data_ptr(), plan.bias.data_ptr(), plan.q, self.chain_offset,
+                    None if v is None else v.data_ptr(), self._rng_n_sweeps if v is not None else 0, seed, sweep_idx,
+                    ctl, stream,
+                ),
+                "tthrml_potts3d_step",
             )
         elif plan.kind in ("spin_csr", "spin_bits"):
             step = self._lib.tthrml_spin_bits_step if plan.kind == "spin_bits" else self._lib.tthrml_spin_csr_step
@@ -542,14 +554,6 @@ class Executor:
         self._stream.synchronize()
         self._state_loaded = True
 
-    def _pinned_buffer(self, key, shape, dtype):
-        torch = _torch()
-        buf = self._pinned.get(key)
-        if buf is None or tuple(buf.shape) != tuple(shape) or buf.dtype != dtype:
-            buf = torch.empty(shape, dtype=dtype, pin_memory=True)
-            self._pinned[key] = buf
-        return buf
-
     def _decode_block(self, block_index: int, *, to_host: bool = True):
         """One block as chain-major (C, n) bool / int32 / float32 (tt_thrml/executor.py:433-438)."""
         torch = _torch()
@@ -563,7 +567,7 @@ class Executor:
                 dev = (b > 0).to(torch.uint8) if spec.family == Family.SPIN else b.contiguous()
             if not to_host:
                 return dev
-            host = self._pinned_buffer(("blk", block_index), dev.shape, dtype)
+            host = torch.empty(dev.shape, dtype=dtype, pin_memory=True)
             with torch.cuda.stream(self._stream):
                 host.copy_(dev, non_blocking=True)
             return host
@@ -585,7 +589,10 @@ class Executor:
         )
         if not to_host:
             return dev
-        host = self._pinned_buffer(("blk", block_index), dev.shape, dtype)
+        # a fresh pinned buffer from torch's caching host allocator: the caller
+        # receives it as is (no host-side copy) and it returns to the cache
+        # when the caller drops the array
+        host = torch.empty(dev.shape, dtype=dtype, pin_memory=True)
         with torch.cuda.stream(self._stream):
             host.copy_(dev, non_blocking=True)
         dev.record_stream(self._stream)
@@ -597,9 +604,9 @@ class Executor:
         out = []
         for bi, h in zip(block_indices, hosts):
             spec = self.compiled.blocks[bi].spec
-            a = h.numpy().copy()
+            a = h.numpy()  # shares the pinned buffer, which the array keeps alive
             if spec.family == Family.SPIN:
-                a = a.astype(bool)
+                a = a.view(np.bool_)  # decoded spins are 0 / 1 bytes
             out.append(a.reshape(spec.n_nodes) if self.n_chains == 1 else a)
         return out
 
@@ -619,8 +626,12 @@ class Executor:
         all_states = self._block_states_host(range(len(self.compiled.blocks)))
         return all_states[:n_free], all_states[n_free:]
 
-    def block_sums(self, blocks: Sequence) -> np.ndarray:
-        """Per-chain sum over the listed blocks' rows, on device; returns (n_chains,) float64."""
+    def block_sums(self, blocks: Sequence, *, to_host: bool = True):
+        """Per-chain sum over the listed blocks' rows, on device.
+
+        Returns a (n_chains,) float64 numpy array, or the device tensor when
+        to_host is False (no synchronisation).
+        """
         torch = _torch()
         lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
         with torch.cuda.stream(self._stream):
@@ -632,6 +643,8 @@ class Executor:
                 for b in blocks:
                     bi = lookup[id(b)] if not isinstance(b, int) else b
                     out += self._dense_block_values(bi).double().sum(1)
+                if not to_host:
+                    return out
                 host = out.cpu()
             return host.numpy()
         for b in blocks:
@@ -649,6 +662,8 @@ class Executor:
                 ),
                 "tthrml_sum_rows",
             )
+        if not to_host:
+            return out
         with torch.cuda.stream(self._stream):
             host = out.cpu()
         return host.numpy()
@@ -691,13 +706,15 @@ class Executor:
             return f_observe(self.program, state_free, state_clamped, carry, np.asarray(i))
 
         carry, obs = observe(carry, 0)
-        if schedule.n_samples <= 1:
-            return carry, tree_expand(obs)
         all_obs = [obs]
         for i in range(1, schedule.n_samples):
             self.run_sweeps(schedule.steps_per_sample)
             carry, obs = observe(carry, i)
             all_obs.append(obs)
+        if device_side:  # observations are device tensors: one read-back for the whole run
+            all_obs = _device_obs_to_host(all_obs, self._stream)
+        if schedule.n_samples <= 1:
+            return carry, tree_expand(all_obs[0])
         if all(o is None for o in all_obs):
             return carry, None
         return carry, tree_stack(all_obs)
@@ -719,6 +736,22 @@ class Executor:
                 "kernel_total_ms": sum(ks),
             }
         return summary
+
+
+def _device_obs_to_host(all_obs: list, stream) -> list:
+    """Stacks per-sample device tensors (or lists/tuples of them) and copies them to the host once."""
+    torch = _torch()
+    first = all_obs[0]
+    if first is None:
+        return all_obs
+    if isinstance(first, (list, tuple)):
+        cols = [_device_obs_to_host([o[k] for o in all_obs], stream) for k in range(len(first))]
+        return [type(first)(c[i] for c in cols) for i in range(len(all_obs))]
+    if not isinstance(first, torch.Tensor):
+        return all_obs
+    with torch.cuda.stream(stream):
+        host = torch.stack(all_obs).cpu().numpy()
+    return list(host)
 
 
 def make_executor(

@@ -217,7 +217,9 @@ class MeshExecutor(Executor):
         merged = self._state_lists()
         return {b: merged[lookup[id(b)]] for b in blocks if id(b) in lookup}
 
-    def block_sums(self, blocks: Sequence) -> np.ndarray:
+    def block_sums(self, blocks: Sequence, *, to_host: bool = True) -> np.ndarray:
+        """Per-chain sums over all shards; always a host array (the shards live on several devices)."""
+        del to_host
         return self._gather_chains([sh.block_sums(blocks) for sh in self.shards])
 
     def sample_states(self, key, schedule, nodes_to_sample, *, init_state_free, state_clamp=()):

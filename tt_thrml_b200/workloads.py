@@ -333,3 +333,123 @@ def gaussian_bernoulli_rbm(
     prog = DenseBipartiteProgram(W, b_v, b_h, name=f"gb-rbm-{n_visible}x{n_hidden}")
     prog.meta.update(seed=seed, w_std=w_std, visible_bias_variance=visible_bias_variance)
     return prog
+
+
+class PottsLattice3D(TableProgram):
+    """q-state Potts model on a periodic X x Y x Z lattice, two checkerboard blocks.
+
+    Site (x, y, z) has linear index L = (z*Y + y)*X + x and colour (x+y+z) % 2;
+    block c holds the colour-c sites in increasing L, so site L sits at block
+    row L // 2 (X even).  Field of category k at a site:
+        theta_k = ((b[k] + (Jx[k][s_x-] + Jx[k][s_x+])) + (Jy[k][s_y-] + Jy[k][s_y+]))
+                  + (Jz[k][s_z-] + Jz[k][s_z+])
+    i.e. four interactions (bias, x pair, y pair, z pair), each summed over its
+    terms first, in the order the reference accumulates interactions
+    (tt_thrml/compiler.py:289-318).  `tt_stencil()` describes the lattice for
+    the stencil kernel; `tt_lower_blocks()` builds the equivalent per-term
+    tables (each term carries a q x q matrix) for the generic kernel and the
+    oracle, which is only reasonable for small lattices.
+    """
+
+    MAX_TABLE_SITES = 1 << 18
+
+    def __init__(self, dims, J, bias, *, name: str = "potts3d"):
+        X, Y, Z = (int(d) for d in dims)
+        if X % 2 or Y % 2 or Z % 2:
+            raise ValueError("the checkerboard colouring of a periodic lattice needs even dimensions")
+        J = np.ascontiguousarray(J, dtype=np.float32)
+        q = int(J.shape[-1])
+        if J.shape != (3, q, q):
+            raise ValueError(f"J must have shape (3, q, q), got {J.shape}")
+        n = X * Y * Z
+        bias = np.ascontiguousarray(bias, dtype=np.float32).reshape(n, q)
+        blocks = [IndexBlock(n // 2, Family.CATEGORICAL, q, name=f"colour{c}:") for c in range(2)]
+        gspec = TableGibbsSpec(free_blocks=blocks, clamped_blocks=[], sampling_order=[[0], [1]])
+        super().__init__(gspec, [], {"name": name, "dims": (X, Y, Z), "q": q, "n_sites": n})
+        self.dims = (X, Y, Z)
+        self.q = q
+        self.J = J
+        self.site_bias = bias
+        self._specs = None
+
+    def sites_of_block(self, c: int) -> np.ndarray:
+        """Linear site indices of block c, in block-row order."""
+        X, Y, Z = self.dims
+        r = np.arange(X * Y * Z // 2, dtype=np.int64)
+        even = 2 * r
+        y = (even // X) % Y
+        z = even // (X * Y)
+        return even + ((y + z + c) & 1)
+
+    def tt_stencil(self) -> dict:
+        return {
+            "kind": "potts3d",
+            "dims": self.dims,
+            "q": self.q,
+            "J": self.J,
+            "bias": [self.site_bias[self.sites_of_block(c)] for c in range(2)],
+            "block_rows": (0, self.n_sites // 2),
+        }
+
+    @property
+    def n_sites(self) -> int:
+        X, Y, Z = self.dims
+        return X * Y * Z
+
+    def neighbour_rows(self, c: int) -> np.ndarray:
+        """(n/2, 6) flat state rows of the neighbours (x-, x+, y-, y+, z-, z+) of block c's sites."""
+        X, Y, Z = self.dims
+        L = self.sites_of_block(c)
+        x, y, z = L % X, (L // X) % Y, L // (X * Y)
+        half = self.n_sites // 2
+        other = (1 - c) * half
+        out = []
+        for dx, dy, dz in ((-1, 0, 0), (1, 0, 0), (0, -1, 0), (0, 1, 0), (0, 0, -1), (0, 0, 1)):
+            Ln = (((z + dz) % Z) * Y + (y + dy) % Y) * X + (x + dx) % X
+            out.append(other + Ln // 2)
+        return np.stack(out, axis=1)
+
+    def tt_lower_blocks(self):
+        if self._specs is None:
+            n, q = self.n_sites, self.q
+            if n > self.MAX_TABLE_SITES:
+                raise ValueError(
+                    f"per-term tables of a {self.dims} Potts lattice take {n * 6 * q * q * 4 / 2**30:.1f} GiB; "
+                    "the stencil kernel runs it without them"
+                )
+            half = n // 2
+            specs = []
+            for c in range(2):
+                nb = self.neighbour_rows(c).astype(np.int32)
+                inters = [
+                    FusedInteractionSpec(
+                        weighted_mask=self.site_bias[self.sites_of_block(c)].reshape(half, 1, q),
+                        gather_indices=(), n_spin=0, n_categorical=0, n_terms=1, contribution_kind="default",
+                    )
+                ]
+                for a in range(3):
+                    wm = np.broadcast_to(self.J[a], (half, 2, q, q)).copy()
+                    inters.append(
+                        FusedInteractionSpec(
+                            weighted_mask=wm, gather_indices=(np.ascontiguousarray(nb[:, 2 * a : 2 * a + 2]),),
+                            n_spin=0, n_categorical=1, n_terms=2, contribution_kind="default",
+                        )
+                    )
+                specs.append(FusedBlockSpec(c, Family.CATEGORICAL, half, q, c * half, n, tuple(inters)))
+            self._specs = specs
+        return list(self._specs)
+
+
+def potts_lattice_3d(
+    side: int = 128, q: int = 8, *, seed: int = 0, j_std: float = 1.0, bias_variance: float = 0.5
+) -> PottsLattice3D:
+    """3-D q-state Potts lattice side^3 (periodic): per axis one q x q matrix with
+    entries ~ N(0, j_std^2), symmetrised as (A + A^T) / 2; per-site bias
+    q-vectors ~ N(0, bias_variance) (0.5 read as the variance)."""
+    rng = np.random.default_rng(seed)
+    A = (rng.standard_normal((3, q, q)) * j_std).astype(np.float32)
+    J = ((A + A.transpose(0, 2, 1)) * np.float32(0.5)).astype(np.float32)
+    bias = (rng.standard_normal((side**3, q)) * np.sqrt(bias_variance)).astype(np.float32)
+    prog = PottsLattice3D((side, side, side), J, bias, name=f"potts3d-{side}-q{q}")
+    prog.meta.update(seed=seed, j_std=j_std, bias_variance=bias_variance)
+    return prog
