@@ -219,6 +219,34 @@ int tthrml_potts3d_step(int8_t* state_dev, int64_t n_chains, int32_t X, int32_t 
                         uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl_dev, void* stream);
 
 /*
+ * One checkerboard half-sweep of a single-chain 2-D Ising lattice (uniform
+ * couplings) on split-colour int8 state.  Replaces the spin group kernel
+ * (tt_thrml/compiler.py:303-324) for lattice programs, where neighbours follow
+ * from the site position.  colour_state / other_state: int8 +-1 arrays
+ * [rows_local][width/2] of the updated colour and of the other colour; local
+ * row i is lattice row (global_row0 + i) mod height; site (Y, x) of colour
+ * (x + Y) % 2 is column x/2.  Rows [row_lo, row_hi) are updated; their up and
+ * down neighbours are local rows i-1 and i+1 (halo rows of a strip), or wrap
+ * around when wrap_rows is set (rows_local == height, the whole lattice).
+ * The decision uses the 4 neighbour signs (left, right, up, down; bit set =
+ * -1) as an index into thresholds[16] (Philox: "up" iff (bits >> 9) <
+ * threshold) or fields[16] (variates: "up" iff 2 * field > logit, variates
+ * [variates_sweeps][height * width/2] per colour block).  Philox counter
+ * (chain, (block_row0 + Y*width/2 + x/2) / 4, sweep, "DSPI").  trace (NULL to
+ * skip): int64 [trace_len][2]; entry `sweep` receives the sum of the new
+ * spins of local rows [count_lo, count_hi) and, for colour 1, the bond sum
+ * sum_i s_i (s_left + s_right + s_up + s_down) over them.  Requires width %
+ * 32 == 0, even height and 16-byte aligned buffers.
+ */
+int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, int64_t width, int64_t rows_local,
+                             int32_t wrap_rows, int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height,
+                             int32_t colour, int64_t block_row0, const uint32_t* thresholds_dev,
+                             const float* fields_dev, const float* variates_dev, int64_t variates_sweeps,
+                             int64_t chain, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl_dev,
+                             int64_t count_lo, int64_t count_hi, int64_t* trace_dev, int64_t trace_len,
+                             void* stream);
+
+/*
  * Dense bipartite block update on the tensor cores (tcgen05, bf16 operands,
  * fp32 accumulation in TMEM).  Replaces the group kernel of a block whose
  * interaction with another block is a dense weight matrix (the RBM case:

@@ -48,9 +48,10 @@ typedef struct {
   int32_t cat_q[4];
 } or_interaction;
 
-/* rng_layout 0: one Philox counter per (site, chain group), as the sparse and
- * generic kernels draw; 1: counters along the unit axis of one chain, as the
- * dense tensor-core kernel draws (tt_thrml_b200/csrc/dense_tc.cu draw_chunk) */
+/* rng_layout 0: counter (chain/4, row, sweep), word chain % 4, as the sparse,
+ * generic and Potts kernels draw; 1: counter (chain, row/4, sweep), word
+ * row % 4, as the dense tensor-core kernel and the 2-D lattice stencil kernel
+ * draw (four consecutive rows of one chain per counter) */
 typedef struct {
   int32_t family, q, n_interactions, rng_layout;
   int64_t n_nodes, row_start;

@@ -311,13 +311,19 @@ class OracleSampler:
     """Runs lowered programs on the CPU over a float32 [rows, chains] state."""
 
     def __init__(self, program, n_chains: int = 1, chain_offset: int = 0, n_threads: int | None = None,
-                 rng_layout: str = "site"):
-        """rng_layout: "site" (Philox counter per site and chain group, the sparse and
-        generic kernels) or "dense" (counters along one chain's unit axis, the
-        tensor-core dense kernel)."""
-        if rng_layout not in ("site", "dense"):
-            raise ValueError(f"rng_layout must be 'site' or 'dense', got {rng_layout!r}")
-        self.rng_layout = 1 if rng_layout == "dense" else 0
+                 rng_layout="chain4"):
+        """rng_layout: Philox counter layout of Philox-mode draws, one name for
+        every block or a dict block index -> name.  "chain4": counter (chain/4,
+        row, sweep), word chain % 4 (the sparse, generic and Potts kernels);
+        "row4": counter (chain, row/4, sweep), word row % 4 (the tensor-core
+        dense kernel and the 2-D lattice stencil kernel)."""
+        names = {"chain4": 0, "row4": 1}
+        layouts = rng_layout if isinstance(rng_layout, dict) else None
+        for v in (layouts.values() if layouts is not None else [rng_layout]):
+            if v not in names:
+                raise ValueError(f"rng_layout must be 'chain4' or 'row4', got {v!r}")
+        self._rng_layout = {int(k): names[v] for k, v in layouts.items()} if layouts is not None else {}
+        self._rng_default = 0 if layouts is not None else names[rng_layout]
         self.prog = program if isinstance(program, OProgram) else lower_program(program)
         self.program = program
         self.C = int(n_chains)
@@ -379,7 +385,7 @@ class OracleSampler:
             d.n_interactions = len(b.interactions)
             d.n_nodes = b.n_nodes
             d.row_start = b.start
-            d.rng_layout = self.rng_layout
+            d.rng_layout = self._rng_layout.get(int(bi), self._rng_default)
             d.inter = ctypes.addressof(self._inter_structs[bi])
             if variates is not None:
                 v = np.ascontiguousarray(variates[bi], dtype=np.float32)

@@ -28,6 +28,15 @@ class ParityReport:
         return self.band / max(1, self.sites)
 
 
+def rng_layouts(compiled) -> dict:
+    """Block index -> Philox counter layout of the kernel that samples it."""
+    out = {}
+    for g in compiled.sampling_groups:
+        for bi in g.block_indices:
+            out[int(bi)] = getattr(g.kernel_artifact, "rng_layout", "chain4")
+    return out
+
+
 def random_init(program, C, seed=0, clamp=None):
     rng = np.random.default_rng(seed)
     out = []
@@ -116,8 +125,7 @@ def run_parity(program, C: int, n_sweeps: int, *, mode: str, seed: int = 11, ini
                            dense_precision=dense_precision)
     compiled = compile_program(None, 0, program, cfg, n_sweeps=n_sweeps, n_chains=C, force_generic=force_generic)
     ex = Executor(None, 0, program, cfg, compiled, n_sweeps=n_sweeps, n_chains=C)
-    dense = compiled.state_dtype == "dense_bf16"
-    o = orc.OracleSampler(program, n_chains=C, rng_layout="dense" if dense else "site")
+    o = orc.OracleSampler(program, n_chains=C, rng_layout=rng_layouts(compiled))
     init = init if init is not None else random_init(program, C, seed)
     ex.load_state(init, clamp)
     o.load_state(init, clamp)

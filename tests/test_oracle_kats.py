@@ -163,7 +163,7 @@ def test_oracle_dense_rng_layout_differs_from_site_layout():
     rng = np.random.default_rng(13)
     init = [rng.standard_normal((8, 256)).astype(np.float32), rng.integers(0, 2, (8, 256)).astype(bool)]
     res = []
-    for layout in ("site", "dense"):
+    for layout in ("chain4", "row4"):
         o = orc.OracleSampler(prog, n_chains=8, rng_layout=layout)
         o.load_state(init)
         o.group_step(0, 0, seed=99)

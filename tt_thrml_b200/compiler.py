@@ -646,6 +646,7 @@ class DenseGroupPlan:
     in_place: bool = True
     group_rows: int = 0
     device: Any = None
+    rng_layout: str = "row4"  # Philox counter (chain, row / 4, sweep), word row % 4
 
 
 DENSE_CHAIN_MULTIPLE = 128
@@ -748,6 +749,49 @@ class PottsStencilGroupPlan:
 POTTS_MAX_Q = 8
 
 
+@dataclass
+class IsingStencilGroupPlan:
+    """One checkerboard colour of a single-chain 2-D Ising lattice (tthrml_ising2d_halfsweep)."""
+
+    block_indices: tuple[int, ...]
+    dims: tuple[int, int]
+    colour: int
+    target_row0: int
+    source_row0: int
+    thresholds: Any  # uint32 [16] device tensor (Philox mode)
+    fields: Any  # float32 [16] device tensor (variates mode)
+    family: Family = Family.SPIN
+    family_label: str = "spin"
+    kind: str = "ising2d"
+    in_place: bool = True
+    group_rows: int = 0
+    device: Any = None
+    rng_layout: str = "row4"  # Philox counter (chain, row / 4, sweep), word row % 4
+
+
+def ising_pattern_tables(edge_weight, site_bias) -> tuple[np.ndarray, np.ndarray]:
+    """(fields float32 [16], thresholds uint32 [16]) of a uniform lattice site.
+
+    Pattern bit k (k = 0..3: left, right, up, down) set means neighbour k is
+    -1.  field = b + (((w s_0 + w s_1) + w s_2) + w s_3) in float32 -- the
+    bias interaction first, then the pair interaction summed over its terms
+    (tt_thrml/compiler.py:303-318).  threshold = ceil((sigmoid(2 field) 2^24 -
+    1) / 2): with u = (2m + 1) / 2^24 the Philox uniform of m = bits >> 9,
+    u < sigmoid(2 field) exactly when m < threshold.
+    """
+    w, b = np.float32(edge_weight), np.float32(site_bias)
+    fields = np.empty(16, np.float32)
+    for idx in range(16):
+        terms = [np.float32(-w) if (idx >> k) & 1 else w for k in range(4)]
+        acc = terms[0]
+        for t in terms[1:]:
+            acc = np.float32(acc + t)
+        fields[idx] = np.float32(b + acc)
+    p = 1.0 / (1.0 + np.exp(-2.0 * fields.astype(np.float64)))
+    thr = np.ceil((p * 2.0**24 - 1.0) / 2.0)
+    return fields, np.clip(thr, 0, 2**23).astype(np.uint32)
+
+
 def stencil_eligible(program, n_chains: int) -> bool:
     """True when the program is a lattice the stencil kernels run at this chain count."""
     stencil = getattr(program, "tt_stencil", None)
@@ -756,12 +800,29 @@ def stencil_eligible(program, n_chains: int) -> bool:
     st = stencil()
     if st.get("kind") == "potts3d":
         return 1 <= int(st["q"]) <= POTTS_MAX_Q and n_chains % 4 == 0
+    if st.get("kind") == "ising2d":
+        H, W = st["dims"]
+        return n_chains == 1 and W % 32 == 0 and H % 2 == 0
     return False
 
 
 def _plan_stencil(program, device):
     torch = _torch()
     st = program.tt_stencil()
+    if st["kind"] == "ising2d":
+        fields, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
+        f_dev = torch.from_numpy(fields).to(device)
+        t_dev = torch.from_numpy(thr.view(np.int32)).to(device)
+        rows = st["block_rows"]
+        H, W = st["dims"]
+        return [
+            IsingStencilGroupPlan(
+                block_indices=(int(g[0]),), dims=(int(H), int(W)), colour=int(g[0]), target_row0=int(rows[int(g[0])]),
+                source_row0=int(rows[1 - int(g[0])]), thresholds=t_dev, fields=f_dev, group_rows=H * W // 2,
+                device=device,
+            )
+            for g in program.gibbs_spec.sampling_order
+        ]
     if st["kind"] != "potts3d":
         raise ValueError(f"unknown stencil kind {st['kind']!r}")
     J = torch.from_numpy(np.ascontiguousarray(st["J"], dtype=np.float32)).to(device)
@@ -785,10 +846,12 @@ def _stencil_specs(program):
     st = program.tt_stencil()
     blocks = program.gibbs_spec.blocks
     total = sum(len(b.nodes) for b in blocks)
-    q = int(st["q"])
+    if st["kind"] == "ising2d":
+        fam, q = Family.SPIN, None
+    else:
+        fam, q = Family.CATEGORICAL, int(st["q"])
     return tuple(
-        FusedBlockSpec(bi, Family.CATEGORICAL, len(b.nodes), q, int(st["block_rows"][bi]), total, ())
-        for bi, b in enumerate(blocks)
+        FusedBlockSpec(bi, fam, len(b.nodes), q, int(st["block_rows"][bi]), total, ()) for bi, b in enumerate(blocks)
     )
 
 
@@ -854,4 +917,6 @@ __all__ = [
     "SpinCSRGroupPlan",
     "DenseGroupPlan",
     "PottsStencilGroupPlan",
+    "IsingStencilGroupPlan",
+    "ising_pattern_tables",
 ]

@@ -1,0 +1,225 @@
+// Single-chain 2-D Ising checkerboard half-sweep on a split-colour int8 lattice.
+//
+// Layout: colour c of an H x W periodic lattice (W % 32 == 0) is an int8 array
+// [rows][W/2] of +-1 spins: site (Y, x) of colour c = (x + Y) % 2 sits at row
+// Y, column x/2 -- exactly the executor's block-ordered flat state of a
+// lattice program with one chain (block row = linear index / 2).  A strip of
+// the lattice is the same array restricted to some rows, with halo rows above
+// and below holding the neighbours' rows.
+//
+// One thread updates 16 consecutive sites of a row (one 16-byte vector): the
+// other colour's rows Y-1, Y, Y+1 give the up, left/right and down
+// neighbours; site j of row Y (x = 2j + p, p = (Y + c) % 2) has its left and
+// right neighbours at other-colour columns j-1+p and j+p.  The four sign bits
+// (left, right, up, down: the reference lattice's neighbour order) index a
+// 16-entry table built on the host from the program's float32 weights:
+//   Philox mode: threshold T with "up" iff (bits >> 9) < T, the exact integer
+//     form of u < sigmoid(2 * gamma) for u = (2 (bits >> 9) + 1) / 2^24;
+//   variates mode: the float32 field gamma, "up" iff 2 * gamma > logit.
+// gamma is the left-to-right float32 sum of the bias interaction and the
+// pair terms (tt_thrml/compiler.py:303-324), so both modes decide as the
+// table-driven kernels do.  Philox counter: (chain, flat row / 4, sweep,
+// "DSPI"), word flat row % 4 -- four consecutive sites of a row per call.
+//
+// Observables (optional, for the energy/magnetisation trace): the sum of the
+// new spins over the counted rows, and in the colour-1 half-sweep the bond
+// sum sum_i s_i (s_left + s_right + s_up + s_down), which counts every bond
+// of the lattice once; both exact int64, one atomic per CTA.
+#include "common.cuh"
+
+namespace tthrml {
+namespace {
+
+constexpr int kIsingThreads = 256;
+
+__device__ __forceinline__ uint4 ld16(const int8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+template <bool VARIATES, bool TRACE>
+__global__ void __launch_bounds__(kIsingThreads) k_ising2d(
+    int8_t* __restrict__ cc, const int8_t* __restrict__ co, int64_t half_w, int64_t rows_local, int32_t wrap,
+    int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+    const uint32_t* __restrict__ thresholds, const float* __restrict__ fields, const float* __restrict__ variates,
+    int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl,
+    int64_t count_lo, int64_t count_hi, unsigned long long* __restrict__ trace, int64_t trace_len) {
+  __shared__ uint32_t T[16];
+  __shared__ float F[16];
+  __shared__ long long red[2];
+  if (threadIdx.x < 16) {
+    if (VARIATES)
+      F[threadIdx.x] = fields[threadIdx.x];
+    else
+      T[threadIdx.x] = thresholds[threadIdx.x];
+  }
+  if (TRACE && threadIdx.x < 2) red[threadIdx.x] = 0;
+  __syncthreads();
+
+  const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
+  const uint64_t sd = ctl ? ctl->seed : seed;
+  const uint32_t k0 = seed_lo(sd), k1 = seed_hi(sd);
+  const int64_t chunks = half_w >> 4;
+  const int64_t items = (row_hi - row_lo) * chunks;
+  const int64_t vs = VARIATES ? (int64_t)(sweep % (uint32_t)(variates_sweeps > 0 ? variates_sweeps : 1)) : 0;
+  long long mag = 0, bonds = 0;
+
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = row_lo + it / chunks;  // local row
+    const int64_t j0 = (it % chunks) << 4;   // first column
+    int64_t Y = global_row0 + i;
+    if (Y >= height) Y -= height;
+    if (Y >= height) Y -= height;
+    const int p = (int)((Y + colour) & 1);
+    const int64_t iu = i == 0 ? (wrap ? rows_local - 1 : 0) : i - 1;
+    const int64_t id = i == rows_local - 1 ? (wrap ? 0 : i) : i + 1;
+    const int8_t* rowc = co + i * half_w;
+    const uint4 mid = ld16(rowc + j0);
+    const uint4 up = ld16(co + iu * half_w + j0);
+    const uint4 dn = ld16(co + id * half_w + j0);
+    // the byte beyond the 16 on the neighbour side (periodic in x)
+    const int64_t je = p ? (j0 + 16 == half_w ? 0 : j0 + 16) : (j0 == 0 ? half_w - 1 : j0 - 1);
+    const uint32_t edge = (uint32_t)(uint8_t)__ldg(rowc + je);
+    const uint32_t m[6] = {p ? 0u : edge << 24, mid.x, mid.y, mid.z, mid.w, p ? edge : 0u};
+    const uint32_t uw[4] = {up.x, up.y, up.z, up.w};
+    const uint32_t dw[4] = {dn.x, dn.y, dn.z, dn.w};
+
+    const int64_t flat0 = block_row0 + Y * half_w + j0;  // flat row of the first site
+    uint32_t outw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      // neighbour words of sites 4k..4k+3
+      const uint32_t L = p ? m[k + 1] : __byte_perm(m[k], m[k + 1], 0x6543u);
+      const uint32_t R = p ? __byte_perm(m[k + 1], m[k + 2], 0x4321u) : m[k + 1];
+      const uint32_t idx4 = ((L >> 7) & 0x01010101u) | ((R >> 6) & 0x02020202u) | ((uw[k] >> 5) & 0x04040404u) |
+                            ((dw[k] >> 4) & 0x08080808u);
+      uint32_t minus = 0u;  // bit 8v set: site 4k+v samples -1
+      if (VARIATES) {
+        const float* lrow = variates + vs * (height * half_w) + (flat0 - block_row0) + 4 * k;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float g = F[(idx4 >> (8 * v)) & 0xFu];
+          minus |= (__fmul_rn(2.0f, g) > __ldg(lrow + v) ? 0u : 1u) << (8 * v);
+        }
+      } else {
+        const int64_t flat = flat0 + 4 * k;
+        const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, (uint32_t)(flat >> 2), sweep, kSaltDenseSpin}, k0, k1);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          minus |= ((word_of(r, v) >> 9) < T[(idx4 >> (8 * v)) & 0xFu] ? 0u : 1u) << (8 * v);
+      }
+      outw[k] = 0x01010101u + minus * 0xFEu;  // +1 -> 0x01, -1 -> 0xFF per byte
+      if (TRACE && i >= count_lo && i < count_hi) {
+        const int nm = __popc(minus);
+        mag += 4 - 2 * nm;
+        if (colour == 1) {
+          // sum_v s_v * n_v with n_v = 4 - 2 k_v (k_v minus neighbours), s_v = 1 - 2 m_v
+          const int ksum = __popc(idx4);
+          const int mk = __popc(idx4 & (minus * 0x0Fu));
+          bonds += 4 * (4 - 2 * nm) - 2 * ksum + 4 * mk;
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(cc + i * half_w + j0) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+  }
+  if (TRACE) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mag += __shfl_xor_sync(0xffffffffu, mag, o);
+      bonds += __shfl_xor_sync(0xffffffffu, bonds, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red[0]), (unsigned long long)mag);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red[1]), (unsigned long long)bonds);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && (int64_t)sweep < trace_len) {
+      atomicAdd(trace + 2 * (int64_t)sweep, (unsigned long long)red[0]);
+      if (colour == 1) atomicAdd(trace + 2 * (int64_t)sweep + 1, (unsigned long long)red[1]);
+    }
+  }
+}
+
+template <bool VARIATES, bool TRACE>
+int launch_ising(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_local, int32_t wrap, int64_t row_lo,
+                 int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                 const uint32_t* thresholds, const float* fields, const float* variates, int64_t variates_sweeps,
+                 int64_t chain, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int64_t count_lo,
+                 int64_t count_hi, unsigned long long* trace, int64_t trace_len, cudaStream_t s) {
+  static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
+  if (!per_sm) {
+    int dev = 0, n = 0, b = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_ising2d<VARIATES, TRACE>, kIsingThreads, 0);
+    if (e != cudaSuccess) return cuda_status(e, "k_ising2d set-up");
+    sms = n;
+    per_sm = b > 0 ? b : 1;
+  }
+  const int64_t items = (row_hi - row_lo) * (half_w >> 4);
+  const int64_t need = (items + kIsingThreads - 1) / kIsingThreads;
+  const int64_t full = (int64_t)sms * per_sm;
+  const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
+  k_ising2d<VARIATES, TRACE><<<grid, kIsingThreads, 0, s>>>(
+      cc, co, half_w, rows_local, wrap, row_lo, row_hi, global_row0, height, colour, block_row0, thresholds, fields,
+      variates, variates_sweeps, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len);
+  return launch_status("k_ising2d launch");
+}
+
+}  // namespace
+}  // namespace tthrml
+
+extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, int64_t width,
+                                        int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                        int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                        const uint32_t* thresholds, const float* fields, const float* variates,
+                                        int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
+                                        const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
+                                        int64_t* trace, int64_t trace_len, void* stream) {
+  using namespace tthrml;
+  if (!colour_state || !other_state || (colour != 0 && colour != 1)) {
+    set_error("tthrml_ising2d_halfsweep: invalid arguments");
+    return TTHRML_ERR_ARG;
+  }
+  if (width <= 0 || width % 32 || height <= 0 || height % 2 || rows_local <= 0) {
+    set_error("tthrml_ising2d_halfsweep: width must be a positive multiple of 32 and height positive and even "
+              "(got %lld x %lld)", (long long)height, (long long)width);
+    return TTHRML_ERR_ARG;
+  }
+  if (row_lo < 0 || row_hi > rows_local || row_lo > row_hi || global_row0 < 0 || global_row0 >= height ||
+      rows_local > 2 * height) {
+    set_error("tthrml_ising2d_halfsweep: row range [%lld, %lld) outside the %lld local rows", (long long)row_lo,
+              (long long)row_hi, (long long)rows_local);
+    return TTHRML_ERR_ARG;
+  }
+  if (!wrap_rows && (row_lo < 1 || row_hi > rows_local - 1)) {
+    set_error("tthrml_ising2d_halfsweep: without wrapping, updated rows need a halo row on both sides");
+    return TTHRML_ERR_ARG;
+  }
+  if (wrap_rows && rows_local != height) {
+    set_error("tthrml_ising2d_halfsweep: wrapping rows needs the whole lattice (rows_local == height)");
+    return TTHRML_ERR_ARG;
+  }
+  if (variates ? !fields : !thresholds) {
+    set_error("tthrml_ising2d_halfsweep: %s table missing", variates ? "field" : "threshold");
+    return TTHRML_ERR_ARG;
+  }
+  if (((uintptr_t)colour_state % 16) || ((uintptr_t)other_state % 16) || (variates && (uintptr_t)variates % 16)) {
+    set_error("tthrml_ising2d_halfsweep: buffers must be 16-byte aligned");
+    return TTHRML_ERR_ARG;
+  }
+  if (row_hi == row_lo) return TTHRML_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned long long* tr = reinterpret_cast<unsigned long long*>(trace);
+  const int64_t hw = width / 2;
+#define TTHRML_ISING_LAUNCH(V, TR)                                                                                  \
+  return launch_ising<V, TR>(colour_state, other_state, hw, rows_local, wrap_rows, row_lo, row_hi, global_row0,   \
+                             height, colour, block_row0, thresholds, fields, variates, variates_sweeps, chain, seed, \
+                             sweep, ctl, count_lo, count_hi, tr, trace_len, s)
+  if (variates) {
+    if (trace) TTHRML_ISING_LAUNCH(true, true);
+    TTHRML_ISING_LAUNCH(true, false);
+  }
+  if (trace) TTHRML_ISING_LAUNCH(false, true);
+  TTHRML_ISING_LAUNCH(false, false);
+#undef TTHRML_ISING_LAUNCH
+}

@@ -145,10 +145,89 @@ def lattice_2d_csr(height: int, width: int, periodic: bool = True):
     return row_ptr, nb[valid]
 
 
+class IsingLattice2D(TableProgram):
+    """Periodic H x W Ising lattice with uniform coupling J and field h, two checkerboard blocks.
+
+    Site (y, x) has linear index L = y*W + x and colour (x + y) % 2; block c
+    holds the colour-c sites in increasing L, so site L sits at block row L // 2
+    (W even) and each block is the split-colour array [H][W/2].  Couplings are
+    beta*J per edge and beta*h per site in float32, neighbours in the order
+    (left, right, up, down), i.e. exactly the tables `spin_graph_program`
+    builds from `lattice_2d_csr` -- `tt_lower_blocks()` materialises them on
+    demand (small lattices; a 32768^2 lattice would need ~32 GB of tables).
+    `tt_stencil()` describes the lattice for the single-chain stencil kernel.
+    """
+
+    MAX_TABLE_SITES = 1 << 24
+
+    def __init__(self, height: int, width: int, *, J: float = 1.0, h: float = 0.0, beta: float = 0.44,
+                 name: str | None = None):
+        height, width = int(height), int(width)
+        if height % 2 or width % 2:
+            raise ValueError("the checkerboard colouring of a periodic lattice needs even dimensions")
+        n = height * width
+        blocks = [IndexBlock(n // 2, Family.SPIN, name=f"colour{c}:") for c in range(2)]
+        gspec = TableGibbsSpec(free_blocks=blocks, clamped_blocks=[], sampling_order=[[0], [1]])
+        meta = {"name": name or f"ising2d-{height}x{width}", "n_nodes": n, "n_blocks": 2, "height": height,
+                "width": width, "J": J, "h": h, "beta": beta}
+        super().__init__(gspec, [], meta)
+        self.height, self.width = height, width
+        self.J, self.h, self.beta = float(J), float(h), float(beta)
+        self._specs = None
+
+    @property
+    def n_sites(self) -> int:
+        return self.height * self.width
+
+    def edge_weight(self) -> np.float32:
+        return np.float32(self.beta) * np.float32(self.J)
+
+    def site_bias(self) -> np.float32:
+        return np.float32(self.beta) * np.float32(self.h)
+
+    def tt_stencil(self) -> dict:
+        return {
+            "kind": "ising2d",
+            "dims": (self.height, self.width),
+            "edge_weight": self.edge_weight(),
+            "site_bias": self.site_bias(),
+            "block_rows": (0, self.n_sites // 2),
+        }
+
+    def tt_lower_blocks(self):
+        if self._specs is None:
+            if self.n_sites > self.MAX_TABLE_SITES:
+                raise ValueError(
+                    f"per-edge tables of a {self.height}x{self.width} lattice take "
+                    f"{self.n_sites * 4 * 12 / 2**30:.0f} GiB; the stencil kernel runs it without them"
+                )
+            row_ptr, cols = lattice_2d_csr(self.height, self.width, True)
+            n = self.n_sites
+            colours = ((np.arange(n) // self.width + np.arange(n) % self.width) % 2).astype(np.int64)
+            Jv = np.full(cols.shape[0], self.J, dtype=np.float32)
+            hv = np.full(n, self.h, dtype=np.float32)
+            self._specs = spin_graph_program(row_ptr, cols, Jv, hv, colours, beta=self.beta).specs
+        return list(self._specs)
+
+    @property
+    def specs(self):
+        return self.tt_lower_blocks()
+
+    @specs.setter
+    def specs(self, value):  # TableProgram's constructor assigns an empty list
+        pass
+
+
 def ising_lattice_2d(
     height: int = 64, width: int = 64, *, J: float = 1.0, h: float = 0.0, beta: float = 0.44, periodic: bool = True
-) -> TableProgram:
-    """2-D Ising lattice with two checkerboard blocks, one per sampling group."""
+):
+    """2-D Ising lattice with two checkerboard blocks, one per sampling group.
+
+    Periodic lattices are `IsingLattice2D` programs (tables built on demand,
+    stencil description for the single-chain kernel); open boundaries give a
+    table program."""
+    if periodic:
+        return IsingLattice2D(height, width, J=J, h=h, beta=beta)
     row_ptr, cols = lattice_2d_csr(height, width, periodic)
     n = height * width
     colours = ((np.arange(n) // width + np.arange(n) % width) % 2).astype(np.int64)
