@@ -63,6 +63,57 @@ __host__ __device__ __forceinline__ u32x4 philox4x32_10(u32x4 c, uint32_t k0, ui
   return c;
 }
 
+// Philox4x32-10 with its ten round keys precomputed once per thread: the key
+// schedule of a persistent kernel is loop-invariant, so each call is left
+// with the multiplies and XORs of the rounds.
+struct PhiloxKeys {
+  uint32_t a[10], b[10];
+};
+__host__ __device__ __forceinline__ PhiloxKeys philox_keys(uint32_t k0, uint32_t k1) {
+  PhiloxKeys k;
+#ifdef __CUDA_ARCH__
+#pragma unroll
+#endif
+  for (int r = 0; r < 10; ++r) {
+    k.a[r] = k0 + (uint32_t)r * 0x9E3779B9u;
+    k.b[r] = k1 + (uint32_t)r * 0xBB67AE85u;
+  }
+  return k;
+}
+__host__ __device__ __forceinline__ u32x4 philox4x32_10(u32x4 c, const PhiloxKeys& k) {
+#ifdef __CUDA_ARCH__
+#pragma unroll
+#endif
+  for (int r = 0; r < 10; ++r) {
+#ifdef __CUDA_ARCH__
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+#else
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c.x, p1 = (uint64_t)0xCD9E8D57u * c.z;
+    const uint32_t lo0 = (uint32_t)p0, hi0 = (uint32_t)(p0 >> 32);
+    const uint32_t lo1 = (uint32_t)p1, hi1 = (uint32_t)(p1 >> 32);
+#endif
+    c = u32x4{hi1 ^ c.y ^ k.a[r], lo1, hi0 ^ c.w ^ k.b[r], lo0};
+  }
+  return c;
+}
+
+// n / d for 0 <= n < 2^31 as (umulhi(n, m) + n) >> l with a host-computed
+// magic number (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994).
+struct FastDiv {
+  uint32_t d, m, l;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, l};
+}
+#ifdef __CUDACC__
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return (__umulhi(n, f.m) + n) >> f.l; }
+#endif
+
 __host__ __device__ __forceinline__ uint32_t word_of(const u32x4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }

@@ -36,7 +36,8 @@ __device__ __forceinline__ uint4 ld16(const int8_t* p) { return __ldg(reinterpre
 
 template <bool VARIATES, bool TRACE>
 __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
-    int8_t* __restrict__ cc, const int8_t* __restrict__ co, int64_t half_w, int64_t rows_local, int32_t wrap,
+    int8_t* __restrict__ cc, const int8_t* __restrict__ co, int64_t half_w, FastDiv div_chunks, int64_t rows_local,
+    int32_t wrap,
     int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
     const uint32_t* __restrict__ thresholds, const float* __restrict__ fields, const float* __restrict__ variates,
     int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl,
@@ -55,16 +56,16 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
 
   const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
   const uint64_t sd = ctl ? ctl->seed : seed;
-  const uint32_t k0 = seed_lo(sd), k1 = seed_hi(sd);
-  const int64_t chunks = half_w >> 4;
-  const int64_t items = (row_hi - row_lo) * chunks;
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
+  const uint32_t chunks = div_chunks.d;
+  const uint32_t items = (uint32_t)(row_hi - row_lo) * chunks;  // < 2^31, checked by the host
   const int64_t vs = VARIATES ? (int64_t)(sweep % (uint32_t)(variates_sweeps > 0 ? variates_sweeps : 1)) : 0;
   long long mag = 0, bonds = 0;
 
-  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
-       it += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = row_lo + it / chunks;  // local row
-    const int64_t j0 = (it % chunks) << 4;   // first column
+  for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+    const uint32_t ri = fdiv(it, div_chunks);
+    const int64_t i = row_lo + ri;                   // local row
+    const int64_t j0 = (int64_t)(it - ri * chunks) << 4;  // first column
     int64_t Y = global_row0 + i;
     if (Y >= height) Y -= height;
     if (Y >= height) Y -= height;
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
         }
       } else {
         const int64_t flat = flat0 + 4 * k;
-        const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, (uint32_t)(flat >> 2), sweep, kSaltDenseSpin}, k0, k1);
+        const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, (uint32_t)(flat >> 2), sweep, kSaltDenseSpin}, keys);
 #pragma unroll
         for (int v = 0; v < 4; ++v)
           minus |= ((word_of(r, v) >> 9) < T[(idx4 >> (8 * v)) & 0xFu] ? 0u : 1u) << (8 * v);
@@ -160,7 +161,7 @@ int launch_ising(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_loca
   const int64_t full = (int64_t)sms * per_sm;
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
   k_ising2d<VARIATES, TRACE><<<grid, kIsingThreads, 0, s>>>(
-      cc, co, half_w, rows_local, wrap, row_lo, row_hi, global_row0, height, colour, block_row0, thresholds, fields,
+      cc, co, half_w, make_fastdiv((uint32_t)(half_w >> 4)), rows_local, wrap, row_lo, row_hi, global_row0, height, colour, block_row0, thresholds, fields,
       variates, variates_sweeps, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len);
   return launch_status("k_ising2d launch");
 }
@@ -206,6 +207,10 @@ extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* othe
   if (((uintptr_t)colour_state % 16) || ((uintptr_t)other_state % 16) || (variates && (uintptr_t)variates % 16)) {
     set_error("tthrml_ising2d_halfsweep: buffers must be 16-byte aligned");
     return TTHRML_ERR_ARG;
+  }
+  if ((row_hi - row_lo) * (width / 32) >= (1ll << 31)) {
+    set_error("tthrml_ising2d_halfsweep: more than 2^31 16-site chunks in one launch");
+    return TTHRML_ERR_UNSUPPORTED;
   }
   if (row_hi == row_lo) return TTHRML_OK;
   cudaStream_t s = (cudaStream_t)stream;

@@ -31,19 +31,6 @@ constexpr int kPottsThreads = 256;
 constexpr int kPottsQ = 8;  // categories handled by this kernel
 constexpr int kRows = kPottsQ + 1;  // matrix rows per neighbour category, the last one all zero
 
-// n / d for 0 <= n < 2^31 as (umulhi(n, m) + n) >> l (Granlund and Montgomery,
-// "Division by invariant integers using multiplication", PLDI 1994).
-struct FastDiv {
-  uint32_t d, m, l;
-};
-FastDiv make_fastdiv(uint32_t d) {
-  uint32_t l = 0;
-  while ((1ull << l) < d) ++l;
-  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
-  return FastDiv{d, (uint32_t)m, l};
-}
-__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return (__umulhi(n, f.m) + n) >> f.l; }
-
 template <bool VARIATES>
 __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
@@ -64,7 +51,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
 
   const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
   const uint64_t sd = ctl ? ctl->seed : seed;
-  const uint32_t k0 = seed_lo(sd), k1 = seed_hi(sd);
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
   const uint32_t words = div_words.d;
   const int64_t half = (int64_t)X * Y * Z / 2;
   const uint32_t items = (uint32_t)(half * words);  // < 2^31, checked by the host
@@ -103,7 +90,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     uint32_t out = 0u;
     u32x4 rr{0u, 0u, 0u, 0u};
     if (!VARIATES)
-      rr = philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w), (uint32_t)row, sweep, kSaltCat}, k0, k1);
+      rr = philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w), (uint32_t)row, sweep, kSaltCat}, keys);
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       float theta[kPottsQ];

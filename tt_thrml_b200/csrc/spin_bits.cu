@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(kBitsThreads, TTHRML_BITS_MIN_BLOCKS) k_spin_b
   int64_t item = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
   const uint64_t sd = ctl ? ctl->seed : seed;
-  const uint32_t k0 = seed_lo(sd), k1 = seed_hi(sd);
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
   const unsigned char* state_bytes = reinterpret_cast<const unsigned char*>(state);
   auto row_of = [&](int64_t it) -> int64_t { return slices == 1 ? it : (int64_t)((uint64_t)it / (uint64_t)slices); };
 
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kBitsThreads, TTHRML_BITS_MIN_BLOCKS) k_spin_b
       const int64_t g0 = chain_offset + c0;
 #pragma unroll
       for (int v = 0; v < 8; v += 4) {
-        const u32x4 rr = philox4x32_10(u32x4{(uint32_t)((g0 + v) >> 2), (uint32_t)row, sweep, kSaltSpin}, k0, k1);
+        const u32x4 rr = philox4x32_10(u32x4{(uint32_t)((g0 + v) >> 2), (uint32_t)row, sweep, kSaltSpin}, keys);
         bits[v] = rr.x;
         bits[v + 1] = rr.y;
         bits[v + 2] = rr.z;
