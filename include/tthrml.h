@@ -25,7 +25,9 @@
  *     captured CUDA graph of n sweeps serves every position of every run.
  *   - RNG: with `variates == NULL` the kernels draw from an on-device
  *     counter-based Philox4x32-10 stream keyed by `seed`, counter
- *     (chain/4, row, sweep, salt).  With `variates != NULL` they consume
+ *     (chain/4, row, sweep, salt) -- or (chain, row/4, sweep, salt) for the
+ *     dense and 2-D lattice kernels, as documented at each entry point.
+ *     With `variates != NULL` they consume
  *     caller-provided variates exactly like the reference's uploaded RNG
  *     slices (tt_thrml/rng.py:132-222): spin threshold logits, categorical
  *     Gumbel noise, gaussian standard normals.
@@ -317,6 +319,20 @@ int tthrml_encode_rows(const void* in_dev, int32_t in_dtype, int32_t as_spin, in
  */
 int tthrml_sum_rows(const void* state_dev, int32_t state_dtype, int64_t n_chains,
                     int64_t row_start, int64_t n_rows, double* out_dev, void* stream);
+
+/*
+ * Device-side moment accumulation (the reference's MomentAccumulatorObserver
+ * with the state left on the device, tt_thrml/executor.py:389-409): for each
+ * moment m, acc[m][chain] += product over k < order of value(rows[m][k],
+ * chain), stopping at the first row < 0.  value: spins +-1, or 1 / 0 when
+ * spin_as_bool is set (the reference's boolean spin state, spin rows flagged
+ * in spin_rows[m][k]; every row of a bit-packed state is a spin); other rows
+ * as stored.  rows / spin_rows: device [n_moments][order]; acc: device
+ * float64 [n_moments][n_chains].  n_moments <= 65535.
+ */
+int tthrml_moments_accumulate(const void* state_dev, int32_t state_dtype, int64_t n_chains,
+                              const int64_t* rows_dev, const uint8_t* spin_rows_dev, int32_t order,
+                              int64_t n_moments, int32_t spin_as_bool, double* acc_dev, void* stream);
 
 /* Host-only: greedy graph colouring in node order (smallest free colour).
  * Returns the number of colours in *n_colours.  No device work. */

@@ -131,3 +131,29 @@ def test_strip_arguments_are_checked():
     st.prepare_rng(0, 4)
     with pytest.raises(ValueError):
         st.run_sweeps(3)  # not a multiple of halo/2
+
+
+def test_strip_checkpoint_continues_bit_for_bit():
+    prog = workloads.IsingLattice2D(16, 32, beta=0.4407)
+
+    def fresh():
+        st = LatticeStrips(prog, device="cpu", halo=2, halfsweep=lambda *a: None)
+        st._halfsweep = ising_ref.make_halfsweep(st)
+        return st
+
+    a = fresh()
+    a.load_random(2)
+    a.prepare_rng(5, 10)
+    a.run_sweeps(10)
+    b = fresh()
+    b.load_random(2)
+    b.prepare_rng(5, 10)
+    b.run_sweeps(4)
+    ck = b.checkpoint()
+    c = fresh()
+    c.restore(ck)
+    c.run_sweeps(6)
+    np.testing.assert_array_equal(c.gather_lattice(), a.gather_lattice())
+    np.testing.assert_array_equal(c.trace(), a.trace())
+    with pytest.raises(ValueError):
+        LatticeStrips(prog, device="cpu", halo=4, halfsweep=lambda *a: None).restore(ck)

@@ -103,6 +103,7 @@ _SIGNATURES = {
         [c_vp, c_vp, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,
          c_u64, c_u32, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp],
     ),
+    "tthrml_moments_accumulate": (c_i32, [c_vp, c_i32, c_i64, c_vp, c_vp, c_i32, c_i64, c_i32, c_vp, c_vp]),
     "tthrml_ctl_advance": (c_i32, [c_vp, c_u32, c_vp]),
     "tthrml_decode_rows": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp]),
     "tthrml_encode_rows": (c_i32, [c_vp, c_i32, c_i32, c_i64, c_i32, c_i64, c_i64, c_vp, c_vp]),

@@ -276,6 +276,80 @@ extern "C" int tthrml_sum_rows(const void* state, int32_t dtype, int64_t C, int6
   return launch_status("k_sum_rows launch");
 }
 
+namespace tthrml {
+namespace {
+
+// Value of (row, chain) for the moment products: spins as +-1 (spin_as_bool:
+// 1 for +1, 0 for -1, the reference's boolean spin state), other states as
+// stored (categorical index, gaussian value).
+template <typename T>
+__device__ __forceinline__ double moment_value(const T* state, int64_t C, int64_t row, int64_t chain, bool spin_row,
+                                               int32_t spin_as_bool) {
+  const double v = (double)state[row * C + chain];
+  return spin_row && spin_as_bool ? (v > 0 ? 1.0 : 0.0) : v;
+}
+__device__ __forceinline__ double moment_value_bits(const uint32_t* state, int64_t W, int64_t row, int64_t chain,
+                                                    int32_t spin_as_bool) {
+  const bool minus = (state[row * W + (chain >> 5)] >> (chain & 31)) & 1u;
+  return spin_as_bool ? (minus ? 0.0 : 1.0) : (minus ? -1.0 : 1.0);
+}
+
+// acc[m][chain] += prod_k value(rows[m][k], chain) over the k < order with rows >= 0.
+template <typename T, bool BITS>
+__global__ void k_moments(const T* state, int64_t C, const int64_t* __restrict__ rows, const uint8_t* __restrict__ spin,
+                          int32_t order, int64_t n_moments, int32_t spin_as_bool, double* acc) {
+  const int64_t m = blockIdx.y;
+  for (int64_t chain = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; chain < C; chain += (int64_t)gridDim.x * blockDim.x) {
+    double p = 1.0;
+    for (int k = 0; k < order; ++k) {
+      const int64_t r = rows[m * order + k];
+      if (r < 0) break;
+      if (BITS)
+        p *= moment_value_bits(reinterpret_cast<const uint32_t*>(state), C / 32, r, chain, spin_as_bool);
+      else
+        p *= moment_value(state, C, r, chain, spin[m * order + k] != 0, spin_as_bool);
+    }
+    acc[m * C + chain] += p;
+  }
+}
+
+}  // namespace
+}  // namespace tthrml
+
+extern "C" int tthrml_moments_accumulate(const void* state, int32_t dtype, int64_t C, const int64_t* rows,
+                                         const uint8_t* spin_rows, int32_t order, int64_t n_moments,
+                                         int32_t spin_as_bool, double* acc, void* stream) {
+  using namespace tthrml;
+  if (n_moments == 0 || C == 0) return TTHRML_OK;
+  if (!state || !rows || !acc || order < 1 || n_moments < 0 || C < 0 || n_moments > 65535 ||
+      (dtype != TTHRML_STATE_BITS && !spin_rows)) {
+    set_error("tthrml_moments_accumulate: invalid arguments");
+    return TTHRML_ERR_ARG;
+  }
+  const int threads = 128;
+  const int64_t bx = (C + threads - 1) / threads;
+  dim3 grid((unsigned)(bx < 1024 ? bx : 1024), (unsigned)n_moments);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == TTHRML_STATE_BITS) {
+    if (C % 32) {
+      set_error("tthrml_moments_accumulate: bit-packed state needs n_chains %% 32 == 0");
+      return TTHRML_ERR_ARG;
+    }
+    k_moments<uint32_t, true><<<grid, threads, 0, s>>>((const uint32_t*)state, C, rows, spin_rows, order, n_moments,
+                                                       spin_as_bool, acc);
+  } else if (dtype == TTHRML_STATE_I8) {
+    k_moments<int8_t, false><<<grid, threads, 0, s>>>((const int8_t*)state, C, rows, spin_rows, order, n_moments,
+                                                      spin_as_bool, acc);
+  } else if (dtype == TTHRML_STATE_F32) {
+    k_moments<float, false><<<grid, threads, 0, s>>>((const float*)state, C, rows, spin_rows, order, n_moments,
+                                                     spin_as_bool, acc);
+  } else {
+    set_error("tthrml_moments_accumulate: unknown dtype %d", dtype);
+    return TTHRML_ERR_ARG;
+  }
+  return launch_status("k_moments launch");
+}
+
 extern "C" int tthrml_greedy_colouring(int64_t n, const int64_t* row_ptr, const int32_t* cols, int32_t* colour,
                                        int32_t* n_colours) {
   if (n < 0 || (n > 0 && (!row_ptr || !cols || !colour)) || !n_colours) {

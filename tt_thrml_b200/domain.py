@@ -319,6 +319,43 @@ class LatticeStrips:
     def synchronize(self) -> None:
         self._sync()
 
+    # ------------------------------------------------------------ checkpoint
+    def checkpoint(self) -> dict:
+        """This rank's strip (both colours, halos included), sweep, seed and trace: enough to continue
+        bit for bit.  Taken between run_sweeps calls, i.e. right after a halo exchange."""
+        self._sync()
+        return {
+            "format": "tt_thrml_b200.strips/1",
+            "dims": (self.H, self.W),
+            "strips": self.world,
+            "rank": self.rank,
+            "halo": self.D,
+            "colours": [c.cpu().numpy() for c in self.colours],
+            "sweep": int(self.sweep),
+            "seed": int(self.seed),
+            "trace": None if self._trace is None else self._trace.cpu().numpy(),
+        }
+
+    def restore(self, ckpt: dict) -> None:
+        torch = _torch()
+        want = ("tt_thrml_b200.strips/1", (self.H, self.W), self.world, self.rank, self.D)
+        got = (ckpt.get("format"), tuple(ckpt["dims"]), ckpt["strips"], ckpt["rank"], ckpt["halo"])
+        if want != got:
+            raise ValueError(f"checkpoint {got} does not match this decomposition {want}")
+        for dst, src in zip(self.colours, ckpt["colours"]):
+            dst.copy_(torch.from_numpy(np.ascontiguousarray(src)))
+        self.seed = int(ckpt["seed"])
+        if ckpt["trace"] is not None:
+            t = torch.from_numpy(np.ascontiguousarray(ckpt["trace"])).to(self.device)
+            if self._trace is None or self._trace.shape != t.shape:
+                self._trace = t
+                self._graphs.clear()
+            else:
+                self._trace.copy_(t)
+        self.sweep = int(ckpt["sweep"])
+        self._ctl_value = None
+        self._after_load()
+
     # ------------------------------------------------------------ observables
     def trace(self) -> np.ndarray:
         """int64 [sweeps run][2]: (magnetisation, bond sum) of the whole lattice after each sweep."""

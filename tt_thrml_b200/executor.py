@@ -507,6 +507,82 @@ class Executor:
 
     # ------------------------------------------------------------- read-back
 
+    # ------------------------------------------------------------ checkpoint
+
+    CHECKPOINT_FORMAT = "tt_thrml_b200.checkpoint/1"
+
+    def _device_buffers(self) -> list:
+        if self._dense:
+            return list(self._block_states) + [b for b in self._block_f32 if b is not None]
+        return [self._global_state]
+
+    def checkpoint(self) -> dict:
+        """What a later run needs to continue these chains bit for bit: the raw device state (in its own
+        layout), the sweep counter and the Philox seed.  Parity-mode variates are not stored: restore()
+        rebuilds them from the same key."""
+        torch = _torch()
+        if not self._state_loaded:
+            raise RuntimeError("State must be loaded before a checkpoint")
+        self._stream.synchronize()
+        rng = self._rng_buffers
+        return {
+            "format": self.CHECKPOINT_FORMAT,
+            "state_dtype": self.compiled.state_dtype,
+            "n_chains": self.n_chains,
+            "chain_offset": self.chain_offset,
+            "total_nodes": self.compiled.total_nodes,
+            "buffers": [(b.view(torch.int16) if b.dtype == torch.bfloat16 else b).cpu().numpy()
+                        for b in self._device_buffers()],
+            "sweep": int(self._sweep_counter),
+            "seed": None if rng is None or rng.seed is None else int(rng.seed),
+            "rng_sweeps": int(self._rng_n_sweeps),
+            "rng_mode": self.config.rng_mode,
+        }
+
+    def restore(self, ckpt: dict, key=None) -> None:
+        """Continues from checkpoint(): state, sweep counter and RNG position (parity mode: pass the key)."""
+        torch = _torch()
+        if ckpt.get("format") != self.CHECKPOINT_FORMAT:
+            raise ValueError(f"not a {self.CHECKPOINT_FORMAT} checkpoint")
+        mine = (self.compiled.state_dtype, self.n_chains, self.chain_offset, self.compiled.total_nodes)
+        theirs = (ckpt["state_dtype"], int(ckpt["n_chains"]), int(ckpt["chain_offset"]), int(ckpt["total_nodes"]))
+        if mine != theirs:
+            raise ValueError(f"checkpoint of a different executor: {theirs} (state layout, chains, chain offset, "
+                             f"nodes), this one is {mine}")
+        self._ensure_state()
+        bufs = self._device_buffers()
+        if len(bufs) != len(ckpt["buffers"]):
+            raise ValueError("checkpoint buffers do not match this program")
+        for dst, src in zip(bufs, ckpt["buffers"]):
+            src = np.asarray(src)
+            if tuple(src.shape) != tuple(dst.shape):
+                raise ValueError(f"checkpoint buffer of shape {src.shape}, expected {tuple(dst.shape)}")
+            dst.copy_(torch.from_numpy(np.ascontiguousarray(src)).view(dst.dtype).reshape(dst.shape))
+        torch.cuda.synchronize(self._tdev)
+        self._state_loaded = True
+        if ckpt["seed"] is not None:
+            n = int(ckpt["rng_sweeps"])
+            self._install_rng(BulkRNGBuffers(None, None, None, seed=int(ckpt["seed"]), n_sweeps=n), n)
+        else:
+            if key is None:
+                raise ValueError("a parity-mode checkpoint needs the RNG key to rebuild its variates")
+            self.prepare_rng(key)
+        self._sweep_counter = int(ckpt["sweep"])
+
+    def save_checkpoint(self, path) -> None:
+        ck = self.checkpoint()
+        meta = {k: v for k, v in ck.items() if k != "buffers"}
+        arrays = {f"buffer{i}": b for i, b in enumerate(ck["buffers"])}
+        np.savez(path, meta=np.array(repr(meta)), **arrays)
+
+    def load_checkpoint(self, path, key=None) -> None:
+        import ast
+
+        with np.load(path, allow_pickle=False) as f:
+            meta = ast.literal_eval(str(f["meta"]))
+            meta["buffers"] = [f[f"buffer{i}"] for i in range(sum(1 for k in f.files if k.startswith("buffer")))]
+        self.restore(meta, key=key)
+
     def check_device_errors(self) -> None:
         """Raises if a kernel recorded an expired in-kernel wait (dense programs)."""
         if self._error_word is not None:
@@ -682,6 +758,20 @@ class Executor:
             host = out.cpu()
         return host.numpy()
 
+    def accumulate_moments(self, rows, spin_rows, order: int, acc, spin_as_bool: bool = True) -> None:
+        """acc[m][chain] += product of the values at rows[m][:order] (device tensors; DeviceMomentObserver)."""
+        if self._dense:
+            raise NotImplementedError("device-side moments need a row-major state (not a dense program)")
+        nat.bind_device(self._tdev.index)
+        nat.check(
+            self._lib.tthrml_moments_accumulate(
+                self._global_state.data_ptr(), self._state_code, self.n_chains, rows.data_ptr(), spin_rows.data_ptr(),
+                int(order), int(rows.shape[0]), 1 if spin_as_bool else 0, acc.data_ptr(),
+                nat.stream_handle(self._stream),
+            ),
+            "tthrml_moments_accumulate",
+        )
+
     # --------------------------------------------------------------- schedule
 
     def sample_states(self, key, schedule, nodes_to_sample: Sequence, *, init_state_free, state_clamp=()):
@@ -727,6 +817,10 @@ class Executor:
             all_obs.append(obs)
         if device_side:  # observations are device tensors: one read-back for the whole run
             all_obs = _device_obs_to_host(all_obs, self._stream)
+            finalize = getattr(f_observe, "finalize", None)
+            if callable(finalize):
+                self._stream.synchronize()
+                carry = finalize(carry)
         if schedule.n_samples <= 1:
             return carry, tree_expand(all_obs[0])
         if all(o is None for o in all_obs):

@@ -12,8 +12,9 @@ here give the same two observers without thrml/JAX (NumPy arrays in and out):
   products of node values over the samples (thrml.observers.
   MomentAccumulatorObserver; used by the reference's parity scenarios).
 
-A device-side observer, `MagnetizationObserver`, sums spin blocks per chain on
-the GPU so no state crosses to the host per sample.
+Device-side observers never copy the state to the host per sample:
+`MagnetizationObserver` sums spin blocks per chain, `DeviceMomentObserver`
+accumulates MomentAccumulatorObserver's products on the GPU.
 """
 
 from __future__ import annotations
@@ -104,6 +105,66 @@ class MomentAccumulatorObserver:
                 contrib.append(prod)
             new.append(np.asarray(acc) + np.stack(contrib, axis=-1).astype(np.float32))
         return new, None
+
+
+class DeviceMomentObserver:
+    """MomentAccumulatorObserver with the products accumulated on the GPU.
+
+    Same moment_spec (groups of node tuples) and the same final carry -- one
+    float32 array per group, [n_chains, len(group)] ([len(group)] with one
+    chain) -- but each sample is one launch of tthrml_moments_accumulate on
+    the device state instead of a full state read-back (the reference reads
+    the whole state back per sample, tt_thrml/executor.py:294-295, 389-409).
+    spin_as_bool: spins enter the products as 1 / 0 (the reference's boolean
+    spin state, what the default transform of MomentAccumulatorObserver
+    multiplies) or, when False, as +-1.
+    """
+
+    device_side = True
+
+    def __init__(self, moment_spec, spin_as_bool: bool = True):
+        self.moment_spec = [list(group) for group in moment_spec]
+        self.spin_as_bool = bool(spin_as_bool)
+
+    def init(self):
+        return None
+
+    def _tables(self, executor):
+        import torch
+
+        program = executor.program
+        pos = _node_positions(program)
+        specs = [cb.spec for cb in executor.compiled.blocks]
+        tuples = [nodes for group in self.moment_spec for nodes in group]
+        order = max((len(t) for t in tuples), default=1)
+        rows = np.full((len(tuples), order), -1, dtype=np.int64)
+        spin = np.zeros((len(tuples), order), dtype=np.uint8)
+        for m, nodes in enumerate(tuples):
+            for k, node in enumerate(nodes):
+                bi, j = pos[node]
+                rows[m, k] = specs[bi].block_global_start + j
+                spin[m, k] = 1 if getattr(specs[bi].family, "value", specs[bi].family) == "spin" else 0
+        dev = executor.compiled.device
+        acc = torch.zeros((len(tuples), executor.n_chains), dtype=torch.float64, device=dev)
+        return {"rows": torch.from_numpy(rows).to(dev), "spin": torch.from_numpy(spin).to(dev), "order": order,
+                "acc": acc}
+
+    def observe_device(self, executor, carry, sample_index):
+        if carry is None:
+            carry = self._tables(executor)
+        executor.accumulate_moments(carry["rows"], carry["spin"], carry["order"], carry["acc"], self.spin_as_bool)
+        return carry, None
+
+    def finalize(self, carry, stream=None):
+        if carry is None:
+            return [np.zeros(len(group), dtype=np.float32) for group in self.moment_spec]
+        acc = carry["acc"].cpu().numpy()  # [n_moments][C]
+        out, m = [], 0
+        for group in self.moment_spec:
+            part = acc[m : m + len(group)].T.astype(np.float32)  # [C][len(group)]
+            out.append(part[0] if part.shape[0] == 1 else part)
+            m += len(group)
+        return out
 
 
 class MagnetizationObserver:
