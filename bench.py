@@ -378,6 +378,7 @@ def run_ising(args, W):
             e1.record(stream)
         barrier()
     del flush
+    st.check_errors()
     dt_ms = sum(e0.elapsed_time(e1) for e0, e1 in events)
     if dist is not None:
         t = torch.tensor([dt_ms], device=dev)
@@ -387,7 +388,7 @@ def run_ising(args, W):
     updates = n_sites * S * args.steps
     value = updates / (dt_ms / 1000.0)
     periods = S // (W.halo // 2)
-    gpu_launches = args.steps * periods * (W.halo + 1)  # half-sweeps + run-control advance per period
+    gpu_launches = args.steps * (periods * (W.halo + 2) + 1)  # import + half-sweeps + signal per period, ctl advance
     em = st.energy_magnetisation()
 
     # roofline: one eager half-sweep of the own rows, CUDA events on the launch stream
@@ -459,7 +460,8 @@ def run_ising(args, W):
                 "sweeps_per_step": S,
                 "strips": world,
                 "halo_rows": W.halo,
-                "exchange": "NCCL send/recv of halo rows every halo/2 sweeps" if world > 1 else "local halo copies",
+                "exchange": "boundary rows stored into the neighbours' mailboxes by the half-sweep kernel (peer "
+                            "memory over NVLink), flag per period, every halo/2 sweeps",
                 "rng": "philox4x32-10 on device",
                 "l2": "state 1 GiB exceeds L2; flushed before every timed step (256 MiB write)",
                 "parallelism": f"row strips x{world}",

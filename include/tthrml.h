@@ -249,6 +249,69 @@ int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, in
                              void* stream);
 
 /*
+ * Halo export of a strip-decomposed lattice (tthrml_ising2d_halfsweep_x):
+ * while a half-sweep computes local rows [up_row0, up_row0 + rows) it also
+ * stores them at `up` (the up neighbour's mailbox, peer memory), rows
+ * [down_row0, down_row0 + rows) at `down`, in parity slot
+ * ((sweep / sweeps_per_period) + 1) % 2 (slot_bytes apart).  rows = 0: none.
+ */
+typedef struct tthrml_halo_export {
+  int8_t* up;
+  int8_t* down;
+  int64_t up_row0;
+  int64_t down_row0;
+  int64_t rows;
+  int64_t slot_bytes;
+  uint32_t sweeps_per_period;
+  uint32_t reserved;
+} tthrml_halo_export;
+
+/* tthrml_ising2d_halfsweep with the fused halo export (export_host may be NULL). */
+int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* other_state, int64_t width, int64_t rows_local,
+                               int32_t wrap_rows, int64_t row_lo, int64_t row_hi, int64_t global_row0,
+                               int64_t height, int32_t colour, int64_t block_row0, const uint32_t* thresholds_dev,
+                               const float* fields_dev, const float* variates_dev, int64_t variates_sweeps,
+                               int64_t chain, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl_dev,
+                               int64_t count_lo, int64_t count_hi, int64_t* trace_dev, int64_t trace_len,
+                               const tthrml_halo_export* export_host, void* stream);
+
+/*
+ * Peer memory for the halo mailboxes: tthrml_ipc_malloc allocates zeroed
+ * device memory and writes its 64-byte CUDA IPC handle to `handle_host`;
+ * another process opens it with tthrml_ipc_open (peer access enabled on
+ * demand) and releases it with tthrml_ipc_close; tthrml_free frees the
+ * owner's allocation.
+ */
+int tthrml_ipc_malloc(int64_t bytes, void** ptr_out, void* handle_host);
+int tthrml_ipc_open(const void* handle_host, void** ptr_out);
+int tthrml_ipc_close(void* ptr);
+int tthrml_free(void* ptr);
+/* cudaMemcpyAsync with the kind inferred from the addresses (host, device or
+ * a peer's IPC mapping), ordered on `stream`. */
+int tthrml_memcpy(void* dst, const void* src, int64_t bytes, void* stream);
+
+/*
+ * End of an exchange period: publishes the period number p =
+ * (sweep + ctl->sweep) / sweeps_per_period + 1 in the two neighbours' flags
+ * (system-scope release after a system fence).
+ */
+int tthrml_halo_signal(uint32_t* up_flag_dev, uint32_t* down_flag_dev, uint32_t sweeps_per_period, uint32_t sweep,
+                       const tthrml_run_ctl* ctl_dev, void* stream);
+
+/*
+ * Start of exchange period p (computed as above; p = 1 imports nothing):
+ * waits until both own flags (from up, from down) reach p - 1 -- a bounded
+ * wait of about one second; on expiry *error_dev is set to 1 and nothing is
+ * copied -- then copies the mailbox slot (p - 1) % 2 ([2 directions][2
+ * colours][rows][width/2]) into local rows [top_row0, +rows) (from up) and
+ * [bottom_row0, +rows) (from down) of both colours.
+ */
+int tthrml_halo_import(int8_t* colour0_dev, int8_t* colour1_dev, int64_t width, int64_t rows, int64_t top_row0,
+                       int64_t bottom_row0, const int8_t* mailbox_dev, const uint32_t* flags_dev,
+                       uint32_t sweeps_per_period, uint32_t sweep, const tthrml_run_ctl* ctl_dev, int32_t* error_dev,
+                       void* stream);
+
+/*
  * Dense bipartite block update on the tensor cores (tcgen05, bf16 operands,
  * fp32 accumulation in TMEM).  Replaces the group kernel of a block whose
  * interaction with another block is a dense weight matrix (the RBM case:

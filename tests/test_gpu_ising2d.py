@@ -2,10 +2,11 @@
 
 The kernel is checked against the oracle on the lattice's per-edge tables
 (spins bit-exact outside the 1e-5 band, counters in the row4 layout); the
-strip decomposition (LatticeStrips) against the executor's whole-lattice run,
-and its energy/magnetisation trace against the lattice it leaves.  With two
-or more GPUs visible, a 2-rank NCCL run must reproduce the 1-GPU run bit for
-bit.
+strip decomposition (LatticeStrips, peer-memory and NCCL exchanges) against
+the executor's whole-lattice run, and its energy/magnetisation trace against
+the lattice it leaves.  With two or more GPUs visible, a 2-rank run must
+reproduce the 1-GPU run bit for bit, and resume from a mid-run checkpoint.
+The halo import's wait is bounded: a flag nobody sets ends it with an error.
 """
 
 from __future__ import annotations
@@ -51,15 +52,18 @@ def _split(lattice, c):
     return np.take_along_axis(lattice, cols, axis=1)
 
 
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
 @pytest.mark.parametrize("graphs", [False, True])
-def test_strips_reproduce_the_executor(cuda_device, graphs):
+def test_strips_reproduce_the_executor(cuda_device, graphs, exchange):
     H, W, n = 128, 256, 12
     prog = workloads.IsingLattice2D(H, W, beta=0.4407)
-    st = LatticeStrips(prog, device=cuda_device, halo=4, cuda_graphs=graphs)
+    st = LatticeStrips(prog, device=cuda_device, halo=4, cuda_graphs=graphs, exchange=exchange)
     st.load_random(9)
     lat0 = st.gather_lattice()
     st.prepare_rng(33, n)
-    st.run_sweeps(n)
+    st.run_sweeps(n // 2)
+    st.run_sweeps(n // 2)
+    st.check_errors()
     lat = st.gather_lattice()
 
     ex = Executor(None, 0, prog, make_cuda_config(n_chains=1, cuda_graphs=graphs), n_sweeps=n, n_chains=1)
@@ -93,7 +97,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, H, W, halo, n, out):
+def _nccl_worker(rank, world, port, H, W, halo, n, out, exchange):
     import datetime
 
     import torch
@@ -107,12 +111,21 @@ def _nccl_worker(rank, world, port, H, W, halo, n, out):
                             device_id=torch.device("cuda", rank))
     try:
         prog = workloads.IsingLattice2D(H, W, beta=0.4407)
-        st = LatticeStrips(prog, device=torch.device("cuda", rank), halo=halo)
+        st = LatticeStrips(prog, device=torch.device("cuda", rank), halo=halo, exchange=exchange)
         st.load_random(9)
         st.prepare_rng(33, n)
-        st.run_sweeps(n)
+        st.run_sweeps(n // 2)
+        ck = st.checkpoint()
+        st.run_sweeps(n // 2)
+        st.check_errors()
         lat = st.gather_lattice()
         tr = st.trace()
+        # resume from the mid-run checkpoint: the same lattice again
+        st.restore(ck)
+        st.run_sweeps(n // 2)
+        st.check_errors()
+        assert np.array_equal(st.gather_lattice(), lat)
+        st.close()
         if rank == 0:
             np.savez(out, lattice=lat, trace=tr)
         dist.barrier()
@@ -120,7 +133,8 @@ def _nccl_worker(rank, world, port, H, W, halo, n, out):
         dist.destroy_process_group()
 
 
-def test_two_gpu_strips_reproduce_one_gpu(cuda_device, tmp_path):
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_two_gpu_strips_reproduce_one_gpu(cuda_device, tmp_path, exchange):
     import torch
 
     if torch.cuda.device_count() < 2:
@@ -135,8 +149,64 @@ def test_two_gpu_strips_reproduce_one_gpu(cuda_device, tmp_path):
     st.run_sweeps(n)
     lat1, tr1 = st.gather_lattice(), st.trace()
     out = tmp_path / "nccl.npz"
-    mp.start_processes(_nccl_worker, args=(2, _free_port(), H, W, halo, n, str(out)), nprocs=2, join=True,
-                       start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(2, _free_port(), H, W, halo, n, str(out), exchange), nprocs=2,
+                       join=True, start_method="spawn")
     res = np.load(out)
     np.testing.assert_array_equal(res["lattice"], lat1)
     np.testing.assert_array_equal(res["trace"], tr1)
+
+
+def test_strip_checkpoint_continues_on_one_gpu(cuda_device):
+    prog = workloads.IsingLattice2D(64, 128, beta=0.4407)
+    a = LatticeStrips(prog, device=cuda_device, halo=4)
+    a.load_random(1)
+    a.prepare_rng(2, 12)
+    a.run_sweeps(12)
+    b = LatticeStrips(prog, device=cuda_device, halo=4)
+    b.load_random(1)
+    b.prepare_rng(2, 12)
+    b.run_sweeps(6)
+    ck = b.checkpoint()
+    c = LatticeStrips(prog, device=cuda_device, halo=4)
+    c.restore(ck)
+    c.run_sweeps(6)
+    c.check_errors()
+    np.testing.assert_array_equal(c.gather_lattice(), a.gather_lattice())
+    np.testing.assert_array_equal(c.trace(), a.trace())
+
+
+def test_halo_import_wait_is_bounded(cuda_device):
+    """A neighbour that never publishes its period: the import gives up after its wait budget, reports
+    the error and leaves the halo rows untouched; the context stays usable."""
+    import time
+
+    import torch
+
+    from tt_thrml_b200 import _native as nat
+
+    W, D, rows = 64, 2, 8
+    hw = W // 2
+    c0 = torch.ones((rows, hw), dtype=torch.int8, device=cuda_device)
+    c1 = torch.ones((rows, hw), dtype=torch.int8, device=cuda_device)
+    mailbox = torch.full((8 * D * hw,), -1, dtype=torch.int8, device=cuda_device)
+    flags = torch.zeros(2, dtype=torch.int32, device=cuda_device)  # nobody sets them
+    err = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    nat.bind_device(0)
+    t0 = time.perf_counter()
+    rc = nat.lib().tthrml_halo_import(c0.data_ptr(), c1.data_ptr(), W, D, 0, rows - D, mailbox.data_ptr(),
+                                      flags.data_ptr(), 1, 1, None, err.data_ptr(),
+                                      torch.cuda.current_stream().cuda_stream)  # sweep 1, 1 sweep/period: p = 2
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 30.0
+    assert int(err.item()) == 1
+    assert bool((c0 == 1).all()) and bool((c1 == 1).all())
+    # the same call with the flag published imports the mailbox
+    flags.fill_(1)
+    err.zero_()
+    rc = nat.lib().tthrml_halo_import(c0.data_ptr(), c1.data_ptr(), W, D, 0, rows - D, mailbox.data_ptr(),
+                                      flags.data_ptr(), 1, 1, None, err.data_ptr(),
+                                      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0 and int(err.item()) == 0
+    assert bool((c0[:D] == -1).all()) and bool((c0[rows - D :] == -1).all()) and bool((c0[D : rows - D] == 1).all())

@@ -57,6 +57,21 @@ class BlockDesc(ctypes.Structure):
     ]
 
 
+class HaloExport(ctypes.Structure):
+    """tthrml_halo_export (include/tthrml.h)."""
+
+    _fields_ = [
+        ("up", ctypes.c_void_p),
+        ("down", ctypes.c_void_p),
+        ("up_row0", ctypes.c_int64),
+        ("down_row0", ctypes.c_int64),
+        ("rows", ctypes.c_int64),
+        ("slot_bytes", ctypes.c_int64),
+        ("sweeps_per_period", ctypes.c_uint32),
+        ("reserved", ctypes.c_uint32),
+    ]
+
+
 class GroupDesc(ctypes.Structure):
     _fields_ = [
         ("blocks", c_vp),
@@ -104,6 +119,18 @@ _SIGNATURES = {
          c_u64, c_u32, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp],
     ),
     "tthrml_moments_accumulate": (c_i32, [c_vp, c_i32, c_i64, c_vp, c_vp, c_i32, c_i64, c_i32, c_vp, c_vp]),
+    "tthrml_ising2d_halfsweep_x": (
+        c_i32,
+        [c_vp, c_vp, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,
+         c_u64, c_u32, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
+    ),
+    "tthrml_ipc_malloc": (c_i32, [c_i64, c_vp, c_vp]),
+    "tthrml_ipc_open": (c_i32, [c_vp, c_vp]),
+    "tthrml_ipc_close": (c_i32, [c_vp]),
+    "tthrml_free": (c_i32, [c_vp]),
+    "tthrml_memcpy": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
+    "tthrml_halo_signal": (c_i32, [c_vp, c_vp, c_u32, c_u32, c_vp, c_vp]),
+    "tthrml_halo_import": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_u32, c_u32, c_vp, c_vp, c_vp]),
     "tthrml_ctl_advance": (c_i32, [c_vp, c_u32, c_vp]),
     "tthrml_decode_rows": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp]),
     "tthrml_encode_rows": (c_i32, [c_vp, c_i32, c_i32, c_i64, c_i32, c_i64, c_i64, c_vp, c_vp]),

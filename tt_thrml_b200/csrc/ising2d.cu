@@ -41,7 +41,8 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
     int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
     const uint32_t* __restrict__ thresholds, const float* __restrict__ fields, const float* __restrict__ variates,
     int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl,
-    int64_t count_lo, int64_t count_hi, unsigned long long* __restrict__ trace, int64_t trace_len) {
+    int64_t count_lo, int64_t count_hi, unsigned long long* __restrict__ trace, int64_t trace_len,
+    tthrml_halo_export ex) {
   __shared__ uint32_t T[16];
   __shared__ float F[16];
   __shared__ long long red[2];
@@ -119,7 +120,21 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
         }
       }
     }
-    *reinterpret_cast<uint4*>(cc + i * half_w + j0) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+    const uint4 outv = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+    *reinterpret_cast<uint4*>(cc + i * half_w + j0) = outv;
+    if (ex.rows) {  // boundary rows also go straight to the neighbours' mailboxes (peer memory)
+      const int64_t slot = (int64_t)(((sweep / ex.sweeps_per_period) + 1u) & 1u) * ex.slot_bytes;
+      bool sent = false;
+      if (ex.up && i >= ex.up_row0 && i < ex.up_row0 + ex.rows) {
+        *reinterpret_cast<uint4*>(ex.up + slot + (i - ex.up_row0) * half_w + j0) = outv;
+        sent = true;
+      }
+      if (ex.down && i >= ex.down_row0 && i < ex.down_row0 + ex.rows) {
+        *reinterpret_cast<uint4*>(ex.down + slot + (i - ex.down_row0) * half_w + j0) = outv;
+        sent = true;
+      }
+      if (sent) __threadfence_system();
+    }
   }
   if (TRACE) {
 #pragma unroll
@@ -144,7 +159,8 @@ int launch_ising(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_loca
                  int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
                  const uint32_t* thresholds, const float* fields, const float* variates, int64_t variates_sweeps,
                  int64_t chain, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int64_t count_lo,
-                 int64_t count_hi, unsigned long long* trace, int64_t trace_len, cudaStream_t s) {
+                 int64_t count_hi, unsigned long long* trace, int64_t trace_len, const tthrml_halo_export& ex,
+                 cudaStream_t s) {
   static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
   if (!per_sm) {
     int dev = 0, n = 0, b = 0;
@@ -162,21 +178,33 @@ int launch_ising(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_loca
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
   k_ising2d<VARIATES, TRACE><<<grid, kIsingThreads, 0, s>>>(
       cc, co, half_w, make_fastdiv((uint32_t)(half_w >> 4)), rows_local, wrap, row_lo, row_hi, global_row0, height, colour, block_row0, thresholds, fields,
-      variates, variates_sweeps, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len);
+      variates, variates_sweeps, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len, ex);
   return launch_status("k_ising2d launch");
 }
 
 }  // namespace
 }  // namespace tthrml
 
-extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, int64_t width,
-                                        int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
-                                        int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
-                                        const uint32_t* thresholds, const float* fields, const float* variates,
-                                        int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
-                                        const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
-                                        int64_t* trace, int64_t trace_len, void* stream) {
+extern "C" int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* other_state, int64_t width,
+                                          int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                          int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                          const uint32_t* thresholds, const float* fields, const float* variates,
+                                          int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
+                                          const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
+                                          int64_t* trace, int64_t trace_len, const tthrml_halo_export* export_host,
+                                          void* stream) {
   using namespace tthrml;
+  tthrml_halo_export ex{};
+  if (export_host) {
+    ex = *export_host;
+    if (ex.rows < 0 || (ex.rows && (ex.sweeps_per_period == 0 || ex.slot_bytes < ex.rows * (width / 2) ||
+                                    ((uintptr_t)ex.up % 16) || ((uintptr_t)ex.down % 16) || ex.up_row0 < 0 ||
+                                    ex.down_row0 < 0 || ex.up_row0 + ex.rows > rows_local ||
+                                    ex.down_row0 + ex.rows > rows_local))) {
+      set_error("tthrml_ising2d_halfsweep_x: invalid halo export descriptor");
+      return TTHRML_ERR_ARG;
+    }
+  }
   if (!colour_state || !other_state || (colour != 0 && colour != 1)) {
     set_error("tthrml_ising2d_halfsweep: invalid arguments");
     return TTHRML_ERR_ARG;
@@ -219,7 +247,7 @@ extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* othe
 #define TTHRML_ISING_LAUNCH(V, TR)                                                                                  \
   return launch_ising<V, TR>(colour_state, other_state, hw, rows_local, wrap_rows, row_lo, row_hi, global_row0,   \
                              height, colour, block_row0, thresholds, fields, variates, variates_sweeps, chain, seed, \
-                             sweep, ctl, count_lo, count_hi, tr, trace_len, s)
+                             sweep, ctl, count_lo, count_hi, tr, trace_len, ex, s)
   if (variates) {
     if (trace) TTHRML_ISING_LAUNCH(true, true);
     TTHRML_ISING_LAUNCH(true, false);
@@ -227,4 +255,17 @@ extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* othe
   if (trace) TTHRML_ISING_LAUNCH(false, true);
   TTHRML_ISING_LAUNCH(false, false);
 #undef TTHRML_ISING_LAUNCH
+}
+
+extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, int64_t width,
+                                        int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                        int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                        const uint32_t* thresholds, const float* fields, const float* variates,
+                                        int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
+                                        const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
+                                        int64_t* trace, int64_t trace_len, void* stream) {
+  return tthrml_ising2d_halfsweep_x(colour_state, other_state, width, rows_local, wrap_rows, row_lo, row_hi,
+                                    global_row0, height, colour, block_row0, thresholds, fields, variates,
+                                    variates_sweeps, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len,
+                                    nullptr, stream);
 }

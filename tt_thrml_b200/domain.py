@@ -67,10 +67,16 @@ class LatticeStrips:
     halfsweep: the half-sweep implementation (default: the CUDA kernel
     tthrml_ising2d_halfsweep); tests substitute a host restatement to check
     the decomposition logic on CPU ranks.
+    exchange: "p2p" (default with the CUDA kernel): the last two half-sweeps
+    of a period store the boundary rows straight into the neighbours'
+    mailboxes in peer memory (CUDA IPC over NVLink), a flag publishes the
+    period and the next period imports -- no host step, one CUDA graph for
+    any number of periods; "nccl": the host posts NCCL (or gloo) send/recv
+    of the halo rows between periods.
     """
 
     def __init__(self, program, *, device=None, halo: int = 32, process_group=None,
-                 halfsweep: Callable | None = None, cuda_graphs: bool = True):
+                 halfsweep: Callable | None = None, cuda_graphs: bool = True, exchange: str = "p2p"):
         torch = _torch()
         st = program.tt_stencil()
         if st.get("kind") != "ising2d":
@@ -101,6 +107,10 @@ class LatticeStrips:
         self.J, self.h_field = float(program.J), float(program.h)
         self._halfsweep = halfsweep or self._cuda_halfsweep
         self._custom = halfsweep is not None
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', got {exchange!r}")
+        self.exchange = "nccl" if self._custom else exchange
+        self._p2p = None
         self.cuda_graphs = bool(cuda_graphs) and not self._custom
         fields, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
         self.fields_host, self.thresholds_host = fields, thr
@@ -209,28 +219,158 @@ class LatticeStrips:
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
         self._ctl_value = None
+        if self.exchange == "p2p":
+            self._prime_p2p()
 
     # ----------------------------------------------------------------- sweeps
-    def _cuda_halfsweep(self, colour: int, row_lo: int, row_hi: int, sweep: int, stream, ctl_ptr=None) -> None:
+    def _cuda_halfsweep(self, colour: int, row_lo: int, row_hi: int, sweep: int, stream, ctl_ptr=None,
+                        export=None) -> None:
         c, o = self.colours[colour], self.colours[1 - colour]
         trace = self._trace
         nat.check(
-            self._lib.tthrml_ising2d_halfsweep(
+            self._lib.tthrml_ising2d_halfsweep_x(
                 c.data_ptr(), o.data_ptr(), self.W, self.rows_local, 0, row_lo, row_hi, self.global_row0, self.H,
                 colour, self.block_rows[colour], self.thresholds.data_ptr(), self.fields.data_ptr(), None, 0, 0,
                 self.seed, sweep, ctl_ptr, self.D, self.D + self.h,
                 None if trace is None else trace.data_ptr(), 0 if trace is None else trace.shape[0],
-                nat.stream_handle(stream),
+                None if export is None else ctypes.byref(export), nat.stream_handle(stream),
             ),
-            "tthrml_ising2d_halfsweep",
+            "tthrml_ising2d_halfsweep_x",
         )
 
     def _period(self, sweep0: int, stream, ctl_ptr=None) -> None:
-        """The D half-sweeps of one exchange period, starting at sweep sweep0 (colour 0)."""
+        """One exchange period starting at sweep sweep0 (colour 0): D half-sweeps; with the peer-memory
+        exchange also the halo import before them, the fused boundary-row export in the last two and the
+        flag signal after them."""
+        p2p = self.exchange == "p2p"
+        per = self.D // 2
+        h = stream if stream is None else nat.stream_handle(stream)
+        if p2p:
+            m = self._p2p
+            nat.check(
+                self._lib.tthrml_halo_import(
+                    self.colours[0].data_ptr(), self.colours[1].data_ptr(), self.W, self.D, 0, self.h + self.D,
+                    m["own"], m["own"] + m["flags_off"], per, sweep0, ctl_ptr, m["error"].data_ptr(), h,
+                ),
+                "tthrml_halo_import",
+            )
         for k in range(1, self.D + 1):
             colour = (k - 1) & 1
             sweep = sweep0 + (k - 1) // 2
-            self._halfsweep(colour, k, self.rows_local - k, sweep, stream, ctl_ptr)
+            if p2p and k >= self.D - 1:
+                self._halfsweep(colour, k, self.rows_local - k, sweep, stream, ctl_ptr, self._p2p["export"][colour])
+            else:
+                self._halfsweep(colour, k, self.rows_local - k, sweep, stream, ctl_ptr)
+        if p2p:
+            m = self._p2p
+            nat.check(
+                self._lib.tthrml_halo_signal(m["up"] + m["flags_off"] + 4, m["down"] + m["flags_off"], per, sweep0,
+                                             ctl_ptr, h),
+                "tthrml_halo_signal",
+            )
+
+    # ------------------------------------------------------ peer-memory exchange
+    def _setup_p2p(self) -> None:
+        """Mailboxes in IPC-exported device memory, the neighbours' opened, export descriptors."""
+        if self._p2p is not None:
+            return
+        nat.bind_device(self.device.index)
+        D, hw = self.D, self.W // 2
+        plane = D * hw
+        mb_bytes = 8 * plane  # [2 slots][2 directions][2 colours][D][W/2]
+        flags_off = (mb_bytes + 255) // 256 * 256
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        nat.check(self._lib.tthrml_ipc_malloc(flags_off + 256, ctypes.byref(own), handle), "tthrml_ipc_malloc")
+        ptrs = {self.rank: own.value}
+        opened = []
+        up = (self.rank - 1) % self.world
+        down = (self.rank + 1) % self.world
+        if self.world > 1:
+            dist = _dist()
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+            for r in {up, down} - {self.rank}:
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_char * 64).from_buffer_copy(handles[r])
+                nat.check(self._lib.tthrml_ipc_open(buf, ctypes.byref(p)), "tthrml_ipc_open")
+                ptrs[r] = p.value
+                opened.append(p.value)
+        exports = []
+        for c in range(2):
+            ex = nat.HaloExport()
+            ex.up = ptrs[up] + (1 * 2 + c) * plane  # up neighbour's "from down" mailbox
+            ex.down = ptrs[down] + (0 * 2 + c) * plane  # down neighbour's "from up" mailbox
+            ex.up_row0, ex.down_row0, ex.rows = D, self.h, D
+            ex.slot_bytes = 4 * plane
+            ex.sweeps_per_period = D // 2
+            exports.append(ex)
+        torch = _torch()
+        self._p2p = {
+            "own": own.value, "up": ptrs[up], "down": ptrs[down], "opened": opened, "flags_off": flags_off,
+            "export": exports, "error": torch.zeros(1, dtype=torch.int32, device=self.device), "plane": plane,
+        }
+
+    def _prime_p2p(self) -> None:
+        """Resets this rank's flags and, when resuming mid-run, replays the exchange of the period that
+        completed last (its own boundary rows into the neighbours' mailboxes, then the signal), so the
+        next period's import finds current halos.  Collective over the ranks."""
+        torch = _torch()
+        self._setup_p2p()
+        m = self._p2p
+        per = self.D // 2
+        cuda_rt = torch.cuda
+        cuda_rt.synchronize(self.device)
+        dist = _dist()
+        flags = (ctypes.c_uint32 * 2)(0, 0)
+        nat.bind_device(self.device.index)
+        nat.check(self._lib.tthrml_memcpy(ctypes.c_void_p(m["own"] + m["flags_off"]), flags, 8, None),
+                  "tthrml_memcpy")
+        m["error"].zero_()
+        cuda_rt.synchronize(self.device)
+        if self.world > 1 and dist is not None:
+            dist.barrier(group=self.group)
+        if self.sweep > 0:
+            p_done = self.sweep // per
+            slot = (p_done & 1) * 4 * m["plane"]
+            hw = self.W // 2
+            for c in range(2):
+                ex = m["export"][c]
+                top = self.colours[c][self.D : 2 * self.D]
+                bottom = self.colours[c][self.h : self.h + self.D]
+                for dst, src in ((ex.up + slot, top.data_ptr()), (ex.down + slot, bottom.data_ptr())):
+                    nat.check(self._lib.tthrml_memcpy(ctypes.c_void_p(dst), ctypes.c_void_p(src), self.D * hw, None),
+                              "tthrml_memcpy")
+            nat.check(
+                self._lib.tthrml_halo_signal(m["up"] + m["flags_off"] + 4, m["down"] + m["flags_off"], per,
+                                             self.sweep - per, None, None),
+                "tthrml_halo_signal",
+            )
+            cuda_rt.synchronize(self.device)
+            if self.world > 1 and dist is not None:
+                dist.barrier(group=self.group)
+
+    def check_errors(self) -> None:
+        """Raises if a halo import gave up waiting for a neighbour (peer-memory exchange)."""
+        if self._p2p is not None:
+            self._sync()
+            if int(self._p2p["error"].item()):
+                raise RuntimeError("halo exchange: a neighbour's period flag did not arrive in time")
+
+    def close(self) -> None:
+        """Releases the peer mappings and the mailbox (collective when several ranks share the lattice)."""
+        if self._p2p is None:
+            return
+        self._sync()
+        dist = _dist()
+        if self.world > 1 and dist is not None:
+            dist.barrier(group=self.group)
+        nat.bind_device(self.device.index)
+        for p in self._p2p["opened"]:
+            self._lib.tthrml_ipc_close(ctypes.c_void_p(p))
+        self._lib.tthrml_free(ctypes.c_void_p(self._p2p["own"]))
+        self._p2p = None
+        self._graphs.clear()
 
     def run_sweeps(self, n: int) -> None:
         """n sweeps (n a multiple of D/2), one halo exchange per D/2 sweeps."""
@@ -240,35 +380,51 @@ class LatticeStrips:
         if self._trace is None:
             raise RuntimeError("prepare_rng must be called before running sweeps")
         torch = _torch()
+        if self.exchange == "p2p":
+            if self._p2p is None:
+                self._prime_p2p()
+            if self.cuda_graphs:
+                self._replay_periods(n // per)
+            else:
+                nat.bind_device(self.device.index)
+                with torch.cuda.stream(self._stream):
+                    for _ in range(n // per):
+                        self._period(self.sweep, self._stream)
+                        self.sweep += per
+            return
         for _ in range(n // per):
             if self.cuda_graphs:
-                self._replay_period()
+                self._replay_periods(1)
             elif self._custom:
                 self._period(self.sweep, None)
+                self.sweep += per
             else:
                 nat.bind_device(self.device.index)
                 with torch.cuda.stream(self._stream):
                     self._period(self.sweep, self._stream)
-            self.sweep += per
+                self.sweep += per
             self._exchange()
 
-    def _replay_period(self) -> None:
+    def _replay_periods(self, n_periods: int) -> None:
+        """Replays the graph of n_periods consecutive periods (captured once per count); advances self.sweep."""
         torch = _torch()
         nat.bind_device(self.device.index)
+        per = self.D // 2
         if self._ctl is None:
             self._ctl = torch.zeros(2, dtype=torch.int64, device=self.device)
             self._ctl_host = torch.zeros(2, dtype=torch.int64, pin_memory=True)
             self._ctl_value = None
-        g = self._graphs.get("period")
+        g = self._graphs.get(n_periods)
         if g is None:
             g = torch.cuda.CUDAGraph()
             self._stream.synchronize()
             with torch.cuda.graph(g, stream=self._stream):
                 s = torch.cuda.current_stream(self.device)
-                self._period(0, s, self._ctl.data_ptr())
-                nat.check(self._lib.tthrml_ctl_advance(self._ctl.data_ptr(), self.D // 2, nat.stream_handle(s)),
+                for j in range(n_periods):
+                    self._period(j * per, s, self._ctl.data_ptr())
+                nat.check(self._lib.tthrml_ctl_advance(self._ctl.data_ptr(), n_periods * per, nat.stream_handle(s)),
                           "tthrml_ctl_advance")
-            self._graphs["period"] = g
+            self._graphs[n_periods] = g
         want = (self.sweep, self.seed)
         with torch.cuda.stream(self._stream):
             if self._ctl_value != want:
@@ -278,7 +434,8 @@ class LatticeStrips:
                 self._ctl_host[1] = lo - (1 << 64) if lo >= (1 << 63) else lo
                 self._ctl.copy_(self._ctl_host, non_blocking=True)
             g.replay()
-        self._ctl_value = (self.sweep + self.D // 2, self.seed)
+        self.sweep += n_periods * per
+        self._ctl_value = (self.sweep, self.seed)
 
     def _backend_is_nccl(self) -> bool:
         dist = _dist()
@@ -355,6 +512,8 @@ class LatticeStrips:
         self.sweep = int(ckpt["sweep"])
         self._ctl_value = None
         self._after_load()
+        if self.exchange == "p2p":
+            self._prime_p2p()
 
     # ------------------------------------------------------------ observables
     def trace(self) -> np.ndarray:
