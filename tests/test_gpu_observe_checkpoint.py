@@ -125,3 +125,25 @@ def test_checkpoint_rejects_a_different_executor(cuda_device):
     b = Executor(None, 0, prog, make_cuda_config(n_chains=32), n_sweeps=4, n_chains=32)
     with pytest.raises(ValueError):
         b.restore(ck)
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_magnetisation_schedule_equals_state_samples(cuda_device, graphs):
+    """The device-side magnetisation of a whole schedule (one CUDA graph when graphs are on) equals the
+    per-chain sums of the states that sample_states returns for the same key."""
+    from tt_thrml_b200.observers import MagnetizationObserver
+
+    prog = workloads.ising_lattice_2d(32, 32, beta=0.44)
+    C = 256
+    rng = np.random.default_rng(4)
+    init = [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
+    sched = th.SamplingSchedule(n_warmup=6, n_samples=9, steps_per_sample=3)
+    ex = Executor(None, 0, prog, make_cuda_config(n_chains=C, cuda_graphs=graphs), n_sweeps=64, n_chains=C)
+    blocks = prog.gibbs_spec.free_blocks
+    _, mags = ex.sample_with_observation(5, sched, MagnetizationObserver(blocks), init_state_free=init)
+    _, mags2 = ex.sample_with_observation(5, sched, MagnetizationObserver(blocks), init_state_free=init)
+    states = ex.sample_states(5, sched, blocks, init_state_free=init)
+    want = sum(np.where(s, 1.0, -1.0).sum(-1) for s in states)  # [n_samples, C]
+    assert mags.shape == (9, C)
+    np.testing.assert_array_equal(mags, want)
+    np.testing.assert_array_equal(mags2, want)

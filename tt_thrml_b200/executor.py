@@ -321,10 +321,7 @@ class Executor:
         position of every run; the host only rewrites ctl when it drifts.
         """
         torch = _torch()
-        if self._ctl is None:
-            self._ctl = torch.zeros(2, dtype=torch.int64, device=self._tdev)  # tthrml_run_ctl
-            self._ctl_host = torch.zeros(2, dtype=torch.int64, pin_memory=True)
-            self._ctl_value = None
+        self._ensure_ctl()
         g = self._graphs.get(n)
         if g is None:
             self._prepare_launch_state()
@@ -342,6 +339,18 @@ class Executor:
                     "tthrml_ctl_advance",
                 )
             self._graphs[n] = g
+        self._replay_with_ctl(g, n)
+
+    def _ensure_ctl(self) -> None:
+        torch = _torch()
+        if self._ctl is None:
+            self._ctl = torch.zeros(2, dtype=torch.int64, device=self._tdev)  # tthrml_run_ctl
+            self._ctl_host = torch.zeros(2, dtype=torch.int64, pin_memory=True)
+            self._ctl_value = None
+
+    def _replay_with_ctl(self, g, n: int) -> None:
+        """Sets the device run control to (sweep counter, seed) if it drifted, replays g, advances n sweeps."""
+        torch = _torch()
         seed = self._rng_buffers.seed if self._rng_buffers.seed is not None else 0
         want = (self._sweep_counter, seed)
         with torch.cuda.stream(self._stream):
@@ -354,6 +363,44 @@ class Executor:
             g.replay()
         self._sweep_counter += n
         self._ctl_value = (self._sweep_counter, seed)
+
+    def _run_schedule_graph(self, schedule, f_observe, carry):
+        """Warm-up, every sample's sweeps and every observation as one CUDA graph (captured once per
+        schedule and observer); returns the device tensor of observations [n_samples, ...]."""
+        torch = _torch()
+        n_w, n_s, steps = int(schedule.n_warmup), int(schedule.n_samples), int(schedule.steps_per_sample)
+        n_total = n_w + max(0, n_s - 1) * steps
+        self._check_ready(n_total)
+        self._ensure_ctl()
+        key = ("schedule", n_w, n_s, steps, id(f_observe))
+        entry = self._graphs.get(key)
+        if entry is None or entry[2] is not carry:
+            self._prepare_launch_state()
+            obs = f_observe.capture_buffer(self, n_s)
+            nat.bind_device(self._tdev.index)
+            g = torch.cuda.CUDAGraph()
+            self._stream.synchronize()
+            with torch.cuda.graph(g, stream=self._stream):
+                s = torch.cuda.current_stream(self._tdev)
+                k = 0
+                for _ in range(n_w):
+                    for group in self.compiled.sampling_groups:
+                        self._run_sampling_group(group, k, capturing=True)
+                    k += 1
+                f_observe.observe_capture(self, carry, obs, 0, s)
+                for i in range(1, n_s):
+                    for _ in range(steps):
+                        for group in self.compiled.sampling_groups:
+                            self._run_sampling_group(group, k, capturing=True)
+                        k += 1
+                    f_observe.observe_capture(self, carry, obs, i, s)
+                nat.check(self._lib.tthrml_ctl_advance(self._ctl.data_ptr(), n_total, nat.stream_handle(s)),
+                          "tthrml_ctl_advance")
+            entry = (g, obs, carry)
+            self._graphs[key] = entry
+        g, obs, _ = entry
+        self._replay_with_ctl(g, n_total)
+        return obs
 
     def _prepare_launch_state(self) -> None:
         """Uploads descriptors and allocates scratch ahead of a graph capture."""
@@ -758,7 +805,7 @@ class Executor:
             host = out.cpu()
         return host.numpy()
 
-    def accumulate_moments(self, rows, spin_rows, order: int, acc, spin_as_bool: bool = True) -> None:
+    def accumulate_moments(self, rows, spin_rows, order: int, acc, spin_as_bool: bool = True, stream=None) -> None:
         """acc[m][chain] += product of the values at rows[m][:order] (device tensors; DeviceMomentObserver)."""
         if self._dense:
             raise NotImplementedError("device-side moments need a row-major state (not a dense program)")
@@ -767,10 +814,34 @@ class Executor:
             self._lib.tthrml_moments_accumulate(
                 self._global_state.data_ptr(), self._state_code, self.n_chains, rows.data_ptr(), spin_rows.data_ptr(),
                 int(order), int(rows.shape[0]), 1 if spin_as_bool else 0, acc.data_ptr(),
-                nat.stream_handle(self._stream),
+                nat.stream_handle(stream if stream is not None else self._stream),
             ),
             "tthrml_moments_accumulate",
         )
+
+    def block_sums_into(self, blocks: Sequence, out, stream) -> None:
+        """Per-chain sums of the listed blocks written into the device tensor `out` on `stream`
+        (no allocation, no synchronisation: usable inside a CUDA-graph capture)."""
+        torch = _torch()
+        lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
+        with torch.cuda.stream(stream):
+            out.zero_()
+            if self._dense:
+                for b in blocks:
+                    bi = lookup[id(b)] if not isinstance(b, int) else b
+                    out += self._dense_block_values(bi).double().sum(1)
+                return
+        nat.bind_device(self._tdev.index)
+        for b in blocks:
+            bi = lookup[id(b)] if not isinstance(b, int) else b
+            spec = self.compiled.blocks[bi].spec
+            nat.check(
+                self._lib.tthrml_sum_rows(
+                    self._global_state.data_ptr(), self._state_code, self.n_chains, spec.block_global_start,
+                    spec.n_nodes, out.data_ptr(), nat.stream_handle(stream),
+                ),
+                "tthrml_sum_rows",
+            )
 
     # --------------------------------------------------------------- schedule
 
@@ -798,10 +869,24 @@ class Executor:
         n_total = schedule.n_warmup + max(0, schedule.n_samples - 1) * schedule.steps_per_sample
         self.load_state(list(init_state_free), list(state_clamp))
         self._prepare_rng_thrml_compat(key, schedule, n_total)
-        self.run_warmup(schedule.n_warmup)
 
         carry = f_observe.init() if observation_carry_init is None else observation_carry_init
         device_side = getattr(f_observe, "device_side", False)
+        if (device_side and self.config.cuda_graphs and not self.profile and schedule.n_samples >= 1
+                and callable(getattr(f_observe, "observe_capture", None))):
+            # the whole schedule is one graph replay; observations stay on the device until the end
+            carry = f_observe.prepare(self, carry)
+            obs = self._run_schedule_graph(schedule, f_observe, carry)
+            with torch_stream(self._stream):
+                host = obs.cpu().numpy() if obs is not None else None
+            finalize = getattr(f_observe, "finalize", None)
+            if callable(finalize):
+                self._stream.synchronize()
+                carry = finalize(carry)
+            if host is None:
+                return carry, None
+            return carry, (tree_expand(host[0]) if schedule.n_samples <= 1 else host)
+        self.run_warmup(schedule.n_warmup)
 
         def observe(carry, i):
             if device_side:
@@ -844,6 +929,10 @@ class Executor:
                 "kernel_total_ms": sum(ks),
             }
         return summary
+
+
+def torch_stream(stream):
+    return _torch().cuda.stream(stream)
 
 
 def _device_obs_to_host(all_obs: list, stream) -> list:

@@ -155,6 +155,23 @@ class DeviceMomentObserver:
         executor.accumulate_moments(carry["rows"], carry["spin"], carry["order"], carry["acc"], self.spin_as_bool)
         return carry, None
 
+    # graph capture of a whole schedule (Executor.sample_with_observation)
+    def prepare(self, executor, carry):
+        if carry is None:  # tables are kept per executor, so a captured schedule graph is reused
+            cache = self.__dict__.setdefault("_carry_cache", {})
+            carry = cache.get(id(executor))
+            if carry is None:
+                carry = cache[id(executor)] = self._tables(executor)
+        carry["acc"].zero_()
+        return carry
+
+    def capture_buffer(self, executor, n_samples):
+        return None
+
+    def observe_capture(self, executor, carry, obs, sample_index, stream):
+        executor.accumulate_moments(carry["rows"], carry["spin"], carry["order"], carry["acc"], self.spin_as_bool,
+                                    stream=stream)
+
     def finalize(self, carry, stream=None):
         if carry is None:
             return [np.zeros(len(group), dtype=np.float32) for group in self.moment_spec]
@@ -186,6 +203,18 @@ class MagnetizationObserver:
     def observe_device(self, executor, carry, sample_index):
         # a device tensor; the executor reads every sample back in one copy at the end
         return carry, executor.block_sums(self.blocks, to_host=False)
+
+    # graph capture of a whole schedule (Executor.sample_with_observation)
+    def prepare(self, executor, carry):
+        return carry
+
+    def capture_buffer(self, executor, n_samples):
+        import torch
+
+        return torch.empty((n_samples, executor.n_chains), dtype=torch.float64, device=executor.compiled.device)
+
+    def observe_capture(self, executor, carry, obs, sample_index, stream):
+        executor.block_sums_into(self.blocks, obs[sample_index], stream)
 
 
 def tree_stack(observations):
