@@ -36,18 +36,16 @@ constexpr int kBitsThreads = 128;
 constexpr int kBitsStageRows = TTHRML_BITS_STAGE_ROWS;
 constexpr int kSliceBytes = 32;  // 256 chains
 
-// Stages the first kBitsStageRows neighbour rows of an item: lane l copies word
-// (l & 7) of neighbour rows (l >> 3), (l >> 3) + 4, ...
+// Stages the first kBitsStageRows neighbour rows of an item (32 bytes each):
+// lane l copies half (l & 1) of neighbour row (l >> 1) with one 16-byte copy.
+static_assert(kBitsStageRows == 16, "one 16-byte copy per lane stages 16 rows of 32 bytes");
 __device__ __forceinline__ void issue_rows_bits(const RowInfo& m, int64_t word0, bool valid, const uint32_t* state,
                                                 int64_t W, unsigned char* stage_buf, int lane) {
   if (!valid) return;
   const int staged = m.deg < kBitsStageRows ? m.deg : kBitsStageRows;
-#pragma unroll
-  for (int i = 0; i < kBitsStageRows / 4; ++i) {
-    const int k = (lane >> 3) + 4 * i;
-    const int32_t j = __shfl_sync(0xffffffffu, m.col, k);
-    if (k < staged) cp_async_bytes<4>(stage_buf + k * kSliceBytes + (lane & 7) * 4, state + (int64_t)j * W + word0 + (lane & 7));
-  }
+  const int k = lane >> 1, half = lane & 1;
+  const int32_t j = __shfl_sync(0xffffffffu, m.col, k);
+  if (k < staged) cp_async_bytes<16>(stage_buf + k * kSliceBytes + half * 16, state + (int64_t)j * W + word0 + half * 4);
 }
 
 // acc[v] += w * s_v for the 8 chains of one lane, s_v = -1 where bit v of b is set.
