@@ -113,7 +113,7 @@ static int or_categorical_icdf(const float* theta, int q, double u, double* marg
   int cat = 0;
   double mg = INFINITY;
   for (int k = 0; k < q - 1; ++k) {
-    const int reached = head[k] <= tail[k + 1] ? head[k] <= u * s : (1.0 - u) * s <= tail[k + 1];
+    const int reached = u < 0.5 ? head[k] <= u * s : (1.0 - u) * s <= tail[k + 1];
     cat += reached;
     if (head[k] > 0.0 && tail[k + 1] > 0.0) {
       const double d = fabs(lu - (log(head[k]) - log(tail[k + 1])));

@@ -85,7 +85,7 @@ __host__ __device__ __forceinline__ u32x4 philox4x32_10(u32x4 c, const PhiloxKey
 #pragma unroll
 #endif
   for (int r = 0; r < 10; ++r) {
-#ifdef __CUDA_ARCH__
+#if defined(__CUDA_ARCH__) && !defined(TTHRML_PHILOX_WIDE)
     const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
     const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
 #else
@@ -131,12 +131,13 @@ __host__ __device__ __forceinline__ uint32_t seed_hi(uint64_t s) { return (uint3
 // Categorical draw in Philox mode by inverse CDF from one uniform u, a sample
 // of softmax(theta): e_k = 2^((theta_k - max theta) * log2 e) (ex2.approx),
 // and the draw is the number of boundaries k < q - 1 that u reaches,
-// u >= C_k / S with C_k = e_0 + ... + e_k and S = C_(q-1).  Each boundary is
-// decided on the side where its mass is small: the head sum C_k against u*S
-// where C_k <= T_(k+1), else the tail sum T_(k+1) = e_(k+1) + ... + e_(q-1)
-// (summed from the end) against (1 - u)*S, which is exact in float32.  The
-// float32 error of a decision then stays near 1e-6 in logit units, inside the
-// 1e-5 threshold band of the parity criteria, at either end of the CDF.
+// u >= C_k / S with C_k = e_0 + ... + e_k and S = C_(q-1).  For u < 1/2 the
+// boundaries are decided on head sums, C_k <= u*S; otherwise on tail sums
+// T_(k+1) = e_(k+1) + ... + e_(q-1) (summed from the end) against (1 - u)*S,
+// which is exact in float32.  Either way every boundary close to u is decided
+// by a sum that is small where the decision is close, so the float32 error of
+// a decision stays near 1e-6 in logit units at both ends of the CDF, inside the
+// 1e-5 threshold band of the parity criteria.
 template <int QMAX>
 __device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int q, float u) {
   constexpr bool kUnroll = QMAX <= 16;  // small bounds stay in registers
@@ -157,6 +158,7 @@ __device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int 
       head[k] = s;
     }
   }
+  const bool low = u < 0.5f;
   const float us = __fmul_rn(u, s), vs = __fmul_rn(1.0f - u, s);
   int cat = 0;
   float tail = 0.0f;  // T_(k+1) while boundary k is decided, walking down from the top
@@ -164,8 +166,7 @@ __device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int 
   for (int k = QMAX - 2; k >= 0; --k) {
     if (k < q - 1) {
       tail = k == q - 2 ? e[k + 1] : __fadd_rn(tail, e[k + 1]);
-      const bool reached = head[k] <= tail ? head[k] <= us : vs <= tail;
-      cat += reached ? 1 : 0;
+      cat += (low ? head[k] <= us : vs <= tail) ? 1 : 0;
     }
   }
   return cat;

@@ -30,6 +30,12 @@ namespace {
 constexpr int kPottsThreads = 256;
 constexpr int kPottsQ = 8;  // categories handled by this kernel
 constexpr int kRows = kPottsQ + 1;  // matrix rows per neighbour category, the last one all zero
+#ifndef TTHRML_POTTS_ROW_FLOATS
+#define TTHRML_POTTS_ROW_FLOATS 12
+#endif
+// a pair-sum row holds kPottsQ floats padded to kRowFloats: rows 48 bytes apart
+// spread the random per-lane row reads over all shared-memory banks
+constexpr int kRowFloats = TTHRML_POTTS_ROW_FLOATS;
 
 template <bool VARIATES>
 __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
@@ -39,10 +45,10 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     int64_t variates_sweeps, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl) {
   // P[a][s0][s1][k] = J[a][k][s0] + J[a][k][s1] (float32), with J[a][k][s] = 0
   // for s >= q (rows kPottsQ: categories out of range) and for k >= q
-  __shared__ __align__(16) float P[3][kRows][kRows][kPottsQ];
-  for (int i = threadIdx.x; i < 3 * kRows * kRows * kPottsQ; i += blockDim.x) {
-    const int k = i % kPottsQ, s1 = (i / kPottsQ) % kRows, s0 = (i / (kPottsQ * kRows)) % kRows;
-    const int a = i / (kPottsQ * kRows * kRows);
+  __shared__ __align__(16) float P[3][kRows][kRows][kRowFloats];
+  for (int i = threadIdx.x; i < 3 * kRows * kRows * kRowFloats; i += blockDim.x) {
+    const int k = i % kRowFloats, s1 = (i / kRowFloats) % kRows, s0 = (i / (kRowFloats * kRows)) % kRows;
+    const int a = i / (kRowFloats * kRows * kRows);
     const float j0 = (s0 < q && k < q) ? J[((int64_t)a * q + k) * q + s0] : 0.0f;
     const float j1 = (s1 < q && k < q) ? J[((int64_t)a * q + k) * q + s1] : 0.0f;
     (&P[0][0][0][0])[i] = __fadd_rn(j0, j1);

@@ -23,7 +23,7 @@
 #include "spin_common.cuh"
 
 #ifndef TTHRML_BITS_MIN_BLOCKS
-#define TTHRML_BITS_MIN_BLOCKS 6
+#define TTHRML_BITS_MIN_BLOCKS 5
 #endif
 #ifndef TTHRML_BITS_STAGE_ROWS
 #define TTHRML_BITS_STAGE_ROWS 16
