@@ -342,3 +342,41 @@ def test_parity_variates_follow_schedule_key_tree():
     assert buf.categorical_gumbel[1].shape == (n_total, 1, 3, 2)
     assert buf.gaussian_noise[2].shape == (n_total, 1, 1, 2)
     assert isinstance(buf.spin_threshold_logits[0], torch.Tensor)
+
+
+def test_ising_pattern_tables_are_the_exact_threshold_of_the_float32_field():
+    import numpy as np
+
+    from tt_thrml_b200.compiler import ising_pattern_tables
+
+    w, b = np.float32(0.4407), np.float32(0.0)
+    fields, thr = ising_pattern_tables(w, b)
+    for idx in range(16):
+        signs = [-1 if (idx >> k) & 1 else 1 for k in range(4)]
+        acc = np.float32(signs[0] * w)
+        for sgn in signs[1:]:
+            acc = np.float32(acc + np.float32(sgn * w))
+        assert fields[idx] == np.float32(b + acc)
+        p = 1.0 / (1.0 + np.exp(-2.0 * float(fields[idx])))
+        T = int(thr[idx])
+        # m < T  <=>  u = (2m + 1) / 2^24 < p, checked at the boundary
+        if T > 0:
+            assert (2 * (T - 1) + 1) / 2.0**24 < p
+        if T < 2**23:
+            assert (2 * T + 1) / 2.0**24 >= p
+    assert thr[0] > thr[15]  # all neighbours up favours up
+
+
+def test_stencil_and_dense_eligibility():
+    from tt_thrml_b200 import workloads
+    from tt_thrml_b200.compiler import dense_eligible, stencil_eligible
+
+    potts = workloads.potts_lattice_3d(4, 8, seed=0)
+    assert stencil_eligible(potts, 64) and not stencil_eligible(potts, 6)
+    lat = workloads.IsingLattice2D(8, 64)
+    assert stencil_eligible(lat, 1) and not stencil_eligible(lat, 2)
+    assert not stencil_eligible(workloads.IsingLattice2D(8, 48), 1)  # width not a multiple of 32
+    rbm = workloads.gaussian_bernoulli_rbm(256, 512, seed=0)
+    assert dense_eligible(rbm, 128) and not dense_eligible(rbm, 64)
+    assert not dense_eligible(workloads.gaussian_bernoulli_rbm(128, 512, seed=0), 128)  # 128 units
+    assert not stencil_eligible(rbm, 128) and not dense_eligible(potts, 128)
