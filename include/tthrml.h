@@ -249,6 +249,29 @@ int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, in
                              void* stream);
 
 /*
+ * Persistent multi-sweep update of a small periodic 2-D Ising lattice with
+ * many chains (uniform couplings): every CTA keeps the lattice of 8 chains in
+ * shared memory (height * width bytes) and runs n_half_sweeps checkerboard
+ * half-sweeps from colour0 (sweep index sweep0 + (colour0 + t) / 2 for
+ * half-sweep t), then writes the state back.  state_dev: bit-packed uint32
+ * [rows][n_chains/32] (bit set = -1) with colour c's site (Y, x) at row
+ * row0_colour_c + Y*width/2 + x/2.  Decision as tthrml_ising2d_halfsweep
+ * (16-entry threshold table over the left/right/up/down sign pattern);
+ * Philox counter (chain/4, row, sweep, "SPIN"), word chain % 4 (the sparse
+ * spin kernels' layout).  obs_dev (NULL: none): float64 [n_obs][n_chains],
+ * sample i = per-chain sum of the spins of the colours in obs_colours (bit
+ * mask) after half-sweep obs_first + i * obs_every.  A thrml schedule with
+ * its magnetisation observable is one launch.  Requires n_chains % 32 == 0,
+ * chain_offset % 8 == 0, even dimensions.
+ */
+int tthrml_ising2d_resident(uint32_t* state_dev, int64_t n_chains, int32_t height, int32_t width,
+                            int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds_dev,
+                            uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
+                            double* obs_dev, int64_t obs_first, int64_t obs_every, int64_t n_obs,
+                            int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl_dev,
+                            void* stream);
+
+/*
  * Halo export of a strip-decomposed lattice (tthrml_ising2d_halfsweep_x):
  * while a half-sweep computes local rows [up_row0, up_row0 + rows) it also
  * stores them at `up` (the up neighbour's mailbox, peer memory), rows

@@ -117,12 +117,13 @@ def compare_group(report: ParityReport, ex: Executor, o: orc.OracleSampler, gi: 
 
 
 def run_parity(program, C: int, n_sweeps: int, *, mode: str, seed: int = 11, init=None, clamp=(), force_generic=False,
-               dense_precision: str = "auto", gauss_rtol: float = GAUSS_RTOL, follow_gpu: bool = False):
+               dense_precision: str = "auto", gauss_rtol: float = GAUSS_RTOL, follow_gpu: bool = False,
+               stencil: bool = True):
     """Runs n_sweeps group by group on the GPU and in the oracle from the same state and variates."""
     from tt_thrml_b200.compiler import compile_program
 
     cfg = make_cuda_config(rng_mode="parity" if mode == "variates" else "philox", n_chains=C, cuda_graphs=False,
-                           dense_precision=dense_precision)
+                           dense_precision=dense_precision, stencil=stencil)
     compiled = compile_program(None, 0, program, cfg, n_sweeps=n_sweeps, n_chains=C, force_generic=force_generic)
     ex = Executor(None, 0, program, cfg, compiled, n_sweeps=n_sweeps, n_chains=C)
     o = orc.OracleSampler(program, n_chains=C, rng_layout=rng_layouts(compiled))

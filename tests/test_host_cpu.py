@@ -375,6 +375,7 @@ def test_stencil_and_dense_eligibility():
     assert stencil_eligible(potts, 64) and not stencil_eligible(potts, 6)
     lat = workloads.IsingLattice2D(8, 64)
     assert stencil_eligible(lat, 1) and not stencil_eligible(lat, 2)
+    assert stencil_eligible(lat, 64) and not stencil_eligible(lat, 64, "parity")  # shared-memory resident
     assert not stencil_eligible(workloads.IsingLattice2D(8, 48), 1)  # width not a multiple of 32
     rbm = workloads.gaussian_bernoulli_rbm(256, 512, seed=0)
     assert dense_eligible(rbm, 128) and not dense_eligible(rbm, 64)

@@ -750,6 +750,23 @@ POTTS_MAX_Q = 8
 
 
 @dataclass
+class IsingResidentGroupPlan:
+    """One checkerboard colour of a small 2-D Ising lattice with many chains (tthrml_ising2d_resident)."""
+
+    block_indices: tuple[int, ...]
+    dims: tuple[int, int]
+    colour: int
+    block_rows: tuple[int, int]
+    thresholds: Any  # uint32 [16] device tensor
+    family: Family = Family.SPIN
+    family_label: str = "spin"
+    kind: str = "ising2d_resident"
+    in_place: bool = True
+    group_rows: int = 0
+    device: Any = None
+
+
+@dataclass
 class IsingStencilGroupPlan:
     """One checkerboard colour of a single-chain 2-D Ising lattice (tthrml_ising2d_halfsweep)."""
 
@@ -792,7 +809,10 @@ def ising_pattern_tables(edge_weight, site_bias) -> tuple[np.ndarray, np.ndarray
     return fields, np.clip(thr, 0, 2**23).astype(np.uint32)
 
 
-def stencil_eligible(program, n_chains: int) -> bool:
+RESIDENT_MAX_SITES = 96 * 1024  # one byte per site of 8 chains in a CTA's shared memory
+
+
+def stencil_eligible(program, n_chains: int, rng_mode: str = "philox") -> bool:
     """True when the program is a lattice the stencil kernels run at this chain count."""
     stencil = getattr(program, "tt_stencil", None)
     if not callable(stencil):
@@ -802,13 +822,33 @@ def stencil_eligible(program, n_chains: int) -> bool:
         return 1 <= int(st["q"]) <= POTTS_MAX_Q and n_chains % 4 == 0
     if st.get("kind") == "ising2d":
         H, W = st["dims"]
-        return n_chains == 1 and W % 32 == 0 and H % 2 == 0
+        if n_chains == 1:
+            return W % 32 == 0 and H % 2 == 0
+        return resident_eligible(st, n_chains, rng_mode)
     return False
 
 
-def _plan_stencil(program, device):
+def resident_eligible(st: dict, n_chains: int, rng_mode: str) -> bool:
+    """Small 2-D lattices with many chains run shared-memory resident (Philox mode, chains % 32 == 0)."""
+    H, W = st["dims"]
+    return rng_mode == "philox" and n_chains % 32 == 0 and H * W <= RESIDENT_MAX_SITES
+
+
+def _plan_stencil(program, device, n_chains: int = 1):
     torch = _torch()
     st = program.tt_stencil()
+    if st["kind"] == "ising2d" and n_chains > 1:
+        _, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
+        t_dev = torch.from_numpy(thr.view(np.int32)).to(device)
+        H, W = st["dims"]
+        rows = tuple(int(r) for r in st["block_rows"])
+        return [
+            IsingResidentGroupPlan(
+                block_indices=(int(g[0]),), dims=(int(H), int(W)), colour=int(g[0]), block_rows=rows,
+                thresholds=t_dev, group_rows=H * W // 2, device=device,
+            )
+            for g in program.gibbs_spec.sampling_order
+        ]
     if st["kind"] == "ising2d":
         fields, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
         f_dev = torch.from_numpy(fields).to(device)
@@ -869,12 +909,13 @@ def compile_program(
     del ttnn
     n_chains = int(n_chains if n_chains is not None else config.n_chains)
     tdev = resolve_torch_device(device)
-    if not force_generic and stencil_eligible(program, n_chains):
+    if not force_generic and config.stencil and stencil_eligible(program, n_chains, config.rng_mode):
         specs = _stencil_specs(program)
         order = tuple(tuple(int(i) for i in g) for g in program.gibbs_spec.sampling_order)
         lowered = LoweredProgram(specs, order, len(program.gibbs_spec.free_blocks), specs[0].total_nodes,
                                  tuple(s.block_global_start for s in specs))
-        state_dtype, plans = "int8", _plan_stencil(program, tdev)
+        plans = _plan_stencil(program, tdev, n_chains)
+        state_dtype = "bits" if plans[0].kind == "ising2d_resident" else "int8"
     elif not force_generic and dense_eligible(program, n_chains):
         specs = _dense_specs(program)
         order = tuple(tuple(int(i) for i in g) for g in program.gibbs_spec.sampling_order)
@@ -918,5 +959,6 @@ __all__ = [
     "DenseGroupPlan",
     "PottsStencilGroupPlan",
     "IsingStencilGroupPlan",
+    "IsingResidentGroupPlan",
     "ising_pattern_tables",
 ]

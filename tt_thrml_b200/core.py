@@ -52,6 +52,7 @@ class CUDAConfig:
       float32, fed to the GEMM as three bf16 pieces against the weights
       repeated along K (the float32 field up to summation order); "auto" is
       "fp32" in parity mode and "bf16" in Philox mode.
+    stencil: run lattice programs on the stencil kernels (False: their tables).
     """
 
     artifact_root: Path
@@ -61,6 +62,7 @@ class CUDAConfig:
     cuda_graphs: bool = True
     spin_layout: str = "auto"
     dense_precision: str = "auto"
+    stencil: bool = True
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "artifact_root", Path(self.artifact_root).resolve())
@@ -225,6 +227,7 @@ def make_cuda_config(
     cuda_graphs: bool = True,
     spin_layout: str = "auto",
     dense_precision: str = "auto",
+    stencil: bool = True,
 ) -> CUDAConfig:
     """Create a CUDA configuration (the CUDA counterpart of make_ttmlir_config)."""
     root = Path(artifact_root if artifact_root is not None else Path(tempfile.gettempdir()) / "tt-thrml-b200")
@@ -236,6 +239,7 @@ def make_cuda_config(
         cuda_graphs=cuda_graphs,
         spin_layout=spin_layout,
         dense_precision=dense_precision,
+        stencil=stencil,
     )
 
 

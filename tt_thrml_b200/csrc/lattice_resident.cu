@@ -1,0 +1,153 @@
+// Persistent multi-sweep kernel for small 2-D Ising lattices with many chains
+// (uniform couplings, periodic): every CTA keeps the whole lattice of its 8
+// chains in shared memory and runs any number of checkerboard half-sweeps, with
+// the per-chain magnetisation of scheduled samples reduced in the kernel, so a
+// whole sampling schedule is one launch.
+//
+// State: the executor's bit-packed layout, uint32 [rows][C/32] with bit c of a
+// row set when chain c is -1; rows are block-ordered (colour c's sites of row
+// Y, x at block row Y*W/2 + x/2, see csrc/ising2d.cu).  CTA g owns chains
+// 8g..8g+7, i.e. byte g % 4 of word g / 4 of every row, and keeps it as one
+// byte per site in shared memory, [2 colours][H][W/2] bytes.
+//
+// Decision: the four neighbour bytes (left, right, up, down) of a site form
+// a word N whose bit 8k + v is neighbour k of chain v; chain v's 4-bit
+// pattern is gathered with one multiply, (((N >> v) & 0x01010101) *
+// 0x01020408) >> 24, and decides against the exact integer threshold of the
+// pattern's float32 field (as in csrc/ising2d.cu).  Philox counter: (chain/4,
+// flat row, sweep, "SPIN"), word chain % 4 -- the sparse spin kernels' layout.
+#include "common.cuh"
+
+namespace tthrml {
+namespace {
+
+constexpr int kResThreads = 512;
+
+__device__ __forceinline__ int wrapi(int i, int n) { return i < 0 ? i + n : (i >= n ? i - n : i); }
+
+__global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
+    uint32_t* state, int64_t C, int32_t H, int32_t W, int64_t row0_c0, int64_t row0_c1,
+    const uint32_t* __restrict__ thresholds, uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half,
+    double* __restrict__ obs, int64_t obs_first, int64_t obs_every, int64_t n_obs, int32_t obs_colours,
+    int64_t chain_offset, const tthrml_run_ctl* __restrict__ ctl) {
+  extern __shared__ __align__(16) unsigned char lat[];  // [2][H][W/2]
+  __shared__ uint32_t T[16];
+  __shared__ int counts[8];
+  const int hw = W >> 1;
+  const int half_sites = H * hw;
+  const int g = blockIdx.x;  // chain group
+  const int64_t words = C >> 5;
+  const int word = g >> 2, byte_in_word = g & 3;
+  if (threadIdx.x < 16) T[threadIdx.x] = thresholds[threadIdx.x];
+  for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
+    const int c = i / half_sites, r = i - c * half_sites;
+    const int64_t row = (c ? row0_c1 : row0_c0) + r;
+    lat[i] = (unsigned char)(state[row * words + word] >> (8 * byte_in_word));
+  }
+  __syncthreads();
+  const uint64_t sd = ctl ? ctl->seed : seed;
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
+  sweep0 += ctl ? ctl->sweep : 0u;
+  const uint32_t gc0 = (uint32_t)(chain_offset + 8 * g);  // global index of the group's first chain
+
+  int64_t next_obs = obs ? obs_first : -1, taken = 0;
+  for (int64_t t = 0; t < n_half; ++t) {
+    const int c = (int)((colour0 + t) & 1);
+    const uint32_t sweep = sweep0 + (uint32_t)((colour0 + t) >> 1);
+    unsigned char* mine = lat + c * half_sites;
+    const unsigned char* other = lat + (1 - c) * half_sites;
+    const int64_t row0 = c ? row0_c1 : row0_c0;
+    for (int r = threadIdx.x; r < half_sites; r += blockDim.x) {
+      const int Y = r / hw, j = r - Y * hw;
+      const int p = (Y + c) & 1;
+      const int jl = wrapi(j - 1 + p, hw), jr = wrapi(j + p, hw);
+      const int yu = wrapi(Y - 1, H), yd = wrapi(Y + 1, H);
+      const uint32_t N = (uint32_t)other[Y * hw + jl] | ((uint32_t)other[Y * hw + jr] << 8) |
+                         ((uint32_t)other[yu * hw + j] << 16) | ((uint32_t)other[yd * hw + j] << 24);
+      const uint32_t row = (uint32_t)(row0 + r);
+      const u32x4 a = philox4x32_10(u32x4{gc0 >> 2, row, sweep, kSaltSpin}, keys);
+      const u32x4 b = philox4x32_10(u32x4{(gc0 >> 2) + 1u, row, sweep, kSaltSpin}, keys);
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      uint32_t down = 0u;
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const uint32_t idx = ((((N >> v) & 0x01010101u) * 0x01020408u) >> 24) & 0xFu;
+        down |= ((w[v] >> 9) < T[idx] ? 0u : 1u) << v;
+      }
+      mine[r] = (unsigned char)down;
+    }
+    __syncthreads();
+    if (t + 1 == next_obs) {  // per-chain magnetisation after this half-sweep
+      if (threadIdx.x < 8) counts[threadIdx.x] = 0;
+      __syncthreads();
+      int local[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
+        if (!((obs_colours >> (i / half_sites)) & 1)) continue;
+        const uint32_t v8 = lat[i];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) local[v] += (v8 >> v) & 1;
+      }
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        int x = local[v];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        if ((threadIdx.x & 31) == 0) atomicAdd(&counts[v], x);
+      }
+      __syncthreads();
+      if (threadIdx.x < 8) {
+        const int n_sites = ((obs_colours & 1) ? half_sites : 0) + ((obs_colours & 2) ? half_sites : 0);
+        obs[taken * C + 8 * g + threadIdx.x] = (double)(n_sites - 2 * counts[threadIdx.x]);
+      }
+      ++taken;
+      next_obs = taken < n_obs ? next_obs + obs_every : -1;
+      __syncthreads();
+    }
+  }
+  // write back this group's byte of every row (other bytes of the word belong to other CTAs)
+  for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
+    const int c = i / half_sites, r = i - c * half_sites;
+    const int64_t row = (c ? row0_c1 : row0_c0) + r;
+    reinterpret_cast<unsigned char*>(state + row * words + word)[byte_in_word] = lat[i];
+  }
+}
+
+}  // namespace
+}  // namespace tthrml
+
+extern "C" int tthrml_ising2d_resident(uint32_t* state, int64_t n_chains, int32_t height, int32_t width,
+                                       int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds,
+                                       uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
+                                       double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
+                                       int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl,
+                                       void* stream) {
+  using namespace tthrml;
+  if (!state || !thresholds || height <= 0 || width <= 0 || height % 2 || width % 2 || n_chains <= 0 ||
+      n_chains % 32 || chain_offset % 8 || (colour0 != 0 && colour0 != 1) || n_half_sweeps < 0) {
+    set_error("tthrml_ising2d_resident: invalid arguments (even dimensions, n_chains %% 32 == 0, "
+              "chain_offset %% 8 == 0)");
+    return TTHRML_ERR_ARG;
+  }
+  if (obs && (n_obs <= 0 || obs_first < 1 || obs_every < 1 || obs_first + (n_obs - 1) * obs_every > n_half_sweeps ||
+              obs_colours < 1 || obs_colours > 3)) {
+    set_error("tthrml_ising2d_resident: observation schedule outside the run");
+    return TTHRML_ERR_ARG;
+  }
+  const int64_t smem = (int64_t)height * width;  // both colours, one byte per site
+  int dev = 0, max_smem = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return cuda_status(e, "tthrml_ising2d_resident: device query");
+  if (smem + 256 > max_smem) {
+    set_error("tthrml_ising2d_resident: a %d x %d lattice needs %lld bytes of shared memory per CTA (%d available)",
+              (int)height, (int)width, (long long)smem, max_smem);
+    return TTHRML_ERR_UNSUPPORTED;
+  }
+  e = cudaFuncSetAttribute(k_ising2d_resident, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return cuda_status(e, "k_ising2d_resident shared memory attribute");
+  if (n_half_sweeps == 0 && !obs) return TTHRML_OK;
+  k_ising2d_resident<<<(unsigned)(n_chains / 8), kResThreads, (size_t)smem, (cudaStream_t)stream>>>(
+      state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0, n_half_sweeps,
+      obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl);
+  return launch_status("k_ising2d_resident launch");
+}

@@ -301,11 +301,38 @@ class Executor:
     def run_warmup(self, n_warmup: int) -> None:
         self.run_sweeps(n_warmup)
 
+    def _resident_plans(self):
+        """The resident lattice plans when the whole program is one (colour 0 sampled first), else None."""
+        plans = [g.kernel_artifact for g in self.compiled.sampling_groups]
+        if plans and all(p.kind == "ising2d_resident" for p in plans) and [p.colour for p in plans] == [0, 1]:
+            return plans
+        return None
+
+    def _run_resident(self, n_sweeps: int, obs=None, obs_first=0, obs_every=0, n_obs=0, obs_colours=0) -> None:
+        """n sweeps (and scheduled magnetisation samples) of a resident lattice in one launch."""
+        plan = self._resident_plans()[0]
+        H, W = plan.dims
+        nat.bind_device(self._tdev.index)
+        nat.check(
+            self._lib.tthrml_ising2d_resident(
+                self._global_state.data_ptr(), self.n_chains, H, W, plan.block_rows[0], plan.block_rows[1],
+                plan.thresholds.data_ptr(), self._rng_buffers.seed, self._sweep_counter, 0, 2 * n_sweeps,
+                None if obs is None else obs.data_ptr(), obs_first, obs_every, n_obs, obs_colours,
+                self.chain_offset, None, nat.stream_handle(self._stream),
+            ),
+            "tthrml_ising2d_resident",
+        )
+        self._sweep_counter += n_sweeps
+
     def run_sweeps(self, n: int) -> None:
-        """n sweeps; replayed from a CUDA graph when config.cuda_graphs is set."""
+        """n sweeps; replayed from a CUDA graph when config.cuda_graphs is set (one launch for a
+        shared-memory-resident lattice)."""
         if n <= 0:
             return
         self._check_ready(n)
+        if self._resident_plans() is not None and self._rng_buffers.seed is not None and not self.profile:
+            self._run_resident(n)
+            return
         if not self.config.cuda_graphs or self.profile or n < 2:
             for _ in range(n):
                 self.run_sweep()
@@ -340,6 +367,23 @@ class Executor:
                 )
             self._graphs[n] = g
         self._replay_with_ctl(g, n)
+
+    def _resident_observation(self, f_observe, schedule) -> int:
+        """Colour mask for the fused resident schedule when it applies (magnetisation of lattice blocks)."""
+        from .observers import MagnetizationObserver
+
+        if (type(f_observe) is not MagnetizationObserver or self._resident_plans() is None or self.profile
+                or self._rng_buffers is None or self._rng_buffers.seed is None or schedule.n_warmup < 1
+                or schedule.n_samples < 1 or schedule.steps_per_sample < 1):
+            return 0
+        lookup = {id(b): i for i, b in enumerate(self.program.gibbs_spec.blocks)}
+        mask = 0
+        for b in f_observe.blocks:
+            bi = lookup.get(id(b)) if not isinstance(b, int) else b
+            if bi not in (0, 1):
+                return 0
+            mask |= 1 << bi
+        return mask
 
     def _ensure_ctl(self) -> None:
         torch = _torch()
@@ -483,6 +527,16 @@ class Executor:
                     self.chain_offset, seed, sweep_idx, ctl, 0, 0, None, 0, stream,
                 ),
                 "tthrml_ising2d_halfsweep",
+            )
+        elif plan.kind == "ising2d_resident":
+            H, W = plan.dims
+            nat.check(
+                self._lib.tthrml_ising2d_resident(
+                    self._global_state.data_ptr(), self.n_chains, H, W, plan.block_rows[0], plan.block_rows[1],
+                    plan.thresholds.data_ptr(), seed, sweep_idx, plan.colour, 1, None, 0, 0, 0, 0, self.chain_offset,
+                    ctl, stream,
+                ),
+                "tthrml_ising2d_resident",
             )
         elif plan.kind == "potts3d":
             bi = plan.block_indices[0]
@@ -872,6 +926,19 @@ class Executor:
 
         carry = f_observe.init() if observation_carry_init is None else observation_carry_init
         device_side = getattr(f_observe, "device_side", False)
+        colours = self._resident_observation(f_observe, schedule) if device_side else 0
+        if colours:
+            # a resident lattice with its magnetisation observable: the whole schedule is one launch
+            torch = _torch()
+            n_s = int(schedule.n_samples)
+            self._check_ready(n_total)
+            with torch.cuda.stream(self._stream):
+                obs = torch.empty((n_s, self.n_chains), dtype=torch.float64, device=self._tdev)
+            self._run_resident(n_total, obs, 2 * int(schedule.n_warmup), 2 * int(schedule.steps_per_sample), n_s,
+                               colours)
+            with torch.cuda.stream(self._stream):
+                host = obs.cpu().numpy()
+            return carry, (tree_expand(host[0]) if n_s <= 1 else host)
         if (device_side and self.config.cuda_graphs and not self.profile and schedule.n_samples >= 1
                 and callable(getattr(f_observe, "observe_capture", None))):
             # the whole schedule is one graph replay; observations stay on the device until the end
