@@ -920,8 +920,11 @@ def run_profile_target(args, W) -> int:
     ex = Executor(None, 0, prog, make_cuda_config(n_chains=C, cuda_graphs=False), n_sweeps=n, n_chains=C)
     ex.load_state(W.init(prog, C, 100), [])
     ex.prepare_rng(SEED)
-    for _ in range(n):
-        ex.run_sweep()
+    if ex._resident_plans() is not None:
+        ex.run_sweeps(n)  # one persistent launch for all n sweeps
+    else:
+        for _ in range(n):
+            ex.run_sweep()
     torch.cuda.synchronize()
     ex.check_device_errors()
     print(f"profile target: {W.workload}, {C} chains, {n} sweeps x {len(ex.compiled.sampling_groups)} groups", flush=True)
