@@ -157,3 +157,48 @@ def test_strip_checkpoint_continues_bit_for_bit():
     np.testing.assert_array_equal(c.trace(), a.trace())
     with pytest.raises(ValueError):
         LatticeStrips(prog, device="cpu", halo=4, halfsweep=lambda *a: None).restore(ck)
+
+
+def _dropout_worker(rank, world, port, out_path):
+    """Rank 1 leaves before the run (between steps, with nothing in flight); rank 0's next exchange must
+    end with an error from the process group's timeout instead of waiting forever."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    prog = workloads.IsingLattice2D(16, 32, beta=0.4407)
+    st = LatticeStrips(prog, device="cpu", halo=2, halfsweep=lambda *a: None)
+    st._halfsweep = ising_ref.make_halfsweep(st)
+    st.load_random(1)
+    st.prepare_rng(2, 8)
+    st.run_sweeps(2)  # both ranks exchange normally
+    if rank == 1:
+        return  # leaves without a word to its neighbour
+    t0 = time.perf_counter()
+    try:
+        st.run_sweeps(2)
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 - the process group reports the missing peer
+        outcome = f"error: {type(e).__name__}"
+    with open(out_path, "w") as f:
+        f.write(f"{outcome} after {time.perf_counter() - t0:.1f}s")
+
+
+def test_a_rank_that_leaves_ends_the_exchange_with_an_error(tmp_path):
+    import torch.multiprocessing as mp
+
+    out = tmp_path / "dropout.txt"
+    ctx = mp.start_processes(_dropout_worker, args=(2, _free_port(), str(out)), nprocs=2, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=120)
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    text = out.read_text()
+    assert text.startswith("error"), text
+    assert float(text.split(" after ")[1].rstrip("s")) < 60.0
