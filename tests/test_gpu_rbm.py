@@ -166,3 +166,16 @@ def test_dense_pieces_reconstruct_float32(cuda_device):
         # the first piece is the bf16 rounding of the value
         assert torch.equal(out[:, :N], out32.to(torch.bfloat16))
 
+
+
+@pytest.mark.parametrize("mode", ["variates", "philox"])
+def test_plain_table_rbm_runs_on_the_tensor_cores(cuda_device, mode):
+    """The same RBM handed over only as per-term tables (what a thrml-factor program lowers to):
+    the compiler detects the dense structure, and the tensor-core run matches the oracle."""
+    from tt_thrml_b200.workloads import TableProgram
+
+    rbm = _rbm(seed=12)
+    plain = TableProgram(rbm.gibbs_spec, rbm.tt_lower_blocks(), {})
+    rep, ex, _ = gh.run_parity(plain, C, 3, mode=mode, init=_init(13), dense_precision="fp32")
+    assert [g.kernel_artifact.kind for g in ex.compiled.sampling_groups] == ["dense", "dense"]
+    _assert_parity(rep)

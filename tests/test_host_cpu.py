@@ -381,3 +381,32 @@ def test_stencil_and_dense_eligibility():
     assert dense_eligible(rbm, 128) and not dense_eligible(rbm, 64)
     assert not dense_eligible(workloads.gaussian_bernoulli_rbm(128, 512, seed=0), 128)  # 128 units
     assert not stencil_eligible(rbm, 128) and not dense_eligible(potts, 128)
+
+
+def test_dense_structure_is_detected_in_plain_tables():
+    """An RBM handed over as plain per-term tables (as a thrml-factor program lowers) is recognised."""
+    import numpy as np
+
+    from tt_thrml_b200 import workloads
+    from tt_thrml_b200.compiler import detect_dense_couplings, lower_program
+    from tt_thrml_b200.workloads import TableProgram
+
+    rbm = workloads.gaussian_bernoulli_rbm(256, 512, seed=1, w_std=0.05)
+    plain = TableProgram(rbm.gibbs_spec, rbm.tt_lower_blocks(), {})
+    lowered = lower_program(plain)
+    got = detect_dense_couplings(lowered, 128)
+    assert got is not None
+    np.testing.assert_array_equal(got[0]["weights_nk"], rbm.W)
+    np.testing.assert_array_equal(got[1]["weights_nk"], rbm.W.T)
+    np.testing.assert_array_equal(got[0]["bias"], rbm.b_v)
+    assert got[0]["family"] == tb.core.Family.GAUSSIAN and got[0]["precision"] == 1.0
+    assert detect_dense_couplings(lowered, 64) is None  # chains not a multiple of 128
+    # weights that bf16 cannot hold: only with rounding allowed
+    W = rbm.W.copy()
+    W[0, 0] = np.float32(0.1234567)
+    rough = workloads.DenseBipartiteProgram(W, rbm.b_v, rbm.b_h)
+    lowered2 = lower_program(TableProgram(rough.gibbs_spec, rough.tt_lower_blocks(), {}))
+    assert detect_dense_couplings(lowered2, 128) is None
+    assert detect_dense_couplings(lowered2, 128, round_weights=True) is not None
+    # a sparse program is not dense
+    assert detect_dense_couplings(lower_program(workloads.erdos_renyi_ising(512, 4.0, seed=0)), 128) is None

@@ -669,18 +669,86 @@ def dense_eligible(program, n_chains: int) -> bool:
 
 def dense_pieces(program, precision: str) -> dict[int, int]:
     """bf16 pieces per value of each block's state: 3 for gaussian blocks at fp32, else 1."""
-    couplings = program.tt_dense_couplings()
+    return _pieces_of(program.tt_dense_couplings(), precision)
+
+
+def _pieces_of(couplings: dict, precision: str) -> dict[int, int]:
     return {
         bi: 3 if precision == "fp32" and Family(c["family"]) == Family.GAUSSIAN else 1 for bi, c in couplings.items()
     }
 
 
-def _plan_dense(program, device, precision: str = "bf16"):
+def detect_dense_couplings(lowered: LoweredProgram, n_chains: int, round_weights: bool = False):
+    """Dense bipartite structure found in lowered tables, as tt_dense_couplings() would give it, or None.
+
+    Two free blocks sampled one per group, spin or gaussian, where every node of
+    a block has exactly one pair term per node of the other block, in row order
+    (per-node weight rows over a whole block: the RBM case of
+    tt_thrml/compiler.py:173-176), plus one-term bias interactions and, for
+    gaussian blocks, a precision that is the same for every node.  This is how
+    an RBM written with thrml factors reaches the tensor-core kernel.  The
+    weights must be bf16-representable unless round_weights is set.
+    """
+    if len(lowered.specs) != 2 or lowered.n_free_blocks != 2 or n_chains % DENSE_CHAIN_MULTIPLE:
+        return None
+    if sorted(lowered.sampling_order) != [(0,), (1,)]:
+        return None
+    out = {}
+    for bi, spec in enumerate(lowered.specs):
+        other = lowered.specs[1 - bi]
+        if spec.family not in (Family.SPIN, Family.GAUSSIAN) or spec.n_nodes % DENSE_UNIT_MULTIPLE:
+            return None
+        n, m = spec.n_nodes, other.n_nodes
+        bias = np.zeros(n, dtype=np.float32)
+        precision = None
+        pair = None
+        for it in spec.interactions:
+            if it.n_categorical:
+                return None
+            rp, w, src = it.ragged(n)
+            if src.shape[0] == 0:  # one constant term per node
+                if w.shape[1] != 1 or not np.array_equal(np.diff(rp), np.ones(n, np.int64)):
+                    return None
+                if it.contribution_kind == "precision":
+                    if spec.family != Family.GAUSSIAN or not np.all(w[:, 0] == w[0, 0]):
+                        return None
+                    precision = np.float32(w[0, 0]) if precision is None else np.float32(precision + w[0, 0])
+                else:
+                    bias = (bias + w[:, 0]).astype(np.float32)
+            elif src.shape[0] == 1 and it.contribution_kind != "precision" and pair is None:
+                if w.shape[1] != 1 or not np.array_equal(np.diff(rp), np.full(n, m, np.int64)):
+                    return None
+                rows = np.arange(other.block_global_start, other.block_global_start + m, dtype=np.int32)
+                if not np.array_equal(src[0], np.tile(rows, n)):
+                    return None
+                pair = w[:, 0].reshape(n, m)
+            else:
+                return None
+        if pair is None:
+            return None
+        pair = np.ascontiguousarray(pair, dtype=np.float32)
+        rounded = _bf16_round(pair)
+        if not round_weights and not np.array_equal(rounded, pair):
+            return None
+        out[bi] = {"family": spec.family, "row0": spec.block_global_start, "n_units": n, "source": 1 - bi,
+                   "weights_nk": rounded, "bias": bias, "precision": 1.0 if precision is None else float(precision)}
+    return out
+
+
+def _bf16_round(x: np.ndarray) -> np.ndarray:
     torch = _torch()
-    couplings = program.tt_dense_couplings()
-    pieces = dense_pieces(program, precision)
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def _plan_dense(program, device, precision: str = "bf16"):
+    return _plan_dense_couplings(program.tt_dense_couplings(), program.gibbs_spec.sampling_order, device, precision)
+
+
+def _plan_dense_couplings(couplings: dict, sampling_order, device, precision: str = "bf16"):
+    torch = _torch()
+    pieces = _pieces_of(couplings, precision)
     plans = []
-    for group in program.gibbs_spec.sampling_order:
+    for group in sampling_order:
         bi = int(group[0])
         c = couplings[bi]
         w = np.ascontiguousarray(c["weights_nk"], dtype=np.float32)
@@ -924,9 +992,16 @@ def compile_program(
         state_dtype, plans = "dense_bf16", _plan_dense(program, tdev, config.resolved_dense_precision)
     else:
         lowered = lower_program(program)
-        state_dtype, plans = plan_program(
-            lowered, n_chains, tdev, force_generic=force_generic, spin_layout=config.spin_layout
-        )
+        couplings = None
+        if not force_generic and config.dense_detect and not callable(getattr(program, "tt_stencil", None)):
+            couplings = detect_dense_couplings(lowered, n_chains, round_weights=config.dense_round_weights)
+        if couplings is not None:
+            state_dtype = "dense_bf16"
+            plans = _plan_dense_couplings(couplings, lowered.sampling_order, tdev, config.resolved_dense_precision)
+        else:
+            state_dtype, plans = plan_program(
+                lowered, n_chains, tdev, force_generic=force_generic, spin_layout=config.spin_layout
+            )
     _torch().cuda.synchronize(tdev)  # tables uploaded before any stream uses them
     blocks = tuple(CompiledFusedBlock(spec=s, kernel_artifact=None) for s in lowered.specs)
     groups = tuple(
@@ -960,5 +1035,6 @@ __all__ = [
     "PottsStencilGroupPlan",
     "IsingStencilGroupPlan",
     "IsingResidentGroupPlan",
+    "detect_dense_couplings",
     "ising_pattern_tables",
 ]

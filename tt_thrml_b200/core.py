@@ -53,6 +53,10 @@ class CUDAConfig:
       repeated along K (the float32 field up to summation order); "auto" is
       "fp32" in parity mode and "bf16" in Philox mode.
     stencil: run lattice programs on the stencil kernels (False: their tables).
+    dense_detect: look for dense bipartite structure in lowered programs (an RBM
+      written with thrml factors) and run it on the tensor-core kernel.
+    dense_round_weights: allow that path to round the detected weights to bf16
+      (otherwise only bf16-representable weights qualify).
     """
 
     artifact_root: Path
@@ -63,6 +67,8 @@ class CUDAConfig:
     spin_layout: str = "auto"
     dense_precision: str = "auto"
     stencil: bool = True
+    dense_detect: bool = True
+    dense_round_weights: bool = False
 
     def __post_init__(self) -> None:
         object.__setattr__(self, "artifact_root", Path(self.artifact_root).resolve())
@@ -228,6 +234,8 @@ def make_cuda_config(
     spin_layout: str = "auto",
     dense_precision: str = "auto",
     stencil: bool = True,
+    dense_detect: bool = True,
+    dense_round_weights: bool = False,
 ) -> CUDAConfig:
     """Create a CUDA configuration (the CUDA counterpart of make_ttmlir_config)."""
     root = Path(artifact_root if artifact_root is not None else Path(tempfile.gettempdir()) / "tt-thrml-b200")
@@ -240,6 +248,8 @@ def make_cuda_config(
         spin_layout=spin_layout,
         dense_precision=dense_precision,
         stencil=stencil,
+        dense_detect=dense_detect,
+        dense_round_weights=dense_round_weights,
     )
 
 
