@@ -50,8 +50,8 @@ def test_reference_scenarios_match_oracle(cuda_device, name, mode):
     C = 64
     rep, ex, _ = gh.run_parity(case.program, C, 12, mode=mode, init=_case_init(case, C))
     _assert_parity(rep)
-    if name == "spin":
-        assert ex.compiled.sampling_groups[0].kernel_artifact.kind == "generic"
+    if name == "spin":  # the IsingEBM-style program: two pair interactions per block, merged into one CSR
+        assert ex.compiled.sampling_groups[0].kernel_artifact.kind == "spin_csr"
 
 
 @pytest.mark.parametrize("mode", ["variates", "philox"])

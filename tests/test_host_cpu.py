@@ -410,3 +410,14 @@ def test_dense_structure_is_detected_in_plain_tables():
     assert detect_dense_couplings(lowered2, 128, round_weights=True) is not None
     # a sparse program is not dense
     assert detect_dense_couplings(lower_program(workloads.erdos_renyi_ising(512, 4.0, seed=0)), 128) is None
+
+
+def test_merge_rows_concatenates_terms_row_by_row():
+    from tt_thrml_b200.compiler import _merge_rows
+
+    a = (np.array([0, 2, 2, 3], np.int64), np.array([1.0, 2.0, 3.0], np.float32), np.array([10, 11, 12], np.int32))
+    b = (np.array([0, 1, 3, 3], np.int64), np.array([4.0, 5.0, 6.0], np.float32), np.array([20, 21, 22], np.int32))
+    rp, vals, cols = _merge_rows([a, b], 3)
+    assert rp.tolist() == [0, 3, 5, 6]
+    assert vals.tolist() == [1.0, 2.0, 4.0, 5.0, 6.0, 3.0]
+    assert cols.tolist() == [10, 11, 20, 21, 22, 12]

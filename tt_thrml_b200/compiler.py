@@ -438,12 +438,18 @@ def _validate_sources(spec: FusedBlockSpec, tables, total_nodes: int) -> None:
 
 
 def _group_reads_itself(specs, tables_by_block, total_nodes: int) -> bool:
+    """True when a term with a non-zero weight reads a row of the group (the superblock then needs
+    staging).  Masked terms (all weights zero, e.g. the padding of an interaction's term axis) add an
+    exact zero whatever the state holds, so where they point does not matter."""
     inside = np.zeros(total_nodes, dtype=bool)
     for s in specs:
         inside[s.block_global_start : s.block_global_start + s.n_nodes] = True
     for s in specs:
         for it, rp, w, src in tables_by_block[s.block_index]:
-            if src.size and inside[src].any():
+            if not src.size:
+                continue
+            live = np.any(w != 0.0, axis=1)  # per term
+            if (inside[src] & live[None, :]).any():
                 return True
     return False
 
@@ -464,7 +470,7 @@ def _spin_csr_eligible(specs, tables_by_block, state_dtype: str, n_chains: int) 
                 n_pair += 1
             else:
                 return False
-        if n_bias > 1 or n_pair > 1 or n_bias + n_pair == 0:
+        if n_bias + n_pair == 0:
             return False
     return True
 
@@ -490,16 +496,41 @@ def _sequential_row_sum(rp: np.ndarray, w: np.ndarray) -> np.ndarray:
     return out
 
 
+def _merge_rows(parts, n_rows: int):
+    """Concatenates per-row term lists [(row_ptr, vals, cols), ...] row by row, in the given order."""
+    counts = sum(np.diff(rp) for rp, _, _ in parts)
+    rp_out = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    vals = np.empty(int(rp_out[-1]), dtype=np.float32)
+    cols = np.empty(int(rp_out[-1]), dtype=np.int32)
+    fill = rp_out[:-1].copy()
+    for rp, v, c in parts:
+        cnt = np.diff(rp)
+        dst = np.repeat(fill, cnt) + (np.arange(int(rp[-1]), dtype=np.int64) - np.repeat(rp[:-1], cnt))
+        vals[dst], cols[dst] = v, c
+        fill += cnt
+    return rp_out, vals, cols
+
+
 def _plan_spin_csr(group, specs, tables_by_block, device) -> SpinCSRGroupPlan:
+    """Sparse spin plan.  A block's bias interactions collapse into one per-row bias and its pair
+    interactions into one CSR row per node (terms in program order): with one of each the field is the
+    reference's float32 sum exactly; with several (thrml's IsingEBM gives a block two pair interactions,
+    one per edge side) the grouping of the sum differs by rounding only."""
     blocks = []
     for s in specs:
         bias = None
-        pair = None
+        pairs = []
         for it, rp, w, src in tables_by_block[s.block_index]:
             if src.shape[0] == 0:
-                bias = _sequential_row_sum(rp, w)
+                b = _sequential_row_sum(rp, w)
+                bias = b if bias is None else (bias + b).astype(np.float32)
             else:
-                pair = (rp, w[:, 0], src[0])
+                pairs.append((rp, w[:, 0], src[0]))
+        pair = None
+        if len(pairs) == 1:
+            pair = pairs[0]
+        elif pairs:
+            pair = _merge_rows(pairs, s.n_nodes)
         if pair is None:
             rp = np.zeros(s.n_nodes + 1, dtype=np.int64)
             cols = np.zeros(1, dtype=np.int32)
