@@ -37,12 +37,15 @@ constexpr int kRows = kPottsQ + 1;  // matrix rows per neighbour category, the l
 // spread the random per-lane row reads over all shared-memory banks
 constexpr int kRowFloats = TTHRML_POTTS_ROW_FLOATS;
 
-template <bool VARIATES>
+// QC: the category count as a compile-time constant (8, the common case: no
+// per-category predicates) or 0 (any q <= 8, read from the argument).
+template <bool VARIATES, int QC>
 __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
     int32_t colour, int64_t target_row0, int64_t source_row0, const float* __restrict__ J,
-    const float* __restrict__ bias, int32_t q, int64_t chain_offset, const float* __restrict__ variates,
+    const float* __restrict__ bias, int32_t q_arg, int64_t chain_offset, const float* __restrict__ variates,
     int64_t variates_sweeps, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl) {
+  const int q = QC ? QC : q_arg;
   // P[a][s0][s1][k] = J[a][k][s0] + J[a][k][s1] (float32), with J[a][k][s] = 0
   // for s >= q (rows kPottsQ: categories out of range) and for k >= q
   __shared__ __align__(16) float P[3][kRows][kRows][kRowFloats];
@@ -141,7 +144,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
   }
 }
 
-template <bool VARIATES>
+template <bool VARIATES, int QC>
 int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int32_t colour, int64_t target_row0,
                  int64_t source_row0, const float* J, const float* bias, int32_t q, int64_t chain_offset,
                  const float* variates, int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
@@ -151,7 +154,8 @@ int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int3
     int dev = 0, n = 0, b = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_potts3d<VARIATES>, kPottsThreads, 0);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_potts3d<VARIATES, QC>, kPottsThreads, 0);
     if (e != cudaSuccess) return cuda_status(e, "k_potts3d set-up");
     sms = n;
     per_sm = b > 0 ? b : 1;
@@ -160,7 +164,7 @@ int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int3
   const int64_t need = (items + kPottsThreads - 1) / kPottsThreads;
   const int64_t full = (int64_t)sms * per_sm;
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
-  k_potts3d<VARIATES><<<grid, kPottsThreads, 0, s>>>(state, C, X, Y, Z, make_fastdiv((uint32_t)(C / 4)),
+  k_potts3d<VARIATES, QC><<<grid, kPottsThreads, 0, s>>>(state, C, X, Y, Z, make_fastdiv((uint32_t)(C / 4)),
                                                      make_fastdiv((uint32_t)X), make_fastdiv((uint32_t)Y), colour,
                                                      target_row0, source_row0, J, bias, q, chain_offset, variates,
                                                      variates_sweeps, seed, sweep, ctl);
@@ -198,9 +202,14 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
     return TTHRML_ERR_ARG;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  if (variates)
-    return launch_potts<true>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset,
-                              variates, variates_sweeps, seed, sweep, ctl, s);
-  return launch_potts<false>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset,
-                             variates, variates_sweeps, seed, sweep, ctl, s);
+#define TTHRML_POTTS_LAUNCH(V, QC)                                                                          \
+  return launch_potts<V, QC>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset, \
+                             variates, variates_sweeps, seed, sweep, ctl, s)
+  if (variates) {
+    if (q == kPottsQ) TTHRML_POTTS_LAUNCH(true, kPottsQ);
+    TTHRML_POTTS_LAUNCH(true, 0);
+  }
+  if (q == kPottsQ) TTHRML_POTTS_LAUNCH(false, kPottsQ);
+  TTHRML_POTTS_LAUNCH(false, 0);
+#undef TTHRML_POTTS_LAUNCH
 }
