@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     uint32_t* state, int64_t C, int32_t H, int32_t W, int64_t row0_c0, int64_t row0_c1,
     const uint32_t* __restrict__ thresholds, uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half,
     double* __restrict__ obs, int64_t obs_first, int64_t obs_every, int64_t n_obs, int32_t obs_colours,
-    int64_t chain_offset, const tthrml_run_ctl* __restrict__ ctl) {
+    int64_t chain_offset, const tthrml_run_ctl* __restrict__ ctl, FastDiv div_hw) {
   extern __shared__ __align__(16) unsigned char lat[];  // [2][H][W/2]
   __shared__ uint32_t T[16];
   __shared__ int counts[8];
@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     const unsigned char* other = lat + (1 - c) * half_sites;
     const int64_t row0 = c ? row0_c1 : row0_c0;
     for (int r = threadIdx.x; r < half_sites; r += blockDim.x) {
-      const int Y = r / hw, j = r - Y * hw;
+      const int Y = (int)fdiv((uint32_t)r, div_hw), j = r - Y * hw;
       const int p = (Y + c) & 1;
       const int jl = wrapi(j - 1 + p, hw), jr = wrapi(j + p, hw);
       const int yu = wrapi(Y - 1, H), yd = wrapi(Y + 1, H);
@@ -148,6 +148,6 @@ extern "C" int tthrml_ising2d_resident(uint32_t* state, int64_t n_chains, int32_
   if (n_half_sweeps == 0 && !obs) return TTHRML_OK;
   k_ising2d_resident<<<(unsigned)(n_chains / 8), kResThreads, (size_t)smem, (cudaStream_t)stream>>>(
       state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0, n_half_sweeps,
-      obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl);
+      obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, make_fastdiv((uint32_t)(width / 2)));
   return launch_status("k_ising2d_resident launch");
 }
