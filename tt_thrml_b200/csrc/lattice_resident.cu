@@ -11,10 +11,11 @@
 // byte per site in shared memory, [2 colours][H][W/2] bytes.
 //
 // Decision: the four neighbour bytes (left, right, up, down) of a site form
-// a word N whose bit 8k + v is neighbour k of chain v; chain v's 4-bit
-// pattern is gathered with one multiply, (((N >> v) & 0x01010101) *
-// 0x01020408) >> 24, and decides against the exact integer threshold of the
-// pattern's float32 field (as in csrc/ising2d.cu).  Philox counter: (chain/4,
+// a word N whose bit 8k + v is neighbour k of chain v; a bit-matrix transpose
+// of N (the 8x8 transpose of Warren, "Hacker's Delight" 7-3, with the upper
+// four rows zero) turns it into one 4-bit sign pattern per chain, which decides
+// against the exact integer threshold of the pattern's float32 field (as in
+// csrc/ising2d.cu).  Philox counter: (chain/4,
 // flat row, sweep, "SPIN"), word chain % 4 -- the sparse spin kernels' layout.
 #include "common.cuh"
 
@@ -68,10 +69,18 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
       const u32x4 a = philox4x32_10(u32x4{gc0 >> 2, row, sweep, kSaltSpin}, keys);
       const u32x4 b = philox4x32_10(u32x4{(gc0 >> 2) + 1u, row, sweep, kSaltSpin}, keys);
       const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      // transpose: byte v of (lo, hi) = chain v's pattern (bit k = neighbour k is -1)
+      uint32_t lo = N, t;
+      t = (lo ^ (lo >> 7)) & 0x00AA00AAu;
+      lo = lo ^ t ^ (t << 7);
+      t = (lo ^ (lo >> 14)) & 0x0000CCCCu;
+      lo = lo ^ t ^ (t << 14);
+      const uint32_t hi = (lo >> 4) & 0x0F0F0F0Fu;
+      lo &= 0x0F0F0F0Fu;
       uint32_t down = 0u;
 #pragma unroll
       for (int v = 0; v < 8; ++v) {
-        const uint32_t idx = ((((N >> v) & 0x01010101u) * 0x01020408u) >> 24) & 0xFu;
+        const uint32_t idx = __byte_perm(v < 4 ? lo : hi, 0u, 0x4440u + (v & 3));
         down |= ((w[v] >> 9) < T[idx] ? 0u : 1u) << v;
       }
       mine[r] = (unsigned char)down;
