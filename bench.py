@@ -103,7 +103,7 @@ class ErIsing:
         peak, kind = _peaks()["hbm"]
         traffic = _traffic_per_launch(sum(per_block) / len(per_block)) if layout == "bits" else None
         return {
-            "kernel": "k_spin_bits" if layout == "bits" else "k_spin_csr_async",
+            "kernel": "k_spin_bits16" if layout == "bits" else "k_spin_csr_async",
             "bound": "hbm",
             "achieved": achieved,
             "peak": peak,

@@ -216,7 +216,18 @@ int launch_bits(const int64_t* rp, const int32_t* cols, const float* vals, const
 }
 
 }  // namespace
+
+// 16 chains per lane (spin_bits16.cu)
+template <bool VARIATES>
+int launch_bits16(const int64_t* rp, const int32_t* cols, const float* vals, const float* bias, int64_t row_start,
+                  int64_t n_rows, uint32_t* state, int64_t W, int64_t chain_offset, const float* variates,
+                  int64_t variates_sweeps, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, cudaStream_t s);
+
 }  // namespace tthrml
+
+#ifndef TTHRML_BITS16
+#define TTHRML_BITS16 1
+#endif
 
 extern "C" int tthrml_spin_bits_step(const int64_t* row_ptr, const int32_t* cols, const float* vals,
                                      const float* bias, int64_t row_start, int64_t n_rows, uint32_t* state,
@@ -240,6 +251,13 @@ extern "C" int tthrml_spin_bits_step(const int64_t* row_ptr, const int32_t* cols
   }
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t W = n_chains / 32;
+  if (TTHRML_BITS16) {
+    if (variates)
+      return launch_bits16<true>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
+                                 variates_sweeps, seed, sweep, ctl, s);
+    return launch_bits16<false>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
+                                variates_sweeps, seed, sweep, ctl, s);
+  }
   if (variates)
     return launch_bits<true>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
                              variates_sweeps, seed, sweep, ctl, s);
