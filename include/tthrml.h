@@ -231,10 +231,13 @@ int tthrml_potts3d_step(int8_t* state_dev, int64_t n_chains, int32_t X, int32_t 
  * down neighbours are local rows i-1 and i+1 (halo rows of a strip), or wrap
  * around when wrap_rows is set (rows_local == height, the whole lattice).
  * The decision uses the 4 neighbour signs (left, right, up, down; bit set =
- * -1) as an index into thresholds[16] (Philox: "up" iff (bits >> 9) <
+ * -1) as an index into thresholds[16] (Philox: "up" iff the 23-bit draw m <
  * threshold) or fields[16] (variates: "up" iff 2 * field > logit, variates
- * [variates_sweeps][height * width/2] per colour block).  Philox counter
- * (chain, (block_row0 + Y*width/2 + x/2) / 4, sweep, "DSPI").  trace (NULL to
+ * [variates_sweeps][height * width/2] per colour block).  Philox draws are
+ * split uniforms: with flat row f = block_row0 + Y*width/2 + x/2, the top 16
+ * bits of m are half f % 2 of word (f / 2) % 4 of counter (chain, f / 8,
+ * sweep, "LSPI"), the low 7 bits word 0 >> 25 of (chain, f, sweep, "LREF"),
+ * read only when the top bits equal the threshold's.  trace (NULL to
  * skip): int64 [trace_len][2]; entry `sweep` receives the sum of the new
  * spins of local rows [count_lo, count_hi) and, for colour 1, the bond sum
  * sum_i s_i (s_left + s_right + s_up + s_down) over them.  Requires width %
@@ -257,8 +260,9 @@ int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, in
  * [rows][n_chains/32] (bit set = -1) with colour c's site (Y, x) at row
  * row0_colour_c + Y*width/2 + x/2.  Decision as tthrml_ising2d_halfsweep
  * (16-entry threshold table over the left/right/up/down sign pattern);
- * Philox counter (chain/4, row, sweep, "SPIN"), word chain % 4 (the sparse
- * spin kernels' layout).  obs_dev (NULL: none): float64 [n_obs][n_chains],
+ * split-uniform Philox draws: top 16 bits half chain % 2 of word (chain / 2)
+ * % 4 of counter (chain / 8, row, sweep, "LSPI"), low 7 bits word 0 >> 25 of
+ * (chain, row, sweep, "LREF").  obs_dev (NULL: none): float64 [n_obs][n_chains],
  * sample i = per-chain sum of the spins of the colours in obs_colours (bit
  * mask) after half-sweep obs_first + i * obs_every.  A thrml schedule with
  * its magnetisation observable is one launch.  Requires n_chains % 32 == 0,

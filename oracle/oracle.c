@@ -50,8 +50,14 @@ typedef struct {
 
 /* rng_layout 0: counter (chain/4, row, sweep), word chain % 4, as the sparse,
  * generic and Potts kernels draw; 1: counter (chain, row/4, sweep), word
- * row % 4, as the dense tensor-core kernel and the 2-D lattice stencil kernel
- * draw (four consecutive rows of one chain per counter) */
+ * row % 4, as the dense tensor-core kernel draws (four consecutive rows of one
+ * chain per counter).  Layouts 2 and 3 are the lattice kernels' split
+ * uniforms (spin blocks): the 23-bit draw m = (h << 7) | f with h = 16 bits
+ * of a shared counter "LSPI" and f = word 0 >> 25 of the draw's own counter
+ * (chain, row, sweep, "LREF"); 2: counter (chain, row/8, sweep), half row % 2
+ * of word (row/2) % 4 (the single-chain lattice stencil kernel); 3: counter
+ * (chain/8, row, sweep), half chain % 2 of word (chain/2) % 4 (the
+ * shared-memory resident lattice kernel). */
 typedef struct {
   int32_t family, q, n_interactions, rng_layout;
   int64_t n_nodes, row_start;
@@ -86,8 +92,19 @@ void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t
 
 static const uint32_t SALT_SPIN = 0x5350494eu, SALT_GAUSS = 0x47415553u, SALT_CAT = 0x43415400u;
 static const uint32_t SALT_DENSE_SPIN = 0x44535049u, SALT_DENSE_GAUSS = 0x44474155u;
+static const uint32_t SALT_LATTICE_SPIN = 0x4C535049u, SALT_LATTICE_REFILL = 0x4C524546u;
 
 static double or_uniform(uint32_t bits) { return (double)((((bits >> 9) << 1) | 1u)) * 5.9604644775390625e-08; }
+
+/* the 23-bit split-uniform draw of rng layouts 2 and 3, as the top 23 bits of a word */
+static uint32_t or_split_bits(int layout, int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
+  const int64_t pos = layout == 2 ? row : gc;
+  const or_u32x4 r = layout == 2 ? or_philox((uint32_t)gc, (uint32_t)(row >> 3), sweep, SALT_LATTICE_SPIN, k0, k1)
+                                 : or_philox((uint32_t)(gc >> 3), (uint32_t)row, sweep, SALT_LATTICE_SPIN, k0, k1);
+  const uint32_t h = (r.v[(pos >> 1) & 3] >> (16 * (pos & 1))) & 0xFFFFu;
+  const uint32_t f = or_philox((uint32_t)gc, (uint32_t)row, sweep, SALT_LATTICE_REFILL, k0, k1).v[0] >> 25;
+  return ((h << 7) | f) << 9;
+}
 
 static double or_logit(double p) { return log(p) - log1p(-p); }
 
@@ -240,9 +257,14 @@ static void* run_rows(void* arg) {
           m = (double)two_g - (double)l;
         } else {
           const int dense = B->rng_layout == 1;
-          const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 2), t->sweep, SALT_DENSE_SPIN, t->k0, t->k1)
-                                   : or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_SPIN, t->k0, t->k1);
-          const double u = or_uniform(r.v[dense ? (row & 3) : (gc & 3)]);
+          double u;
+          if (B->rng_layout == 2 || B->rng_layout == 3) {
+            u = or_uniform(or_split_bits(B->rng_layout, gc, row, t->sweep, t->k0, t->k1));
+          } else {
+            const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 2), t->sweep, SALT_DENSE_SPIN, t->k0, t->k1)
+                                     : or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_SPIN, t->k0, t->k1);
+            u = or_uniform(r.v[dense ? (row & 3) : (gc & 3)]);
+          }
           const double l = log(u) - log1p(-u);
           m = (double)two_g - l;
           v = m > 0.0 ? 1.0f : -1.0f;

@@ -316,12 +316,15 @@ class OracleSampler:
         every block or a dict block index -> name.  "chain4": counter (chain/4,
         row, sweep), word chain % 4 (the sparse, generic and Potts kernels);
         "row4": counter (chain, row/4, sweep), word row % 4 (the tensor-core
-        dense kernel and the 2-D lattice stencil kernel)."""
-        names = {"chain4": 0, "row4": 1}
+        dense kernel); "row8s" / "chain8s": the lattice kernels' split uniforms
+        (spin blocks: 16 bits of counter (chain, row/8, sweep) resp.
+        (chain/8, row, sweep), "LSPI", and 7 refill bits of (chain, row, sweep),
+        "LREF"; the single-chain stencil and the resident lattice kernel)."""
+        names = {"chain4": 0, "row4": 1, "row8s": 2, "chain8s": 3}
         layouts = rng_layout if isinstance(rng_layout, dict) else None
         for v in (layouts.values() if layouts is not None else [rng_layout]):
             if v not in names:
-                raise ValueError(f"rng_layout must be 'chain4' or 'row4', got {v!r}")
+                raise ValueError(f"rng_layout must be one of {sorted(names)}, got {v!r}")
         self._rng_layout = {int(k): names[v] for k, v in layouts.items()} if layouts is not None else {}
         self._rng_default = 0 if layouts is not None else names[rng_layout]
         self.prog = program if isinstance(program, OProgram) else lower_program(program)

@@ -3,9 +3,11 @@
 Mirrors tthrml_ising2d_halfsweep on numpy arrays so the strip decomposition
 of tt_thrml_b200.domain can be checked on CPU ranks (gloo): split-colour
 int8 arrays [rows][W/2], neighbour-sign pattern (left, right, up, down), the
-pattern's Philox threshold, counter (chain, flat row / 4, sweep, "DSPI"),
-word flat row % 4.  It is itself checked against the oracle (the reference's
-group math on the lattice's per-edge tables) in test_domain_cpu.py.
+pattern's Philox threshold and the split-uniform draw: top 16 bits from
+counter (chain, flat row / 8, sweep, "LSPI"), half flat row % 2 of word
+(flat row / 2) % 4, low 7 bits from (chain, flat row, sweep, "LREF") word 0.
+It is itself checked against the oracle (the reference's group math on the
+lattice's per-edge tables) in test_domain_cpu.py.
 """
 
 from __future__ import annotations
@@ -13,7 +15,8 @@ from __future__ import annotations
 import numpy as np
 
 M32 = np.uint64(0xFFFFFFFF)
-SALT_DENSE_SPIN = 0x44535049
+SALT_LATTICE_SPIN = 0x4C535049
+SALT_LATTICE_REFILL = 0x4C524546
 
 
 def philox4x32_10(c0, c1, c2, c3, k0: int, k1: int):
@@ -49,10 +52,14 @@ def make_halfsweep(strips, *, chain: int = 0):
         dnv = co[rows + 1].astype(np.int64)
         idx = (left < 0) * 1 + (right < 0) * 2 + (upv < 0) * 4 + (dnv < 0) * 8
         flat = strips.block_rows[colour] + Y[:, None] * hw + j
-        words = philox4x32_10(np.full(flat.shape, chain), flat >> 2, np.full(flat.shape, sweep),
-                              np.full(flat.shape, SALT_DENSE_SPIN), strips.seed & 0xFFFFFFFF, strips.seed >> 32)
-        w = np.choose((flat & 3).astype(np.int64), words)
-        up = (w >> np.uint64(9)).astype(np.int64) < thr[idx]
+        k0, k1 = strips.seed & 0xFFFFFFFF, strips.seed >> 32
+        cs, ss = np.full(flat.shape, chain), np.full(flat.shape, sweep)
+        words = philox4x32_10(cs, flat >> 3, ss, np.full(flat.shape, SALT_LATTICE_SPIN), k0, k1)
+        w = np.choose(((flat >> 1) & 3).astype(np.int64), words)
+        h = (w >> (np.uint64(16) * (flat & 1).astype(np.uint64))) & np.uint64(0xFFFF)
+        f = philox4x32_10(cs, flat, ss, np.full(flat.shape, SALT_LATTICE_REFILL), k0, k1)[0] >> np.uint64(25)
+        m = ((h << np.uint64(7)) | f).astype(np.int64)
+        up = m < thr[idx]
         new = np.where(up, 1, -1).astype(np.int8)
         cc[rows] = new
         # observables of the counted rows

@@ -171,3 +171,50 @@ def test_oracle_dense_rng_layout_differs_from_site_layout():
     assert not np.array_equal(res[0], res[1])
     with pytest.raises(ValueError):
         orc.OracleSampler(prog, n_chains=8, rng_layout="tiles")
+
+
+def test_oracle_split_uniform_lattice_layouts():
+    """The oracle's split-uniform lattice draws ("row8s", "chain8s") follow their counters:
+    a numpy restatement of one colour half-sweep (neighbour-sign pattern, exact threshold,
+    23-bit draw = 16 shared bits << 7 | 7 refill bits) gives the same states."""
+    import numpy as np
+
+    import ising_ref
+    from tt_thrml_b200 import workloads
+    from tt_thrml_b200.compiler import ising_pattern_tables
+
+    H, W, C, seed, sweep = 8, 16, 16, 0x0123456789ABCDEF, 5
+    prog = workloads.IsingLattice2D(H, W, beta=0.4407)
+    st = prog.tt_stencil()
+    _, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
+    rng = np.random.default_rng(5)
+    lat = rng.choice(np.array([-1, 1], np.int8), size=(C, H, W))
+    blocks = []
+    for c in range(2):
+        ys, xs = np.nonzero(((np.arange(H)[:, None] + np.arange(W)[None, :]) & 1) == c)
+        blocks.append(lat[:, ys, xs] > 0)
+    k0, k1 = seed & 0xFFFFFFFF, seed >> 32
+    for layout in ("row8s", "chain8s"):
+        o = orc.OracleSampler(prog, n_chains=C, rng_layout=layout)
+        o.load_state(blocks)
+        o.group_step(0, sweep, seed=seed)
+        got = o.state[: H * W // 2].T > 0  # [C][rows] of colour 0
+        ys, xs = np.nonzero(((np.arange(H)[:, None] + np.arange(W)[None, :]) & 1) == 0)
+        s = lat.astype(np.int64)
+        idx = ((s[:, ys, (xs - 1) % W] < 0) * 1 + (s[:, ys, (xs + 1) % W] < 0) * 2
+               + (s[:, (ys - 1) % H, xs] < 0) * 4 + (s[:, (ys + 1) % H, xs] < 0) * 8)
+        row = np.broadcast_to(np.arange(len(ys))[None, :], (C, len(ys))).astype(np.uint64)
+        gc = np.broadcast_to(np.arange(C)[:, None], (C, len(ys))).astype(np.uint64)
+        sw = np.full(row.shape, sweep, np.uint64)
+        if layout == "row8s":
+            words = ising_ref.philox4x32_10(gc, row >> np.uint64(3), sw, np.full(row.shape, 0x4C535049), k0, k1)
+            pos = row
+        else:
+            words = ising_ref.philox4x32_10(gc >> np.uint64(3), row, sw, np.full(row.shape, 0x4C535049), k0, k1)
+            pos = gc
+        w = np.choose(((pos >> np.uint64(1)) & np.uint64(3)).astype(np.int64), words)
+        h = (w >> (np.uint64(16) * (pos & np.uint64(1)))) & np.uint64(0xFFFF)
+        f = ising_ref.philox4x32_10(gc, row, sw, np.full(row.shape, 0x4C524546), k0, k1)[0] >> np.uint64(25)
+        m = ((h << np.uint64(7)) | f).astype(np.int64)
+        want = m < thr.astype(np.int64)[idx]
+        np.testing.assert_array_equal(got, want)

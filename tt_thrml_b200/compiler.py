@@ -863,6 +863,8 @@ class IsingResidentGroupPlan:
     in_place: bool = True
     group_rows: int = 0
     device: Any = None
+    # split uniforms: 16 bits of counter (chain / 8, row, sweep, "LSPI") + 7 refill bits
+    rng_layout: str = "chain8s"
 
 
 @dataclass
@@ -882,7 +884,8 @@ class IsingStencilGroupPlan:
     in_place: bool = True
     group_rows: int = 0
     device: Any = None
-    rng_layout: str = "row4"  # Philox counter (chain, row / 4, sweep), word row % 4
+    # split uniforms: 16 bits of counter (chain, row / 8, sweep, "LSPI") + 7 refill bits
+    rng_layout: str = "row8s"
 
 
 def ising_pattern_tables(edge_weight, site_bias) -> tuple[np.ndarray, np.ndarray]:
@@ -892,8 +895,8 @@ def ising_pattern_tables(edge_weight, site_bias) -> tuple[np.ndarray, np.ndarray
     -1.  field = b + (((w s_0 + w s_1) + w s_2) + w s_3) in float32 -- the
     bias interaction first, then the pair interaction summed over its terms
     (tt_thrml/compiler.py:303-318).  threshold = ceil((sigmoid(2 field) 2^24 -
-    1) / 2): with u = (2m + 1) / 2^24 the Philox uniform of m = bits >> 9,
-    u < sigmoid(2 field) exactly when m < threshold.
+    1) / 2): with u = (2m + 1) / 2^24 the Philox uniform of the 23-bit draw
+    m, u < sigmoid(2 field) exactly when m < threshold.
     """
     w, b = np.float32(edge_weight), np.float32(site_bias)
     fields = np.empty(16, np.float32)

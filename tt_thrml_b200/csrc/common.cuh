@@ -35,6 +35,15 @@ constexpr uint32_t kSaltCat = 0x43415400u;       // "CAT\0"
 // (chain, row/2, sweep, salt) the two uniforms of two gaussian rows.
 constexpr uint32_t kSaltDenseSpin = 0x44535049u;   // "DSPI"
 constexpr uint32_t kSaltDenseGauss = 0x44474155u;  // "DGAU"
+// Lattice (threshold-table) spin draws use split uniforms: the 23-bit draw
+// m = (h << 7) | f takes its top 16 bits h from a counter shared by eight
+// draws (two per 32-bit word: low half first) and its low 7 bits f from a
+// counter of its own, (chain, row, sweep, "LREF") word 0 >> 25.  A draw
+// compares h with the threshold's top 16 bits first and needs f only when
+// they are equal (probability 2^-16), so a lattice site costs an eighth of a
+// Philox call instead of a quarter; m is uniform on [0, 2^23) as before.
+constexpr uint32_t kSaltLatticeSpin = 0x4C535049u;    // "LSPI"
+constexpr uint32_t kSaltLatticeRefill = 0x4C524546u;  // "LREF"
 
 struct u32x4 {
   uint32_t x, y, z, w;
@@ -128,6 +137,15 @@ __host__ __device__ __forceinline__ uint32_t seed_lo(uint64_t s) { return (uint3
 __host__ __device__ __forceinline__ uint32_t seed_hi(uint64_t s) { return (uint32_t)(s >> 32); }
 
 #ifdef __CUDACC__
+// PTX prmt in its default mode: each selector nibble picks one of the eight
+// bytes of {b, a} (low 3 bits); with the nibble's top bit set the picked
+// byte's sign bit is replicated over the result byte.
+__device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
 // Categorical draw in Philox mode by inverse CDF from one uniform u, a sample
 // of softmax(theta): e_k = 2^((theta_k - max theta) * log2 e) (ex2.approx),
 // and the draw is the number of boundaries k < q - 1 that u reaches,

@@ -13,13 +13,16 @@
 // right neighbours at other-colour columns j-1+p and j+p.  The four sign bits
 // (left, right, up, down: the reference lattice's neighbour order) index a
 // 16-entry table built on the host from the program's float32 weights:
-//   Philox mode: threshold T with "up" iff (bits >> 9) < T, the exact integer
-//     form of u < sigmoid(2 * gamma) for u = (2 (bits >> 9) + 1) / 2^24;
+//   Philox mode: threshold T with "up" iff m < T, the exact integer form of
+//     u < sigmoid(2 * gamma) for the 23-bit draw m, u = (2 m + 1) / 2^24;
 //   variates mode: the float32 field gamma, "up" iff 2 * gamma > logit.
 // gamma is the left-to-right float32 sum of the bias interaction and the
 // pair terms (tt_thrml/compiler.py:303-324), so both modes decide as the
-// table-driven kernels do.  Philox counter: (chain, flat row / 4, sweep,
-// "DSPI"), word flat row % 4 -- four consecutive sites of a row per call.
+// table-driven kernels do.  Philox draws are split uniforms (common.cuh):
+// the top 16 bits of m from counter (chain, flat row / 8, sweep, "LSPI"),
+// half (flat row % 2) of word (flat row / 2) % 4 -- eight consecutive sites
+// of a row per call -- and the low 7 bits from the per-site refill counter,
+// read only when the top bits tie with the threshold's.
 //
 // Observables (optional, for the energy/magnetisation trace): the sum of the
 // new spins over the counted rows, and in the colour-1 half-sweep the bond
@@ -31,11 +34,14 @@ namespace tthrml {
 namespace {
 
 constexpr int kIsingThreads = 256;
+#ifndef TTHRML_ISING_MIN_BLOCKS
+#define TTHRML_ISING_MIN_BLOCKS 3
+#endif
 
 __device__ __forceinline__ uint4 ld16(const int8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 template <bool VARIATES, bool TRACE>
-__global__ void __launch_bounds__(kIsingThreads) k_ising2d(
+__global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_MIN_BLOCKS) k_ising2d(
     int8_t* __restrict__ cc, const int8_t* __restrict__ co, int64_t half_w, FastDiv div_chunks, int64_t rows_local,
     int32_t wrap,
     int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
@@ -43,14 +49,18 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
     int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl,
     int64_t count_lo, int64_t count_hi, unsigned long long* __restrict__ trace, int64_t trace_len,
     tthrml_halo_export ex) {
-  __shared__ uint32_t T[16];
+  __shared__ int32_t TH[16];   // threshold >> 7: compared with the draw's top 16 bits
+  __shared__ uint32_t TL[16];  // threshold & 127: compared with the refill bits on a tie
   __shared__ float F[16];
   __shared__ long long red[2];
   if (threadIdx.x < 16) {
-    if (VARIATES)
+    if (VARIATES) {
       F[threadIdx.x] = fields[threadIdx.x];
-    else
-      T[threadIdx.x] = thresholds[threadIdx.x];
+    } else {
+      const uint32_t t = thresholds[threadIdx.x];
+      TH[threadIdx.x] = (int32_t)(t >> 7);
+      TL[threadIdx.x] = t & 127u;
+    }
   }
   if (TRACE && threadIdx.x < 2) red[threadIdx.x] = 0;
   __syncthreads();
@@ -84,8 +94,9 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
     const uint32_t uw[4] = {up.x, up.y, up.z, up.w};
     const uint32_t dw[4] = {dn.x, dn.y, dn.z, dn.w};
 
-    const int64_t flat0 = block_row0 + Y * half_w + j0;  // flat row of the first site
+    const int64_t flat0 = block_row0 + Y * half_w + j0;  // flat row of the first site (a multiple of 16)
     uint32_t outw[4];
+    u32x4 rr{0u, 0u, 0u, 0u};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       // neighbour words of sites 4k..4k+3
@@ -93,29 +104,50 @@ __global__ void __launch_bounds__(kIsingThreads) k_ising2d(
       const uint32_t R = p ? __byte_perm(m[k + 1], m[k + 2], 0x4321u) : m[k + 1];
       const uint32_t idx4 = ((L >> 7) & 0x01010101u) | ((R >> 6) & 0x02020202u) | ((uw[k] >> 5) & 0x04040404u) |
                             ((dw[k] >> 4) & 0x08080808u);
-      uint32_t minus = 0u;  // bit 8v set: site 4k+v samples -1
+      uint32_t minus = 0u;  // byte v 0xFF: site 4k+v samples -1, 0x00: +1
       if (VARIATES) {
         const float* lrow = variates + vs * (height * half_w) + (flat0 - block_row0) + 4 * k;
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           const float g = F[(idx4 >> (8 * v)) & 0xFu];
-          minus |= (__fmul_rn(2.0f, g) > __ldg(lrow + v) ? 0u : 1u) << (8 * v);
+          minus |= (__fmul_rn(2.0f, g) > __ldg(lrow + v) ? 0u : 0xFFu) << (8 * v);
         }
       } else {
         const int64_t flat = flat0 + 4 * k;
-        const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, (uint32_t)(flat >> 2), sweep, kSaltDenseSpin}, keys);
+        if ((k & 1) == 0)
+          rr = philox4x32_10(u32x4{(uint32_t)chain, (uint32_t)(flat >> 3), sweep, kSaltLatticeSpin}, keys);
+        int32_t a[4];  // threshold top bits - draw top bits: > 0 up, < 0 down, 0 tie
+        bool tie = false;
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-          minus |= ((word_of(r, v) >> 9) < T[(idx4 >> (8 * v)) & 0xFu] ? 0u : 1u) << (8 * v);
+        for (int v = 0; v < 4; ++v) {
+          const uint32_t wv = word_of(rr, 2 * (k & 1) + (v >> 1));
+          const int32_t h = (int32_t)((v & 1) ? (wv >> 16) : (wv & 0xFFFFu));
+          a[v] = TH[(idx4 >> (8 * v)) & 0xFu] - h;
+          tie |= a[v] == 0;
+        }
+        // byte v = the sign of a[v] replicated (0xFF when the site goes down)
+        minus = prmt_sign(prmt_sign((uint32_t)a[0], (uint32_t)a[1], 0xFFFBu),
+                          prmt_sign((uint32_t)a[2], (uint32_t)a[3], 0xFFFBu), 0x5410u);
+        if (tie) {  // rare: decide the tied sites on their refill bits
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (a[v] == 0) {
+              const uint32_t f =
+                  philox4x32_10(u32x4{(uint32_t)chain, (uint32_t)(flat + v), sweep, kSaltLatticeRefill}, keys).x >> 25;
+              const bool up = f < TL[(idx4 >> (8 * v)) & 0xFu];
+              minus = (minus & ~(0xFFu << (8 * v))) | ((up ? 0u : 0xFFu) << (8 * v));
+            }
+          }
+        }
       }
-      outw[k] = 0x01010101u + minus * 0xFEu;  // +1 -> 0x01, -1 -> 0xFF per byte
+      outw[k] = minus | 0x01010101u;  // +1 -> 0x01, -1 -> 0xFF per byte
       if (TRACE && i >= count_lo && i < count_hi) {
-        const int nm = __popc(minus);
+        const int nm = __popc(minus) >> 3;
         mag += 4 - 2 * nm;
         if (colour == 1) {
           // sum_v s_v * n_v with n_v = 4 - 2 k_v (k_v minus neighbours), s_v = 1 - 2 m_v
           const int ksum = __popc(idx4);
-          const int mk = __popc(idx4 & (minus * 0x0Fu));
+          const int mk = __popc(idx4 & minus);
           bonds += 4 * (4 - 2 * nm) - 2 * ksum + 4 * mk;
         }
       }

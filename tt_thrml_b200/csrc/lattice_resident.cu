@@ -15,8 +15,10 @@
 // of N (the 8x8 transpose of Warren, "Hacker's Delight" 7-3, with the upper
 // four rows zero) turns it into one 4-bit sign pattern per chain, which decides
 // against the exact integer threshold of the pattern's float32 field (as in
-// csrc/ising2d.cu).  Philox counter: (chain/4,
-// flat row, sweep, "SPIN"), word chain % 4 -- the sparse spin kernels' layout.
+// csrc/ising2d.cu).  Philox draws are split uniforms (common.cuh): the top 16
+// bits of chain c's draw come from counter (c / 8, flat row, sweep, "LSPI"),
+// half c % 2 of word (c / 2) % 4 -- one call for the CTA's 8 chains of a site
+// -- and the low 7 bits from the refill counter, read only on a tie.
 #include "common.cuh"
 
 namespace tthrml {
@@ -32,14 +34,18 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     double* __restrict__ obs, int64_t obs_first, int64_t obs_every, int64_t n_obs, int32_t obs_colours,
     int64_t chain_offset, const tthrml_run_ctl* __restrict__ ctl, FastDiv div_hw) {
   extern __shared__ __align__(16) unsigned char lat[];  // [2][H][W/2]
-  __shared__ uint32_t T[16];
+  __shared__ int32_t TH[16];   // threshold >> 7: compared with a draw's top 16 bits
+  __shared__ uint32_t TL[16];  // threshold & 127: compared with the refill bits on a tie
   __shared__ int counts[8];
   const int hw = W >> 1;
   const int half_sites = H * hw;
   const int g = blockIdx.x;  // chain group
   const int64_t words = C >> 5;
   const int word = g >> 2, byte_in_word = g & 3;
-  if (threadIdx.x < 16) T[threadIdx.x] = thresholds[threadIdx.x];
+  if (threadIdx.x < 16) {
+    TH[threadIdx.x] = (int32_t)(thresholds[threadIdx.x] >> 7);
+    TL[threadIdx.x] = thresholds[threadIdx.x] & 127u;
+  }
   for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
     const int c = i / half_sites, r = i - c * half_sites;
     const int64_t row = (c ? row0_c1 : row0_c0) + r;
@@ -66,9 +72,8 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
       const uint32_t N = (uint32_t)other[Y * hw + jl] | ((uint32_t)other[Y * hw + jr] << 8) |
                          ((uint32_t)other[yu * hw + j] << 16) | ((uint32_t)other[yd * hw + j] << 24);
       const uint32_t row = (uint32_t)(row0 + r);
-      const u32x4 a = philox4x32_10(u32x4{gc0 >> 2, row, sweep, kSaltSpin}, keys);
-      const u32x4 b = philox4x32_10(u32x4{(gc0 >> 2) + 1u, row, sweep, kSaltSpin}, keys);
-      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      const u32x4 a = philox4x32_10(u32x4{gc0 >> 3, row, sweep, kSaltLatticeSpin}, keys);
+      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
       // transpose: byte v of (lo, hi) = chain v's pattern (bit k = neighbour k is -1)
       uint32_t lo = N, t;
       t = (lo ^ (lo >> 7)) & 0x00AA00AAu;
@@ -78,10 +83,25 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
       const uint32_t hi = (lo >> 4) & 0x0F0F0F0Fu;
       lo &= 0x0F0F0F0Fu;
       uint32_t down = 0u;
+      int32_t d[8];  // threshold top bits - draw top bits: > 0 up, < 0 down, 0 tie
+      bool tie = false;
 #pragma unroll
       for (int v = 0; v < 8; ++v) {
         const uint32_t idx = __byte_perm(v < 4 ? lo : hi, 0u, 0x4440u + (v & 3));
-        down |= ((w[v] >> 9) < T[idx] ? 0u : 1u) << v;
+        const int32_t h = (int32_t)((v & 1) ? (w[v >> 1] >> 16) : (w[v >> 1] & 0xFFFFu));
+        d[v] = TH[idx] - h;
+        down |= ((uint32_t)d[v] >> 31) << v;
+        tie |= d[v] == 0;
+      }
+      if (tie) {  // rare: decide the tied chains on their refill bits
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          if (d[v] == 0) {
+            const uint32_t idx = __byte_perm(v < 4 ? lo : hi, 0u, 0x4440u + (v & 3));
+            const uint32_t f = philox4x32_10(u32x4{gc0 + v, row, sweep, kSaltLatticeRefill}, keys).x >> 25;
+            if (f >= TL[idx]) down |= 1u << v;
+          }
+        }
       }
       mine[r] = (unsigned char)down;
     }
