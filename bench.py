@@ -488,7 +488,7 @@ def run_ising(args, W):
                 "final_magnetisation_per_site": float(em[-1, 1]),
             },
             "roofline": {
-                "kernel": "k_ising2d",
+                "kernel": "k_ising2d_planes" if st.rng_layout == "planes" else "k_ising2d",
                 "bound": "hbm",
                 "achieved": achieved,
                 "peak": peak,

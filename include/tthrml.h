@@ -303,6 +303,24 @@ int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* other_state, 
                                const tthrml_halo_export* export_host, void* stream);
 
 /*
+ * tthrml_ising2d_halfsweep_x for count-symmetric threshold tables (thresholds
+ * equal for patterns with the same number of -1 neighbours; the kernel reads
+ * thresholds[2^n - 1] for n = 0..4), Philox mode, bit-sliced over 32 sites.
+ * Random bits ("planes"): bit 22 - b of the 23-bit draw of flat row f is bit
+ * 8 (f % 4) + (f % 32) / 4 of word b % 4 of counter (chain, f / 32, sweep,
+ * "LPL0" + b / 4).  Requires width % 64 == 0 and block_row0 % 32 == 0.
+ * Replaces the same reference group call as tthrml_ising2d_halfsweep
+ * (tt_thrml/compiler.py:436-450) for uniform lattices.
+ */
+int tthrml_ising2d_halfsweep_planes(int8_t* colour_state, const int8_t* other_state, int64_t width,
+                                    int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                    int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                    const uint32_t* thresholds_dev, int64_t chain, uint64_t seed, uint32_t sweep,
+                                    const tthrml_run_ctl* ctl_dev, int64_t count_lo, int64_t count_hi,
+                                    int64_t* trace_dev, int64_t trace_len, const tthrml_halo_export* export_host,
+                                    void* stream);
+
+/*
  * Peer memory for the halo mailboxes: tthrml_ipc_malloc allocates zeroed
  * device memory and writes its 64-byte CUDA IPC handle to `handle_host`;
  * another process opens it with tthrml_ipc_open (peer access enabled on

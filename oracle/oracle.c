@@ -57,7 +57,9 @@ typedef struct {
  * (chain, row, sweep, "LREF"); 2: counter (chain, row/8, sweep), half row % 2
  * of word (row/2) % 4 (the single-chain lattice stencil kernel); 3: counter
  * (chain/8, row, sweep), half chain % 2 of word (chain/2) % 4 (the
- * shared-memory resident lattice kernel). */
+ * shared-memory resident lattice kernel).  Layout 4 ("planes", the bit-sliced
+ * lattice kernel): bit 22 - b of m is bit 8 (row % 4) + (row % 32) / 4 of word
+ * b % 4 of counter (chain, row / 32, sweep, "LPL0" + b / 4). */
 typedef struct {
   int32_t family, q, n_interactions, rng_layout;
   int64_t n_nodes, row_start;
@@ -93,8 +95,23 @@ void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t
 static const uint32_t SALT_SPIN = 0x5350494eu, SALT_GAUSS = 0x47415553u, SALT_CAT = 0x43415400u;
 static const uint32_t SALT_DENSE_SPIN = 0x44535049u, SALT_DENSE_GAUSS = 0x44474155u;
 static const uint32_t SALT_LATTICE_SPIN = 0x4C535049u, SALT_LATTICE_REFILL = 0x4C524546u;
+static const uint32_t SALT_LATTICE_PLANES = 0x4C504C30u;
 
 static double or_uniform(uint32_t bits) { return (double)((((bits >> 9) << 1) | 1u)) * 5.9604644775390625e-08; }
+
+/* the 23-bit bit-plane draw of rng layout 4, as the top 23 bits of a word: bit 22 - b is bit
+ * 8 (row % 4) + (row % 32) / 4 of word b % 4 of counter (chain, row / 32, sweep, "LPL0" + b / 4) */
+static uint32_t or_plane_bits(int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
+  const int s = (int)(row & 31), pos = 8 * (s & 3) + (s >> 2);
+  uint32_t m = 0;
+  or_u32x4 r = {{0, 0, 0, 0}};
+  for (int b = 0; b < 23; ++b) {
+    if ((b & 3) == 0)
+      r = or_philox((uint32_t)gc, (uint32_t)(row >> 5), sweep, SALT_LATTICE_PLANES + (uint32_t)(b >> 2), k0, k1);
+    m |= ((r.v[b & 3] >> pos) & 1u) << (22 - b);
+  }
+  return m << 9;
+}
 
 /* the 23-bit split-uniform draw of rng layouts 2 and 3, as the top 23 bits of a word */
 static uint32_t or_split_bits(int layout, int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
@@ -258,7 +275,9 @@ static void* run_rows(void* arg) {
         } else {
           const int dense = B->rng_layout == 1;
           double u;
-          if (B->rng_layout == 2 || B->rng_layout == 3) {
+          if (B->rng_layout == 4) {
+            u = or_uniform(or_plane_bits(gc, row, t->sweep, t->k0, t->k1));
+          } else if (B->rng_layout == 2 || B->rng_layout == 3) {
             u = or_uniform(or_split_bits(B->rng_layout, gc, row, t->sweep, t->k0, t->k1));
           } else {
             const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 2), t->sweep, SALT_DENSE_SPIN, t->k0, t->k1)

@@ -3,9 +3,8 @@
 Mirrors tthrml_ising2d_halfsweep on numpy arrays so the strip decomposition
 of tt_thrml_b200.domain can be checked on CPU ranks (gloo): split-colour
 int8 arrays [rows][W/2], neighbour-sign pattern (left, right, up, down), the
-pattern's Philox threshold and the split-uniform draw: top 16 bits from
-counter (chain, flat row / 8, sweep, "LSPI"), half flat row % 2 of word
-(flat row / 2) % 4, low 7 bits from (chain, flat row, sweep, "LREF") word 0.
+pattern's Philox threshold and the 23-bit draw of the strips' layout
+(lattice_draws: bit-planes for count-symmetric tables, else split uniforms).
 It is itself checked against the oracle (the reference's group math on the
 lattice's per-edge tables) in test_domain_cpu.py.
 """
@@ -17,6 +16,7 @@ import numpy as np
 M32 = np.uint64(0xFFFFFFFF)
 SALT_LATTICE_SPIN = 0x4C535049
 SALT_LATTICE_REFILL = 0x4C524546
+SALT_LATTICE_PLANES = 0x4C504C30
 
 
 def philox4x32_10(c0, c1, c2, c3, k0: int, k1: int):
@@ -30,6 +30,33 @@ def philox4x32_10(c0, c1, c2, c3, k0: int, k1: int):
         k0 = (k0 + np.uint64(0x9E3779B9)) & M32
         k1 = (k1 + np.uint64(0xBB67AE85)) & M32
     return c0, c1, c2, c3
+
+
+def lattice_draws(layout: str, flat, chain: int, sweep: int, seed: int) -> np.ndarray:
+    """The 23-bit Philox draws m of the sites at flat rows `flat` (int64 array) of one chain.
+
+    "row8s": top 16 bits half flat % 2 of word (flat / 2) % 4 of counter (chain,
+    flat / 8, sweep, "LSPI"), low 7 bits word 0 >> 25 of (chain, flat, sweep,
+    "LREF").  "planes": bit 22 - b is bit 8 (flat % 4) + (flat % 32) / 4 of word
+    b % 4 of counter (chain, flat / 32, sweep, "LPL0" + b / 4)."""
+    flat = np.asarray(flat, dtype=np.int64)
+    k0, k1 = seed & 0xFFFFFFFF, seed >> 32
+    cs, ss = np.full(flat.shape, chain), np.full(flat.shape, sweep)
+    if layout == "planes":
+        pos = (8 * (flat & 3) + ((flat & 31) >> 2)).astype(np.uint64)
+        m = np.zeros(flat.shape, dtype=np.int64)
+        for ch in range(6):
+            words = philox4x32_10(cs, flat >> 5, ss, np.full(flat.shape, SALT_LATTICE_PLANES + ch), k0, k1)
+            for q in range(4):
+                b = 4 * ch + q
+                if b < 23:
+                    m |= ((words[q] >> pos) & np.uint64(1)).astype(np.int64) << (22 - b)
+        return m
+    words = philox4x32_10(cs, flat >> 3, ss, np.full(flat.shape, SALT_LATTICE_SPIN), k0, k1)
+    w = np.choose(((flat >> 1) & 3).astype(np.int64), words)
+    h = (w >> (np.uint64(16) * (flat & 1).astype(np.uint64))) & np.uint64(0xFFFF)
+    f = philox4x32_10(cs, flat, ss, np.full(flat.shape, SALT_LATTICE_REFILL), k0, k1)[0] >> np.uint64(25)
+    return ((h << np.uint64(7)) | f).astype(np.int64)
 
 
 def make_halfsweep(strips, *, chain: int = 0):
@@ -52,13 +79,7 @@ def make_halfsweep(strips, *, chain: int = 0):
         dnv = co[rows + 1].astype(np.int64)
         idx = (left < 0) * 1 + (right < 0) * 2 + (upv < 0) * 4 + (dnv < 0) * 8
         flat = strips.block_rows[colour] + Y[:, None] * hw + j
-        k0, k1 = strips.seed & 0xFFFFFFFF, strips.seed >> 32
-        cs, ss = np.full(flat.shape, chain), np.full(flat.shape, sweep)
-        words = philox4x32_10(cs, flat >> 3, ss, np.full(flat.shape, SALT_LATTICE_SPIN), k0, k1)
-        w = np.choose(((flat >> 1) & 3).astype(np.int64), words)
-        h = (w >> (np.uint64(16) * (flat & 1).astype(np.uint64))) & np.uint64(0xFFFF)
-        f = philox4x32_10(cs, flat, ss, np.full(flat.shape, SALT_LATTICE_REFILL), k0, k1)[0] >> np.uint64(25)
-        m = ((h << np.uint64(7)) | f).astype(np.int64)
+        m = lattice_draws(strips.rng_layout, flat, chain, sweep, strips.seed)
         up = m < thr[idx]
         new = np.where(up, 1, -1).astype(np.int8)
         cc[rows] = new

@@ -53,7 +53,7 @@ def test_single_domain_matches_oracle(H, W):
     st._halfsweep = ising_ref.make_halfsweep(st)
     st.load_random(3)
     st.prepare_rng(11, 6)
-    o = orc.OracleSampler(prog, n_chains=1, rng_layout="row8s")
+    o = orc.OracleSampler(prog, n_chains=1, rng_layout=st.rng_layout)
     lat = st.gather_lattice()
     half = H * W // 2
     # oracle state rows: block c = colour-c sites in linear order = split-colour rows

@@ -174,7 +174,7 @@ def test_oracle_dense_rng_layout_differs_from_site_layout():
 
 
 def test_oracle_split_uniform_lattice_layouts():
-    """The oracle's split-uniform lattice draws ("row8s", "chain8s") follow their counters:
+    """The oracle's lattice draws ("row8s", "chain8s" split uniforms, "planes" bit-planes) follow their counters:
     a numpy restatement of one colour half-sweep (neighbour-sign pattern, exact threshold,
     23-bit draw = 16 shared bits << 7 | 7 refill bits) gives the same states."""
     import numpy as np
@@ -194,7 +194,7 @@ def test_oracle_split_uniform_lattice_layouts():
         ys, xs = np.nonzero(((np.arange(H)[:, None] + np.arange(W)[None, :]) & 1) == c)
         blocks.append(lat[:, ys, xs] > 0)
     k0, k1 = seed & 0xFFFFFFFF, seed >> 32
-    for layout in ("row8s", "chain8s"):
+    for layout in ("row8s", "chain8s", "planes"):
         o = orc.OracleSampler(prog, n_chains=C, rng_layout=layout)
         o.load_state(blocks)
         o.group_step(0, sweep, seed=seed)
@@ -206,9 +206,10 @@ def test_oracle_split_uniform_lattice_layouts():
         row = np.broadcast_to(np.arange(len(ys))[None, :], (C, len(ys))).astype(np.uint64)
         gc = np.broadcast_to(np.arange(C)[:, None], (C, len(ys))).astype(np.uint64)
         sw = np.full(row.shape, sweep, np.uint64)
-        if layout == "row8s":
-            words = ising_ref.philox4x32_10(gc, row >> np.uint64(3), sw, np.full(row.shape, 0x4C535049), k0, k1)
-            pos = row
+        if layout in ("row8s", "planes"):  # one chain per counter: the numpy restatement, chain by chain
+            m = np.stack([ising_ref.lattice_draws(layout, row[c].astype(np.int64), c, sweep, seed) for c in range(C)])
+            np.testing.assert_array_equal(got, m < thr.astype(np.int64)[idx])
+            continue
         else:
             words = ising_ref.philox4x32_10(gc >> np.uint64(3), row, sw, np.full(row.shape, 0x4C535049), k0, k1)
             pos = gc

@@ -884,7 +884,8 @@ class IsingStencilGroupPlan:
     in_place: bool = True
     group_rows: int = 0
     device: Any = None
-    # split uniforms: 16 bits of counter (chain, row / 8, sweep, "LSPI") + 7 refill bits
+    # Philox draws: "planes" (bit-sliced kernel, count-symmetric tables) or the split uniforms "row8s"
+    # (16 bits of counter (chain, row / 8, sweep, "LSPI") + 7 refill bits)
     rng_layout: str = "row8s"
 
 
@@ -909,6 +910,23 @@ def ising_pattern_tables(edge_weight, site_bias) -> tuple[np.ndarray, np.ndarray
     p = 1.0 / (1.0 + np.exp(-2.0 * fields.astype(np.float64)))
     thr = np.ceil((p * 2.0**24 - 1.0) / 2.0)
     return fields, np.clip(thr, 0, 2**23).astype(np.uint32)
+
+
+def ising_count_symmetric(thresholds) -> bool:
+    """True when the 16-entry threshold table depends only on the number of -1
+    neighbours (uniform couplings: the bit-sliced lattice kernels apply)."""
+    thr = np.asarray(thresholds).astype(np.int64)
+    by_count = {}
+    for idx in range(16):
+        by_count.setdefault(bin(idx).count("1"), set()).add(int(thr[idx]))
+    return all(len(v) == 1 for v in by_count.values())
+
+
+def ising_stencil_layout(thresholds, width: int) -> str:
+    """Philox layout of the single-chain lattice kernel: "planes" (bit-sliced
+    over 32 sites) for count-symmetric tables and width % 64 == 0, else the
+    split uniforms "row8s"."""
+    return "planes" if width % 64 == 0 and ising_count_symmetric(thresholds) else "row8s"
 
 
 RESIDENT_MAX_SITES = 96 * 1024  # one byte per site of 8 chains in a CTA's shared memory
@@ -957,11 +975,12 @@ def _plan_stencil(program, device, n_chains: int = 1):
         t_dev = torch.from_numpy(thr.view(np.int32)).to(device)
         rows = st["block_rows"]
         H, W = st["dims"]
+        layout = ising_stencil_layout(thr, int(W))
         return [
             IsingStencilGroupPlan(
                 block_indices=(int(g[0]),), dims=(int(H), int(W)), colour=int(g[0]), target_row0=int(rows[int(g[0])]),
                 source_row0=int(rows[1 - int(g[0])]), thresholds=t_dev, fields=f_dev, group_rows=H * W // 2,
-                device=device,
+                device=device, rng_layout=layout,
             )
             for g in program.gibbs_spec.sampling_order
         ]

@@ -44,6 +44,8 @@ constexpr uint32_t kSaltDenseGauss = 0x44474155u;  // "DGAU"
 // Philox call instead of a quarter; m is uniform on [0, 2^23) as before.
 constexpr uint32_t kSaltLatticeSpin = 0x4C535049u;    // "LSPI"
 constexpr uint32_t kSaltLatticeRefill = 0x4C524546u;  // "LREF"
+// Bit-sliced lattice draws: plane b of a 32-site group from salt "LPL0" + b / 4.
+constexpr uint32_t kSaltLatticePlanes = 0x4C504C30u;  // "LPL0"
 
 struct u32x4 {
   uint32_t x, y, z, w;

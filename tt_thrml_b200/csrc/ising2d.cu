@@ -186,6 +186,184 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_MIN_BLOCKS) k_isin
   }
 }
 
+// Bit-sliced variant for count-symmetric tables (the threshold depends only on
+// the number n of -1 neighbours, as on every uniform lattice), Philox mode.
+// A thread updates 32 consecutive sites of a row, held as 32-bit masks in
+// byte-transposed order: site s = 4j + k of the chunk is bit 8k + j (byte k of
+// int8 word j of the row lands in bit 8k + j with one shift and one masked OR).
+// The neighbour masks L, R, U, D (bit set = -1) give the count n in three
+// bit-planes (a small adder); the draw m of a site is compared with T(n) one
+// bit at a time from the top, for all 32 sites at once: per plane the
+// threshold bit T_b(n) is a 5-way select of the plane's per-count masks (0 or
+// ~0, in shared memory), and lt |= eq & T_b & ~u_b, eq &= ~(T_b ^ u_b) with u_b
+// the draws' bits.  A thread stops once no site is tied, on average after
+// three Philox calls for the 32 sites (four planes per call) instead of four
+// calls per 16 sites.  Random bits ("planes" layout): plane b (bit 22 - b of
+// m) of the 32-site group g = flat row / 32 is word b % 4 of counter (chain,
+// g, sweep, "LPL0" + b / 4), site s at bit 8 (s % 4) + s / 4.  The decision is
+// exactly m < T(n): with every plane tied, m == T(n) and the site goes down.
+template <bool TRACE>
+__global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_MIN_BLOCKS) k_ising2d_planes(
+    int8_t* __restrict__ cc, const int8_t* __restrict__ co, int64_t half_w, FastDiv div_chunks, int64_t rows_local,
+    int32_t wrap, int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
+    int64_t block_row0, const uint32_t* __restrict__ thresholds, int64_t chain, uint64_t seed, uint32_t sweep_base,
+    const tthrml_run_ctl* __restrict__ ctl, int64_t count_lo, int64_t count_hi, unsigned long long* __restrict__ trace,
+    int64_t trace_len, tthrml_halo_export ex) {
+  // MS[i][n]: bit 23 - i of the count-n threshold as a 0 / ~0 mask (row 0: bit 23, set only for T = 2^23)
+  __shared__ __align__(16) uint32_t MS[24][8];
+  __shared__ long long red[2];
+  if (threadIdx.x < 24 * 5) {
+    const int i = threadIdx.x / 5, n = threadIdx.x - 5 * i;
+    const uint32_t t = thresholds[(1u << n) - 1u];  // the pattern with the n lowest neighbours at -1
+    MS[i][n] = ((t >> (23 - i)) & 1u) ? 0xFFFFFFFFu : 0u;
+  }
+  if (TRACE && threadIdx.x < 2) red[threadIdx.x] = 0;
+  __syncthreads();
+
+  const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
+  const uint64_t sd = ctl ? ctl->seed : seed;
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
+  const uint32_t chunks = div_chunks.d;
+  const uint32_t items = (uint32_t)(row_hi - row_lo) * chunks;  // < 2^31, checked by the host
+  long long mag = 0, bonds = 0;
+
+  for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+    const uint32_t ri = fdiv(it, div_chunks);
+    const int64_t i = row_lo + ri;
+    const int64_t j0 = (int64_t)(it - ri * chunks) << 5;
+    int64_t Y = global_row0 + i;
+    if (Y >= height) Y -= height;
+    if (Y >= height) Y -= height;
+    const int p = (int)((Y + colour) & 1);
+    const int64_t iu = i == 0 ? (wrap ? rows_local - 1 : 0) : i - 1;
+    const int64_t id = i == rows_local - 1 ? (wrap ? 0 : i) : i + 1;
+    const int8_t* rowc = co + i * half_w + j0;
+    const int8_t* rowu = co + iu * half_w + j0;
+    const int8_t* rowd = co + id * half_w + j0;
+    const uint4 m0 = ld16(rowc), m1 = ld16(rowc + 16);
+    const uint4 u0 = ld16(rowu), u1 = ld16(rowu + 16);
+    const uint4 d0 = ld16(rowd), d1 = ld16(rowd + 16);
+    const int64_t je = p ? (j0 + 32 == half_w ? 0 : j0 + 32) : (j0 == 0 ? half_w - 1 : j0 - 1);
+    const uint32_t e = ((uint32_t)(uint8_t)__ldg(co + i * half_w + je)) >> 7;  // 1: the edge neighbour is -1
+    auto signs = [](const uint4& a, const uint4& b) -> uint32_t {
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      uint32_t acc = 0u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc |= (w[j] >> (7 - j)) & (0x01010101u << j);
+      return acc;
+    };
+    const uint32_t M = signs(m0, m1), U = signs(u0, u1), D = signs(d0, d1);
+    // site s - 1 (left, p = 0) and s + 1 (right, p = 1) in byte-transposed order
+    const uint32_t L = p ? M : (M << 8) | ((M >> 23) & 0xFEu) | e;
+    const uint32_t R = p ? (M >> 8) | ((M << 23) & 0x7F000000u) | (e << 31) : M;
+    // n = L + R + U + D in bit-planes n0, n1, n2 (n2 set only for n = 4)
+    const uint32_t s1 = L ^ R, c1 = L & R, s2 = U ^ D, c2 = U & D;
+    const uint32_t n0 = s1 ^ s2, t = s1 & s2;
+    const uint32_t n1 = c1 ^ c2 ^ t, n2 = (c1 & c2) | (t & (c1 | c2));
+    auto tbit = [&](int row) -> uint32_t {  // the threshold bit of every site, from its count
+      const uint4 a = *reinterpret_cast<const uint4*>(&MS[row][0]);
+      const uint32_t m4 = MS[row][4];
+      const uint32_t lo = (n0 & a.y) | (~n0 & a.x), hi = (n0 & a.w) | (~n0 & a.z);
+      const uint32_t g = (n1 & hi) | (~n1 & lo);
+      return (n2 & m4) | (~n2 & g);
+    };
+    uint32_t lt = tbit(0);  // decided "m < T" (only T = 2^23 so far)
+    uint32_t eq = ~lt;      // still tied with T
+    const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + j0) >> 5);
+#pragma unroll 1
+    for (int ch = 0; ch < 6 && eq; ++ch) {
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, g32, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int b = 4 * ch + q;
+        if (b < 23) {
+          const uint32_t tb = tbit(b + 1), ub = word_of(r, q);
+          lt |= eq & tb & ~ub;
+          eq &= ~(tb ^ ub);
+        }
+      }
+    }
+    const uint32_t dn = ~lt;  // bit set: the site samples -1
+    uint32_t outw[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) outw[j] = ((dn >> j) & 0x01010101u) * 0xFEu + 0x01010101u;  // +1: 0x01, -1: 0xFF
+    if (TRACE && i >= count_lo && i < count_hi) {
+      const int nd = __popc(dn);
+      mag += 32 - 2 * nd;
+      if (colour == 1) {
+        const int ksum = __popc(L) + __popc(R) + __popc(U) + __popc(D);
+        const int mk = __popc(dn & L) + __popc(dn & R) + __popc(dn & U) + __popc(dn & D);
+        bonds += 4 * (32 - 2 * nd) - 2 * ksum + 4 * mk;
+      }
+    }
+    const uint4 o0 = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+    const uint4 o1 = make_uint4(outw[4], outw[5], outw[6], outw[7]);
+    int8_t* dst = cc + i * half_w + j0;
+    *reinterpret_cast<uint4*>(dst) = o0;
+    *reinterpret_cast<uint4*>(dst + 16) = o1;
+    if (ex.rows) {  // boundary rows also go straight to the neighbours' mailboxes (peer memory)
+      const int64_t slot = (int64_t)(((sweep / ex.sweeps_per_period) + 1u) & 1u) * ex.slot_bytes;
+      bool sent = false;
+      if (ex.up && i >= ex.up_row0 && i < ex.up_row0 + ex.rows) {
+        int8_t* q = ex.up + slot + (i - ex.up_row0) * half_w + j0;
+        *reinterpret_cast<uint4*>(q) = o0;
+        *reinterpret_cast<uint4*>(q + 16) = o1;
+        sent = true;
+      }
+      if (ex.down && i >= ex.down_row0 && i < ex.down_row0 + ex.rows) {
+        int8_t* q = ex.down + slot + (i - ex.down_row0) * half_w + j0;
+        *reinterpret_cast<uint4*>(q) = o0;
+        *reinterpret_cast<uint4*>(q + 16) = o1;
+        sent = true;
+      }
+      if (sent) __threadfence_system();
+    }
+  }
+  if (TRACE) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mag += __shfl_xor_sync(0xffffffffu, mag, o);
+      bonds += __shfl_xor_sync(0xffffffffu, bonds, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red[0]), (unsigned long long)mag);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red[1]), (unsigned long long)bonds);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && (int64_t)sweep < trace_len) {
+      atomicAdd(trace + 2 * (int64_t)sweep, (unsigned long long)red[0]);
+      if (colour == 1) atomicAdd(trace + 2 * (int64_t)sweep + 1, (unsigned long long)red[1]);
+    }
+  }
+}
+
+template <bool TRACE>
+int launch_ising_planes(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_local, int32_t wrap,
+                        int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
+                        int64_t block_row0, const uint32_t* thresholds, int64_t chain, uint64_t seed, uint32_t sweep,
+                        const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi, unsigned long long* trace,
+                        int64_t trace_len, const tthrml_halo_export& ex, cudaStream_t s) {
+  static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
+  if (!per_sm) {
+    int dev = 0, n = 0, b = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_ising2d_planes<TRACE>, kIsingThreads, 0);
+    if (e != cudaSuccess) return cuda_status(e, "k_ising2d_planes set-up");
+    sms = n;
+    per_sm = b > 0 ? b : 1;
+  }
+  const int64_t items = (row_hi - row_lo) * (half_w >> 5);
+  const int64_t need = (items + kIsingThreads - 1) / kIsingThreads;
+  const int64_t full = (int64_t)sms * per_sm;
+  const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
+  k_ising2d_planes<TRACE><<<grid, kIsingThreads, 0, s>>>(
+      cc, co, half_w, make_fastdiv((uint32_t)(half_w >> 5)), rows_local, wrap, row_lo, row_hi, global_row0, height,
+      colour, block_row0, thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len, ex);
+  return launch_status("k_ising2d_planes launch");
+}
+
 template <bool VARIATES, bool TRACE>
 int launch_ising(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_local, int32_t wrap, int64_t row_lo,
                  int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
@@ -217,14 +395,13 @@ int launch_ising(int8_t* cc, const int8_t* co, int64_t half_w, int64_t rows_loca
 }  // namespace
 }  // namespace tthrml
 
-extern "C" int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* other_state, int64_t width,
-                                          int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
-                                          int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
-                                          const uint32_t* thresholds, const float* fields, const float* variates,
-                                          int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
-                                          const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
-                                          int64_t* trace, int64_t trace_len, const tthrml_halo_export* export_host,
-                                          void* stream) {
+namespace {
+int halfsweep_impl(int8_t* colour_state, const int8_t* other_state, int64_t width, int64_t rows_local,
+                   int32_t wrap_rows, int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height,
+                   int32_t colour, int64_t block_row0, const uint32_t* thresholds, const float* fields,
+                   const float* variates, int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
+                   const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi, int64_t* trace, int64_t trace_len,
+                   const tthrml_halo_export* export_host, void* stream, bool planes) {
   using namespace tthrml;
   tthrml_halo_export ex{};
   if (export_host) {
@@ -272,10 +449,24 @@ extern "C" int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* ot
     set_error("tthrml_ising2d_halfsweep: more than 2^31 16-site chunks in one launch");
     return TTHRML_ERR_UNSUPPORTED;
   }
+  if (planes && (variates || width % 64 || block_row0 % 32)) {
+    set_error("tthrml_ising2d_halfsweep_planes: Philox mode only, width %% 64 == 0 and block_row0 %% 32 == 0 "
+              "(got width %lld, block_row0 %lld)", (long long)width, (long long)block_row0);
+    return TTHRML_ERR_ARG;
+  }
   if (row_hi == row_lo) return TTHRML_OK;
   cudaStream_t s = (cudaStream_t)stream;
   unsigned long long* tr = reinterpret_cast<unsigned long long*>(trace);
   const int64_t hw = width / 2;
+  if (planes) {
+    if (trace)
+      return launch_ising_planes<true>(colour_state, other_state, hw, rows_local, wrap_rows, row_lo, row_hi,
+                                       global_row0, height, colour, block_row0, thresholds, chain, seed, sweep, ctl,
+                                       count_lo, count_hi, tr, trace_len, ex, s);
+    return launch_ising_planes<false>(colour_state, other_state, hw, rows_local, wrap_rows, row_lo, row_hi,
+                                      global_row0, height, colour, block_row0, thresholds, chain, seed, sweep, ctl,
+                                      count_lo, count_hi, tr, trace_len, ex, s);
+  }
 #define TTHRML_ISING_LAUNCH(V, TR)                                                                                  \
   return launch_ising<V, TR>(colour_state, other_state, hw, rows_local, wrap_rows, row_lo, row_hi, global_row0,   \
                              height, colour, block_row0, thresholds, fields, variates, variates_sweeps, chain, seed, \
@@ -287,6 +478,32 @@ extern "C" int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* ot
   if (trace) TTHRML_ISING_LAUNCH(false, true);
   TTHRML_ISING_LAUNCH(false, false);
 #undef TTHRML_ISING_LAUNCH
+}
+}  // namespace
+
+extern "C" int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* other_state, int64_t width,
+                                          int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                          int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                          const uint32_t* thresholds, const float* fields, const float* variates,
+                                          int64_t variates_sweeps, int64_t chain, uint64_t seed, uint32_t sweep,
+                                          const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
+                                          int64_t* trace, int64_t trace_len, const tthrml_halo_export* export_host,
+                                          void* stream) {
+  return halfsweep_impl(colour_state, other_state, width, rows_local, wrap_rows, row_lo, row_hi, global_row0, height,
+                        colour, block_row0, thresholds, fields, variates, variates_sweeps, chain, seed, sweep, ctl,
+                        count_lo, count_hi, trace, trace_len, export_host, stream, false);
+}
+
+extern "C" int tthrml_ising2d_halfsweep_planes(int8_t* colour_state, const int8_t* other_state, int64_t width,
+                                               int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                               int64_t global_row0, int64_t height, int32_t colour,
+                                               int64_t block_row0, const uint32_t* thresholds, int64_t chain,
+                                               uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl,
+                                               int64_t count_lo, int64_t count_hi, int64_t* trace, int64_t trace_len,
+                                               const tthrml_halo_export* export_host, void* stream) {
+  return halfsweep_impl(colour_state, other_state, width, rows_local, wrap_rows, row_lo, row_hi, global_row0, height,
+                        colour, block_row0, thresholds, nullptr, nullptr, 0, chain, seed, sweep, ctl, count_lo,
+                        count_hi, trace, trace_len, export_host, stream, true);
 }
 
 extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, int64_t width,

@@ -39,7 +39,7 @@ from typing import Callable
 import numpy as np
 
 from . import _native as nat
-from .compiler import ising_pattern_tables
+from .compiler import ising_pattern_tables, ising_stencil_layout
 from .rng import seed_from_key
 
 
@@ -114,6 +114,8 @@ class LatticeStrips:
         self.cuda_graphs = bool(cuda_graphs) and not self._custom
         fields, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
         self.fields_host, self.thresholds_host = fields, thr
+        # Philox layout of the half-sweeps, the same as the executor's single-chain lattice plan
+        self.rng_layout = ising_stencil_layout(thr, self.W)
         self.colours = [torch.empty((self.rows_local, self.W // 2), dtype=torch.int8, device=self.device)
                         for _ in range(2)]
         self.fields = torch.from_numpy(fields).to(self.device)
@@ -227,6 +229,18 @@ class LatticeStrips:
                         export=None) -> None:
         c, o = self.colours[colour], self.colours[1 - colour]
         trace = self._trace
+        if self.rng_layout == "planes":
+            nat.check(
+                self._lib.tthrml_ising2d_halfsweep_planes(
+                    c.data_ptr(), o.data_ptr(), self.W, self.rows_local, 0, row_lo, row_hi, self.global_row0, self.H,
+                    colour, self.block_rows[colour], self.thresholds.data_ptr(), 0, self.seed, sweep, ctl_ptr,
+                    self.D, self.D + self.h, None if trace is None else trace.data_ptr(),
+                    0 if trace is None else trace.shape[0], None if export is None else ctypes.byref(export),
+                    nat.stream_handle(stream),
+                ),
+                "tthrml_ising2d_halfsweep_planes",
+            )
+            return
         nat.check(
             self._lib.tthrml_ising2d_halfsweep_x(
                 c.data_ptr(), o.data_ptr(), self.W, self.rows_local, 0, row_lo, row_hi, self.global_row0, self.H,

@@ -519,15 +519,25 @@ class Executor:
             v = self._variates(bi)
             H, W = plan.dims
             base = self._global_state.data_ptr()  # one chain: flat row r is byte r
-            nat.check(
-                self._lib.tthrml_ising2d_halfsweep(
-                    base + plan.target_row0, base + plan.source_row0, W, H, 1, 0, H, 0, H, plan.colour,
-                    plan.target_row0, plan.thresholds.data_ptr(), plan.fields.data_ptr(),
-                    None if v is None else v.data_ptr(), self._rng_n_sweeps if v is not None else 0,
-                    self.chain_offset, seed, sweep_idx, ctl, 0, 0, None, 0, stream,
-                ),
-                "tthrml_ising2d_halfsweep",
-            )
+            if v is None and plan.rng_layout == "planes":
+                nat.check(
+                    self._lib.tthrml_ising2d_halfsweep_planes(
+                        base + plan.target_row0, base + plan.source_row0, W, H, 1, 0, H, 0, H, plan.colour,
+                        plan.target_row0, plan.thresholds.data_ptr(), self.chain_offset, seed, sweep_idx, ctl, 0, 0,
+                        None, 0, None, stream,
+                    ),
+                    "tthrml_ising2d_halfsweep_planes",
+                )
+            else:
+                nat.check(
+                    self._lib.tthrml_ising2d_halfsweep(
+                        base + plan.target_row0, base + plan.source_row0, W, H, 1, 0, H, 0, H, plan.colour,
+                        plan.target_row0, plan.thresholds.data_ptr(), plan.fields.data_ptr(),
+                        None if v is None else v.data_ptr(), self._rng_n_sweeps if v is not None else 0,
+                        self.chain_offset, seed, sweep_idx, ctl, 0, 0, None, 0, stream,
+                    ),
+                    "tthrml_ising2d_halfsweep",
+                )
         elif plan.kind == "ising2d_resident":
             H, W = plan.dims
             nat.check(
