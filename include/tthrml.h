@@ -276,6 +276,21 @@ int tthrml_ising2d_resident(uint32_t* state_dev, int64_t n_chains, int32_t heigh
                             void* stream);
 
 /*
+ * tthrml_ising2d_resident for count-symmetric threshold tables (the kernel
+ * reads thresholds[2^n - 1] for n = 0..4), bit-sliced over 4 sites x 8 chains
+ * per 32-bit word.  Random bits ("planes8"): bit 22 - b of the 23-bit draw of
+ * chain c at flat row f is bit 8 (f % 4) + c % 8 of word b % 4 of counter
+ * (c / 8, f / 4, sweep, "LPL0" + b / 4).  Requires width % 8 == 0 and block
+ * rows % 4 == 0.
+ */
+int tthrml_ising2d_resident_planes(uint32_t* state_dev, int64_t n_chains, int32_t height, int32_t width,
+                                   int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds_dev,
+                                   uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
+                                   double* obs_dev, int64_t obs_first, int64_t obs_every, int64_t n_obs,
+                                   int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl_dev,
+                                   void* stream);
+
+/*
  * Halo export of a strip-decomposed lattice (tthrml_ising2d_halfsweep_x):
  * while a half-sweep computes local rows [up_row0, up_row0 + rows) it also
  * stores them at `up` (the up neighbour's mailbox, peer memory), rows

@@ -59,7 +59,10 @@ typedef struct {
  * (chain/8, row, sweep), half chain % 2 of word (chain/2) % 4 (the
  * shared-memory resident lattice kernel).  Layout 4 ("planes", the bit-sliced
  * lattice kernel): bit 22 - b of m is bit 8 (row % 4) + (row % 32) / 4 of word
- * b % 4 of counter (chain, row / 32, sweep, "LPL0" + b / 4). */
+ * b % 4 of counter (chain, row / 32, sweep, "LPL0" + b / 4).  Layout 5
+ * ("planes8", the bit-sliced resident kernel): bit 22 - b of m is bit
+ * 8 (row % 4) + chain % 8 of word b % 4 of counter (chain / 8, row / 4,
+ * sweep, "LPL0" + b / 4). */
 typedef struct {
   int32_t family, q, n_interactions, rng_layout;
   int64_t n_nodes, row_start;
@@ -108,6 +111,21 @@ static uint32_t or_plane_bits(int64_t gc, int64_t row, uint32_t sweep, uint32_t 
   for (int b = 0; b < 23; ++b) {
     if ((b & 3) == 0)
       r = or_philox((uint32_t)gc, (uint32_t)(row >> 5), sweep, SALT_LATTICE_PLANES + (uint32_t)(b >> 2), k0, k1);
+    m |= ((r.v[b & 3] >> pos) & 1u) << (22 - b);
+  }
+  return m << 9;
+}
+
+/* the 23-bit bit-plane draw of rng layout 5 ("planes8"), as the top 23 bits of a word: bit 22 - b
+ * is bit 8 (row % 4) + chain % 8 of word b % 4 of counter (chain / 8, row / 4, sweep, "LPL0" + b / 4) */
+static uint32_t or_plane8_bits(int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
+  const int pos = 8 * (int)(row & 3) + (int)(gc & 7);
+  uint32_t m = 0;
+  or_u32x4 r = {{0, 0, 0, 0}};
+  for (int b = 0; b < 23; ++b) {
+    if ((b & 3) == 0)
+      r = or_philox((uint32_t)(gc >> 3), (uint32_t)(row >> 2), sweep, SALT_LATTICE_PLANES + (uint32_t)(b >> 2), k0,
+                    k1);
     m |= ((r.v[b & 3] >> pos) & 1u) << (22 - b);
   }
   return m << 9;
@@ -277,6 +295,8 @@ static void* run_rows(void* arg) {
           double u;
           if (B->rng_layout == 4) {
             u = or_uniform(or_plane_bits(gc, row, t->sweep, t->k0, t->k1));
+          } else if (B->rng_layout == 5) {
+            u = or_uniform(or_plane8_bits(gc, row, t->sweep, t->k0, t->k1));
           } else if (B->rng_layout == 2 || B->rng_layout == 3) {
             u = or_uniform(or_split_bits(B->rng_layout, gc, row, t->sweep, t->k0, t->k1));
           } else {

@@ -322,8 +322,10 @@ class OracleSampler:
         "LREF"; the single-chain stencil and the resident lattice kernel);
         "planes": bit-plane draws of the bit-sliced lattice kernel (bit 22 - b
         of the draw of row r: bit 8 (r % 4) + (r % 32) / 4 of word b % 4 of
-        counter (chain, r / 32, sweep, "LPL0" + b / 4))."""
-        names = {"chain4": 0, "row4": 1, "row8s": 2, "chain8s": 3, "planes": 4}
+        counter (chain, r / 32, sweep, "LPL0" + b / 4)); "planes8": those of the
+        bit-sliced resident kernel (bit 8 (r % 4) + chain % 8 of word b % 4 of
+        counter (chain / 8, r / 4, sweep, "LPL0" + b / 4))."""
+        names = {"chain4": 0, "row4": 1, "row8s": 2, "chain8s": 3, "planes": 4, "planes8": 5}
         layouts = rng_layout if isinstance(rng_layout, dict) else None
         for v in (layouts.values() if layouts is not None else [rng_layout]):
             if v not in names:

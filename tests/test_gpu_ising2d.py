@@ -212,11 +212,20 @@ def test_halo_import_wait_is_bounded(cuda_device):
     assert bool((c0[:D] == -1).all()) and bool((c0[rows - D :] == -1).all()) and bool((c0[D : rows - D] == 1).all())
 
 
-@pytest.mark.parametrize("H,W,C", [(32, 64, 64), (16, 32, 256)])
-def test_resident_lattice_matches_oracle(cuda_device, H, W, C):
+@pytest.mark.parametrize("H,W,C,layout", [(32, 64, 64, "planes8"), (16, 32, 256, "planes8"), (16, 20, 64, "chain8s")])
+def test_resident_lattice_matches_oracle(cuda_device, H, W, C, layout):
     prog = workloads.IsingLattice2D(H, W, beta=0.4407)
     rep, ex, _ = gh.run_parity(prog, C, 4, mode="philox")
     assert [g.kernel_artifact.kind for g in ex.compiled.sampling_groups] == ["ising2d_resident"] * 2
+    assert {g.kernel_artifact.rng_layout for g in ex.compiled.sampling_groups} == {layout}
+    _assert_parity(rep)
+
+
+@pytest.mark.parametrize("H,W,layout", [(64, 64, "planes"), (32, 96, "row8s")])
+def test_single_chain_lattice_layout_choice(cuda_device, H, W, layout):
+    prog = workloads.IsingLattice2D(H, W, beta=0.4407)
+    rep, ex, _ = gh.run_parity(prog, 1, 3, mode="philox")
+    assert {g.kernel_artifact.rng_layout for g in ex.compiled.sampling_groups} == {layout}
     _assert_parity(rep)
 
 

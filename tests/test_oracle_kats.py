@@ -194,7 +194,7 @@ def test_oracle_split_uniform_lattice_layouts():
         ys, xs = np.nonzero(((np.arange(H)[:, None] + np.arange(W)[None, :]) & 1) == c)
         blocks.append(lat[:, ys, xs] > 0)
     k0, k1 = seed & 0xFFFFFFFF, seed >> 32
-    for layout in ("row8s", "chain8s", "planes"):
+    for layout in ("row8s", "chain8s", "planes", "planes8"):
         o = orc.OracleSampler(prog, n_chains=C, rng_layout=layout)
         o.load_state(blocks)
         o.group_step(0, sweep, seed=seed)
@@ -206,6 +206,15 @@ def test_oracle_split_uniform_lattice_layouts():
         row = np.broadcast_to(np.arange(len(ys))[None, :], (C, len(ys))).astype(np.uint64)
         gc = np.broadcast_to(np.arange(C)[:, None], (C, len(ys))).astype(np.uint64)
         sw = np.full(row.shape, sweep, np.uint64)
+        if layout == "planes8":  # bit 8 (row % 4) + chain % 8 of counter (chain / 8, row / 4, sweep, "LPL0" + b / 4)
+            pos = np.uint64(8) * (row & np.uint64(3)) + (gc & np.uint64(7))
+            m = np.zeros(row.shape, np.int64)
+            for b in range(23):
+                wb = ising_ref.philox4x32_10(gc >> np.uint64(3), row >> np.uint64(2), sw,
+                                             np.full(row.shape, 0x4C504C30 + b // 4), k0, k1)[b % 4]
+                m |= ((wb >> pos) & np.uint64(1)).astype(np.int64) << (22 - b)
+            np.testing.assert_array_equal(got, m < thr.astype(np.int64)[idx])
+            continue
         if layout in ("row8s", "planes"):  # one chain per counter: the numpy restatement, chain by chain
             m = np.stack([ising_ref.lattice_draws(layout, row[c].astype(np.int64), c, sweep, seed) for c in range(C)])
             np.testing.assert_array_equal(got, m < thr.astype(np.int64)[idx])

@@ -863,7 +863,8 @@ class IsingResidentGroupPlan:
     in_place: bool = True
     group_rows: int = 0
     device: Any = None
-    # split uniforms: 16 bits of counter (chain / 8, row, sweep, "LSPI") + 7 refill bits
+    # Philox draws: "planes8" (bit-sliced kernel, count-symmetric tables and width % 8 == 0) or the split
+    # uniforms "chain8s" (16 bits of counter (chain / 8, row, sweep, "LSPI") + 7 refill bits)
     rng_layout: str = "chain8s"
 
 
@@ -962,10 +963,12 @@ def _plan_stencil(program, device, n_chains: int = 1):
         t_dev = torch.from_numpy(thr.view(np.int32)).to(device)
         H, W = st["dims"]
         rows = tuple(int(r) for r in st["block_rows"])
+        layout = "planes8" if W % 8 == 0 and all(r % 4 == 0 for r in rows) and ising_count_symmetric(thr) \
+            else "chain8s"
         return [
             IsingResidentGroupPlan(
                 block_indices=(int(g[0]),), dims=(int(H), int(W)), colour=int(g[0]), block_rows=rows,
-                thresholds=t_dev, group_rows=H * W // 2, device=device,
+                thresholds=t_dev, group_rows=H * W // 2, device=device, rng_layout=layout,
             )
             for g in program.gibbs_spec.sampling_order
         ]

@@ -28,6 +28,16 @@ constexpr int kResThreads = 512;
 
 __device__ __forceinline__ int wrapi(int i, int n) { return i < 0 ? i + n : (i >= n ? i - n : i); }
 
+// PLANES: the bit-sliced decision for count-symmetric tables -- a 32-bit
+// shared-memory word is 4 sites x 8 chains (byte k = site j + k, bit v = chain
+// v); its neighbour words L, R (byte funnel shifts of the other colour's row),
+// U and D give each of the 32 spins its count n of -1 neighbours in three
+// bit-planes, and the draws are compared with the count-n thresholds one bit
+// at a time from the top (as in csrc/ising2d.cu's k_ising2d_planes).  Random
+// bits ("planes8"): bit 22 - b of the draw of chain c at flat row f is bit
+// 8 (f % 4) + c % 8 of word b % 4 of counter (c / 8, f / 4, sweep, "LPL0" +
+// b / 4).
+template <bool PLANES>
 __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     uint32_t* state, int64_t C, int32_t H, int32_t W, int64_t row0_c0, int64_t row0_c1,
     const uint32_t* __restrict__ thresholds, uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half,
@@ -36,6 +46,8 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
   extern __shared__ __align__(16) unsigned char lat[];  // [2][H][W/2]
   __shared__ int32_t TH[16];   // threshold >> 7: compared with a draw's top 16 bits
   __shared__ uint32_t TL[16];  // threshold & 127: compared with the refill bits on a tie
+  // PLANES: MS[i][n] = bit 23 - i of the count-n threshold as a 0 / ~0 mask
+  __shared__ __align__(16) uint32_t MS[PLANES ? 24 : 1][8];
   __shared__ int counts[8];
   const int hw = W >> 1;
   const int half_sites = H * hw;
@@ -45,6 +57,11 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
   if (threadIdx.x < 16) {
     TH[threadIdx.x] = (int32_t)(thresholds[threadIdx.x] >> 7);
     TL[threadIdx.x] = thresholds[threadIdx.x] & 127u;
+  }
+  if (PLANES && threadIdx.x < 24 * 5) {
+    const int i = threadIdx.x / 5, n = threadIdx.x - 5 * i;
+    const uint32_t t = thresholds[(1u << n) - 1u];  // the pattern with the n lowest neighbours at -1
+    MS[i][n] = ((t >> (23 - i)) & 1u) ? 0xFFFFFFFFu : 0u;
   }
   for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
     const int c = i / half_sites, r = i - c * half_sites;
@@ -64,7 +81,55 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     unsigned char* mine = lat + c * half_sites;
     const unsigned char* other = lat + (1 - c) * half_sites;
     const int64_t row0 = c ? row0_c1 : row0_c0;
-    for (int r = threadIdx.x; r < half_sites; r += blockDim.x) {
+    if (PLANES) {
+      const uint32_t* ow = reinterpret_cast<const uint32_t*>(other);
+      uint32_t* mw = reinterpret_cast<uint32_t*>(mine);
+      const int qw = hw >> 2;  // words per colour row
+      for (int q = threadIdx.x; q < (half_sites >> 2); q += blockDim.x) {
+        const int r = q << 2;
+        const int Y = (int)fdiv((uint32_t)r, div_hw), j = r - Y * hw;
+        const int p = (Y + c) & 1;
+        const int yu = wrapi(Y - 1, H), yd = wrapi(Y + 1, H);
+        const int wq = j >> 2;
+        const uint32_t M = ow[Y * qw + wq];
+        const uint32_t U = ow[yu * qw + wq], D = ow[yd * qw + wq];
+        uint32_t L, R;
+        if (p) {  // right neighbours: sites j+1..j+4
+          L = M;
+          R = __funnelshift_r(M, ow[Y * qw + (wq + 1 == qw ? 0 : wq + 1)], 8);
+        } else {  // left neighbours: sites j-1..j+2
+          L = __funnelshift_l(ow[Y * qw + (wq == 0 ? qw - 1 : wq - 1)], M, 8);
+          R = M;
+        }
+        const uint32_t s1 = L ^ R, c1 = L & R, s2 = U ^ D, c2 = U & D;
+        const uint32_t n0 = s1 ^ s2, tt = s1 & s2;
+        const uint32_t n1 = c1 ^ c2 ^ tt, n2 = (c1 & c2) | (tt & (c1 | c2));
+        auto tbit = [&](int i) -> uint32_t {
+          const uint4 a = *reinterpret_cast<const uint4*>(&MS[i][0]);
+          const uint32_t m4 = MS[i][4];
+          const uint32_t lo = (n0 & a.y) | (~n0 & a.x), hi = (n0 & a.w) | (~n0 & a.z);
+          const uint32_t g2 = (n1 & hi) | (~n1 & lo);
+          return (n2 & m4) | (~n2 & g2);
+        };
+        uint32_t lt = tbit(0), eq = ~lt;
+        const uint32_t quad = (uint32_t)((row0 + r) >> 2);
+#pragma unroll 1
+        for (int ch = 0; ch < 6 && eq; ++ch) {
+          const u32x4 rr = philox4x32_10(u32x4{gc0 >> 3, quad, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int b = 4 * ch + k;
+            if (b < 23) {
+              const uint32_t tb = tbit(b + 1), ub = word_of(rr, k);
+              lt |= eq & tb & ~ub;
+              eq &= ~(tb ^ ub);
+            }
+          }
+        }
+        mw[q] = ~lt;  // bit set: the chain's site samples -1
+      }
+    }
+    for (int r = threadIdx.x; !PLANES && r < half_sites; r += blockDim.x) {
       const int Y = (int)fdiv((uint32_t)r, div_hw), j = r - Y * hw;
       const int p = (Y + c) & 1;
       const int jl = wrapi(j - 1 + p, hw), jr = wrapi(j + p, hw);
@@ -144,12 +209,11 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
 }  // namespace
 }  // namespace tthrml
 
-extern "C" int tthrml_ising2d_resident(uint32_t* state, int64_t n_chains, int32_t height, int32_t width,
-                                       int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds,
-                                       uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
-                                       double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
-                                       int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl,
-                                       void* stream) {
+namespace {
+int resident_impl(uint32_t* state, int64_t n_chains, int32_t height, int32_t width, int64_t row0_colour0,
+                  int64_t row0_colour1, const uint32_t* thresholds, uint64_t seed, uint32_t sweep0, int32_t colour0,
+                  int64_t n_half_sweeps, double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
+                  int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl, void* stream, bool planes) {
   using namespace tthrml;
   if (!state || !thresholds || height <= 0 || width <= 0 || height % 2 || width % 2 || n_chains <= 0 ||
       n_chains % 32 || chain_offset % 8 || (colour0 != 0 && colour0 != 1) || n_half_sweeps < 0) {
@@ -172,11 +236,38 @@ extern "C" int tthrml_ising2d_resident(uint32_t* state, int64_t n_chains, int32_
               (int)height, (int)width, (long long)smem, max_smem);
     return TTHRML_ERR_UNSUPPORTED;
   }
-  e = cudaFuncSetAttribute(k_ising2d_resident, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (planes && (width % 8 || row0_colour0 % 4 || row0_colour1 % 4)) {
+    set_error("tthrml_ising2d_resident_planes: width %% 8 == 0 and block rows %% 4 == 0 required");
+    return TTHRML_ERR_ARG;
+  }
+  auto kernel = planes ? k_ising2d_resident<true> : k_ising2d_resident<false>;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return cuda_status(e, "k_ising2d_resident shared memory attribute");
   if (n_half_sweeps == 0 && !obs) return TTHRML_OK;
-  k_ising2d_resident<<<(unsigned)(n_chains / 8), kResThreads, (size_t)smem, (cudaStream_t)stream>>>(
+  kernel<<<(unsigned)(n_chains / 8), kResThreads, (size_t)smem, (cudaStream_t)stream>>>(
       state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0, n_half_sweeps,
       obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, make_fastdiv((uint32_t)(width / 2)));
   return launch_status("k_ising2d_resident launch");
+}
+
+}  // namespace
+
+extern "C" int tthrml_ising2d_resident(uint32_t* state, int64_t n_chains, int32_t height, int32_t width,
+                                       int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds,
+                                       uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
+                                       double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
+                                       int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl,
+                                       void* stream) {
+  return resident_impl(state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0,
+                       n_half_sweeps, obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, stream, false);
+}
+
+extern "C" int tthrml_ising2d_resident_planes(uint32_t* state, int64_t n_chains, int32_t height, int32_t width,
+                                              int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds,
+                                              uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
+                                              double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
+                                              int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl,
+                                              void* stream) {
+  return resident_impl(state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0,
+                       n_half_sweeps, obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, stream, true);
 }

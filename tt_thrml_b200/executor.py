@@ -313,14 +313,15 @@ class Executor:
         plan = self._resident_plans()[0]
         H, W = plan.dims
         nat.bind_device(self._tdev.index)
+        fn = "tthrml_ising2d_resident_planes" if plan.rng_layout == "planes8" else "tthrml_ising2d_resident"
         nat.check(
-            self._lib.tthrml_ising2d_resident(
+            getattr(self._lib, fn)(
                 self._global_state.data_ptr(), self.n_chains, H, W, plan.block_rows[0], plan.block_rows[1],
                 plan.thresholds.data_ptr(), self._rng_buffers.seed, self._sweep_counter, 0, 2 * n_sweeps,
                 None if obs is None else obs.data_ptr(), obs_first, obs_every, n_obs, obs_colours,
                 self.chain_offset, None, nat.stream_handle(self._stream),
             ),
-            "tthrml_ising2d_resident",
+            fn,
         )
         self._sweep_counter += n_sweeps
 
@@ -540,13 +541,14 @@ class Executor:
                 )
         elif plan.kind == "ising2d_resident":
             H, W = plan.dims
+            fn = "tthrml_ising2d_resident_planes" if plan.rng_layout == "planes8" else "tthrml_ising2d_resident"
             nat.check(
-                self._lib.tthrml_ising2d_resident(
+                getattr(self._lib, fn)(
                     self._global_state.data_ptr(), self.n_chains, H, W, plan.block_rows[0], plan.block_rows[1],
                     plan.thresholds.data_ptr(), seed, sweep_idx, plan.colour, 1, None, 0, 0, 0, 0, self.chain_offset,
                     ctl, stream,
                 ),
-                "tthrml_ising2d_resident",
+                fn,
             )
         elif plan.kind == "potts3d":
             bi = plan.block_indices[0]
