@@ -37,6 +37,9 @@ constexpr int kIsingThreads = 256;
 #ifndef TTHRML_ISING_MIN_BLOCKS
 #define TTHRML_ISING_MIN_BLOCKS 3
 #endif
+#ifndef TTHRML_ISING_PLANES_MIN_BLOCKS
+#define TTHRML_ISING_PLANES_MIN_BLOCKS 3
+#endif
 
 __device__ __forceinline__ uint4 ld16(const int8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
@@ -203,7 +206,7 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_MIN_BLOCKS) k_isin
 // g, sweep, "LPL0" + b / 4), site s at bit 8 (s % 4) + s / 4.  The decision is
 // exactly m < T(n): with every plane tied, m == T(n) and the site goes down.
 template <bool TRACE>
-__global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_MIN_BLOCKS) k_ising2d_planes(
+__global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS) k_ising2d_planes(
     int8_t* __restrict__ cc, const int8_t* __restrict__ co, int64_t half_w, FastDiv div_chunks, int64_t rows_local,
     int32_t wrap, int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
     int64_t block_row0, const uint32_t* __restrict__ thresholds, int64_t chain, uint64_t seed, uint32_t sweep_base,
