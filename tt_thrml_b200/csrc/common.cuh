@@ -46,6 +46,10 @@ constexpr uint32_t kSaltLatticeSpin = 0x4C535049u;    // "LSPI"
 constexpr uint32_t kSaltLatticeRefill = 0x4C524546u;  // "LREF"
 // Bit-sliced lattice draws: plane b of a 32-site group from salt "LPL0" + b / 4.
 constexpr uint32_t kSaltLatticePlanes = 0x4C504C30u;  // "LPL0"
+// Chunks of four planes the bit-sliced kernels draw before testing for ties.
+#ifndef TTHRML_PLANES_EAGER
+#define TTHRML_PLANES_EAGER 3
+#endif
 
 struct u32x4 {
   uint32_t x, y, z, w;

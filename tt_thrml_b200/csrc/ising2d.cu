@@ -273,8 +273,7 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
     uint32_t lt = tbit(0);  // decided "m < T" (only T = 2^23 so far)
     uint32_t eq = ~lt;      // still tied with T
     const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + j0) >> 5);
-#pragma unroll 1
-    for (int ch = 0; ch < 6 && eq; ++ch) {
+    auto planes4 = [&](int ch) {
       const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, g32, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -285,7 +284,12 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
           eq &= ~(tb ^ ub);
         }
       }
-    }
+    };
+    // planes 0..11 unconditionally (nearly every warp needs them; the three calls overlap), then on demand
+#pragma unroll
+    for (int ch = 0; ch < TTHRML_PLANES_EAGER; ++ch) planes4(ch);
+#pragma unroll 1
+    for (int ch = TTHRML_PLANES_EAGER; ch < 6 && eq; ++ch) planes4(ch);
     const uint32_t dn = ~lt;  // bit set: the site samples -1
     uint32_t outw[8];
 #pragma unroll

@@ -113,8 +113,7 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
         };
         uint32_t lt = tbit(0), eq = ~lt;
         const uint32_t quad = (uint32_t)((row0 + r) >> 2);
-#pragma unroll 1
-        for (int ch = 0; ch < 6 && eq; ++ch) {
+        auto planes4 = [&](int ch) {
           const u32x4 rr = philox4x32_10(u32x4{gc0 >> 3, quad, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -125,7 +124,12 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
               eq &= ~(tb ^ ub);
             }
           }
-        }
+        };
+        // planes 0..11 unconditionally (nearly every warp needs them; the calls overlap), then on demand
+#pragma unroll
+        for (int ch = 0; ch < TTHRML_PLANES_EAGER; ++ch) planes4(ch);
+#pragma unroll 1
+        for (int ch = TTHRML_PLANES_EAGER; ch < 6 && eq; ++ch) planes4(ch);
         mw[q] = ~lt;  // bit set: the chain's site samples -1
       }
     }
