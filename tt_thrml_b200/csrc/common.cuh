@@ -156,12 +156,16 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t s
 // of softmax(theta): e_k = 2^((theta_k - max theta) * log2 e) (ex2.approx),
 // and the draw is the number of boundaries k < q - 1 that u reaches,
 // u >= C_k / S with C_k = e_0 + ... + e_k and S = C_(q-1).  For u < 1/2 the
-// boundaries are decided on head sums, C_k <= u*S; otherwise on tail sums
-// T_(k+1) = e_(k+1) + ... + e_(q-1) (summed from the end) against (1 - u)*S,
-// which is exact in float32.  Either way every boundary close to u is decided
-// by a sum that is small where the decision is close, so the float32 error of
-// a decision stays near 1e-6 in logit units at both ends of the CDF, inside the
-// 1e-5 threshold band of the parity criteria.
+// boundaries are decided on head sums, C_k <= u*S; otherwise the categories
+// are taken in reverse order, so the running sums are the tail sums T_(k+1) =
+// e_(k+1) + ... + e_(q-1) (summed from the end), decided against (1 - u)*S
+// (1 - u is exact in float32), and the count is mirrored.  Either way every
+// boundary close to u is decided by a sum that is small where the decision is
+// close, so the float32 error of a decision stays near 1e-6 in logit units at
+// both ends of the CDF, inside the 1e-5 threshold band of the parity criteria;
+// one pass of running sums and one compare per boundary serve both ends.
+// Small QMAX (unrolled, registers) reverses over QMAX entries with e_k = 0
+// past q, which leaves the same sums with leading zeros.
 template <int QMAX>
 __device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int q, float u) {
   constexpr bool kUnroll = QMAX <= 16;  // small bounds stay in registers
@@ -170,30 +174,45 @@ __device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int 
   for (int k = 1; k < QMAX; ++k)
     if (k < q) m = fmaxf(m, theta[k]);
   const float ml = m * 1.44269502162933349609375f;
-  float e[QMAX], head[QMAX];
-  float s = 0.0f;
-#pragma unroll(kUnroll ? QMAX : 1)
-  for (int k = 0; k < QMAX; ++k) {
-    if (k < q) {
-      float v;
-      asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(__fmaf_rn(theta[k], 1.44269502162933349609375f, -ml)));
-      e[k] = v;
-      s = k == 0 ? v : __fadd_rn(s, v);
-      head[k] = s;
-    }
-  }
   const bool low = u < 0.5f;
-  const float us = __fmul_rn(u, s), vs = __fmul_rn(1.0f - u, s);
-  int cat = 0;
-  float tail = 0.0f;  // T_(k+1) while boundary k is decided, walking down from the top
-#pragma unroll(kUnroll ? QMAX : 1)
-  for (int k = QMAX - 2; k >= 0; --k) {
-    if (k < q - 1) {
-      tail = k == q - 2 ? e[k + 1] : __fadd_rn(tail, e[k + 1]);
-      cat += (low ? head[k] <= us : vs <= tail) ? 1 : 0;
+  float e[QMAX];
+  int cnt = 0;
+  if constexpr (kUnroll) {
+#pragma unroll
+    for (int k = 0; k < QMAX; ++k) {
+      float v = 0.0f;
+      if (k < q) asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(__fmaf_rn(theta[k], 1.44269502162933349609375f, -ml)));
+      e[k] = v;
     }
+    float h[QMAX];
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < QMAX; ++j) {
+      const float x = low ? e[j] : e[QMAX - 1 - j];
+      s = j == 0 ? x : __fadd_rn(s, x);
+      h[j] = s;
+    }
+    const float t = __fmul_rn(low ? u : 1.0f - u, s);
+#pragma unroll
+    for (int j = 0; j < QMAX - 1; ++j) cnt += h[j] <= t ? 1 : 0;
+    return low ? cnt : QMAX - 1 - cnt;
+  } else {
+    for (int k = 0; k < q; ++k)
+      asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e[k]) : "f"(__fmaf_rn(theta[k], 1.44269502162933349609375f, -ml)));
+    float s = 0.0f;  // the total, in the order of the running sums below
+    for (int j = 0; j < q; ++j) {
+      const float x = low ? e[j] : e[q - 1 - j];
+      s = j == 0 ? x : __fadd_rn(s, x);
+    }
+    const float t = __fmul_rn(low ? u : 1.0f - u, s);
+    float h = 0.0f;
+    for (int j = 0; j < q - 1; ++j) {
+      const float x = low ? e[j] : e[q - 1 - j];
+      h = j == 0 ? x : __fadd_rn(h, x);
+      cnt += h <= t ? 1 : 0;
+    }
+    return low ? cnt : q - 1 - cnt;
   }
-  return cat;
 }
 
 // Heat-bath spin decision in Philox mode: +1 with probability sigmoid(2*gamma)
