@@ -318,6 +318,22 @@ int tthrml_ising2d_halfsweep_x(int8_t* colour_state, const int8_t* other_state, 
                                const tthrml_halo_export* export_host, void* stream);
 
 /*
+ * tthrml_ising2d_halfsweep_planes on bit-packed rows: colour_state and
+ * other_state are uint32 [rows_local][width/64], word w of a row holding the
+ * row's sites 32w .. 32w + 31 (site s at bit 8 (s % 4) + s / 4, bit set = -1);
+ * the same draws and decisions as tthrml_ising2d_halfsweep_planes.  The halo
+ * export stores words (slot_bytes >= rows * width/16).  Requires width % 64 ==
+ * 0 and block_row0 % 32 == 0.
+ */
+int tthrml_ising2d_halfsweep_bits(uint32_t* colour_state, const uint32_t* other_state, int64_t width,
+                                  int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                  int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                  const uint32_t* thresholds_dev, int64_t chain, uint64_t seed, uint32_t sweep,
+                                  const tthrml_run_ctl* ctl_dev, int64_t count_lo, int64_t count_hi,
+                                  int64_t* trace_dev, int64_t trace_len, const tthrml_halo_export* export_host,
+                                  void* stream);
+
+/*
  * tthrml_ising2d_halfsweep_x for count-symmetric threshold tables (thresholds
  * equal for patterns with the same number of -1 neighbours; the kernel reads
  * thresholds[2^n - 1] for n = 0..4), Philox mode, bit-sliced over 32 sites.

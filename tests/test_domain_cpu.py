@@ -202,3 +202,32 @@ def test_a_rank_that_leaves_ends_the_exchange_with_an_error(tmp_path):
     text = out.read_text()
     assert text.startswith("error"), text
     assert float(text.split(" after ")[1].rstrip("s")) < 60.0
+
+
+def test_bit_packed_rows_round_trip_and_load():
+    """Bit-packed strip storage: pack/unpack invert each other (site s of a word at bit 8 (s % 4) + s / 4),
+    and loading a lattice then gathering it returns it unchanged."""
+    import torch
+
+    rng = np.random.default_rng(4)
+    rows = torch.from_numpy(rng.choice(np.array([-1, 1], np.int8), size=(5, 128)))
+    words = LatticeStrips.pack_rows(rows)
+    assert words.dtype == torch.int32 and tuple(words.shape) == (5, 4)
+    np.testing.assert_array_equal(LatticeStrips.unpack_rows(words).numpy(), rows.numpy())
+    # bit 8 (s % 4) + s / 4 of word w is site 32 w + s
+    w = words.numpy().astype(np.int64) & 0xFFFFFFFF
+    for s_ in (0, 1, 5, 31):
+        bit = (w[:, 1] >> (8 * (s_ % 4) + s_ // 4)) & 1
+        np.testing.assert_array_equal(bit, (rows.numpy()[:, 32 + s_] < 0).astype(np.int64))
+    prog = workloads.IsingLattice2D(16, 256, beta=0.4407)
+    st = LatticeStrips(prog, device="cpu", halo=2, halfsweep=lambda *a: None, storage="bits")
+    lat = rng.choice(np.array([-1, 1], np.int8), size=(16, 256))
+    st.load_lattice(lat)
+    np.testing.assert_array_equal(st.gather_lattice(), lat)
+    ref = LatticeStrips(prog, device="cpu", halo=2, halfsweep=lambda *a: None, storage="int8")
+    st.load_random(3)
+    ref.load_random(3)
+    np.testing.assert_array_equal(st.gather_lattice(), ref.gather_lattice())
+    with pytest.raises(ValueError):
+        LatticeStrips(workloads.IsingLattice2D(16, 64, beta=0.4407), device="cpu", halo=2,
+                      halfsweep=lambda *a: None, storage="bits")

@@ -156,6 +156,40 @@ def test_two_gpu_strips_reproduce_one_gpu(cuda_device, tmp_path, exchange):
     np.testing.assert_array_equal(res["trace"], tr1)
 
 
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_bit_packed_strips_equal_int8_strips(cuda_device, exchange):
+    """The bit-packed strips (k_ising2d_bits) and the int8 strips (k_ising2d_planes) evolve the same
+    lattice and trace, through a checkpoint and resume of the bit-packed ones."""
+    H, W, n = 128, 512, 12
+    prog = workloads.IsingLattice2D(H, W, beta=0.4407)
+    out = []
+    for storage in ("int8", "bits"):
+        st = LatticeStrips(prog, device=cuda_device, halo=4, exchange=exchange, storage=storage)
+        assert st.storage == storage and st.colours[0].dtype == (torch_dtype("int8") if storage == "int8"
+                                                                   else torch_dtype("int32"))
+        st.load_random(5)
+        st.prepare_rng(7, n)
+        st.run_sweeps(n // 2)
+        ck = st.checkpoint()
+        st.run_sweeps(n // 2)
+        st.check_errors()
+        out.append((st.gather_lattice(), st.trace()))
+        if storage == "bits":
+            st.restore(ck)
+            st.run_sweeps(n // 2)
+            st.check_errors()
+            np.testing.assert_array_equal(st.gather_lattice(), out[-1][0])
+        st.close()
+    np.testing.assert_array_equal(out[0][0], out[1][0])
+    np.testing.assert_array_equal(out[0][1], out[1][1])
+
+
+def torch_dtype(name):
+    import torch
+
+    return getattr(torch, name)
+
+
 def test_strip_checkpoint_continues_on_one_gpu(cuda_device):
     prog = workloads.IsingLattice2D(64, 128, beta=0.4407)
     a = LatticeStrips(prog, device=cuda_device, halo=4)

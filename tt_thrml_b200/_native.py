@@ -129,6 +129,11 @@ _SIGNATURES = {
         [c_vp, c_vp, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp,
          c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
     ),
+    "tthrml_ising2d_halfsweep_bits": (
+        c_i32,
+        [c_vp, c_vp, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp,
+         c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
+    ),
     "tthrml_ipc_malloc": (c_i32, [c_i64, c_vp, c_vp]),
     "tthrml_ipc_open": (c_i32, [c_vp, c_vp]),
     "tthrml_ipc_close": (c_i32, [c_vp]),

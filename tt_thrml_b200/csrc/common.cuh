@@ -152,6 +152,68 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t s
   return r;
 }
 
+// Bit-sliced lattice decision for 32 spins at once (count-symmetric threshold
+// tables).  L, R, U, D: the spins' left / right / up / down neighbour bits
+// (set = -1).  MS[i][n]: bit 23 - i of the count-n threshold as a 0 / ~0 mask.
+// The draw m of each spin (23 bits, bit 22 - b from word b % 4 of counter
+// (c0, c1, sweep, "LPL0" + b / 4), the spin's own bit position) is compared
+// with T(n) from the top bit down; the result has a bit set where m >= T(n),
+// i.e. where the spin goes to -1.  The first TTHRML_PLANES_EAGER chunks of four
+// planes are drawn unconditionally, the rest only while some spin is tied.
+__device__ __forceinline__ uint32_t planes_decide(uint32_t L, uint32_t R, uint32_t U, uint32_t D,
+                                                  const uint32_t (*MS)[8], uint32_t c0, uint32_t c1, uint32_t sweep,
+                                                  const PhiloxKeys& keys) {
+  // n = L + R + U + D in bit-planes n0, n1, n2 (n2 set only for n = 4)
+  const uint32_t s1 = L ^ R, k1 = L & R, s2 = U ^ D, k2 = U & D;
+  const uint32_t n0 = s1 ^ s2, t = s1 & s2;
+  const uint32_t n1 = k1 ^ k2 ^ t, n2 = (k1 & k2) | (t & (k1 | k2));
+  auto tbit = [&](int i) -> uint32_t {  // the threshold bit of every spin, from its count
+    const uint4 a = *reinterpret_cast<const uint4*>(&MS[i][0]);
+    const uint32_t m4 = MS[i][4];
+    const uint32_t lo = (n0 & a.y) | (~n0 & a.x), hi = (n0 & a.w) | (~n0 & a.z);
+    const uint32_t g = (n1 & hi) | (~n1 & lo);
+    return (n2 & m4) | (~n2 & g);
+  };
+  uint32_t lt = tbit(0);  // decided "m < T" (only T = 2^23 so far)
+  uint32_t eq = ~lt;      // still tied with T
+  auto planes4 = [&](int ch) {
+    const u32x4 r = philox4x32_10(u32x4{c0, c1, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int b = 4 * ch + q;
+      if (b < 23) {
+        const uint32_t tb = tbit(b + 1), ub = word_of(r, q);
+        lt |= eq & tb & ~ub;
+        eq &= ~(tb ^ ub);
+      }
+    }
+  };
+#pragma unroll
+  for (int ch = 0; ch < TTHRML_PLANES_EAGER; ++ch) planes4(ch);
+#pragma unroll 1
+  for (int ch = TTHRML_PLANES_EAGER; ch < 6 && eq; ++ch) planes4(ch);
+  return ~lt;
+}
+
+// Fills MS[24][8] (see planes_decide) from a 16-entry threshold table whose
+// entry 2^n - 1 holds the count-n threshold; call with all threads, then sync.
+__device__ __forceinline__ void planes_masks(uint32_t (*MS)[8], const uint32_t* __restrict__ thresholds) {
+  if (threadIdx.x < 24 * 5) {
+    const int i = threadIdx.x / 5, n = threadIdx.x - 5 * i;
+    const uint32_t t = thresholds[(1u << n) - 1u];  // the pattern with the n lowest neighbours at -1
+    MS[i][n] = ((t >> (23 - i)) & 1u) ? 0xFFFFFFFFu : 0u;
+  }
+}
+
+// Byte-transposed 32-site masks (site s = 4j + k at bit 8k + j): the mask of
+// sites s - 1 (e = the bit of site -1) and s + 1 (e = the bit of site 32).
+__device__ __forceinline__ uint32_t sites_minus1(uint32_t M, uint32_t e) {
+  return (M << 8) | ((M >> 23) & 0xFEu) | e;
+}
+__device__ __forceinline__ uint32_t sites_plus1(uint32_t M, uint32_t e) {
+  return (M >> 8) | ((M << 23) & 0x7F000000u) | (e << 31);
+}
+
 // Categorical draw in Philox mode by inverse CDF from one uniform u, a sample
 // of softmax(theta): e_k = 2^((theta_k - max theta) * log2 e) (ex2.approx),
 // and the draw is the number of boundaries k < q - 1 that u reaches,

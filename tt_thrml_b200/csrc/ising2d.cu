@@ -215,11 +215,7 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
   // MS[i][n]: bit 23 - i of the count-n threshold as a 0 / ~0 mask (row 0: bit 23, set only for T = 2^23)
   __shared__ __align__(16) uint32_t MS[24][8];
   __shared__ long long red[2];
-  if (threadIdx.x < 24 * 5) {
-    const int i = threadIdx.x / 5, n = threadIdx.x - 5 * i;
-    const uint32_t t = thresholds[(1u << n) - 1u];  // the pattern with the n lowest neighbours at -1
-    MS[i][n] = ((t >> (23 - i)) & 1u) ? 0xFFFFFFFFu : 0u;
-  }
+  planes_masks(MS, thresholds);
   if (TRACE && threadIdx.x < 2) red[threadIdx.x] = 0;
   __syncthreads();
 
@@ -257,40 +253,10 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
     };
     const uint32_t M = signs(m0, m1), U = signs(u0, u1), D = signs(d0, d1);
     // site s - 1 (left, p = 0) and s + 1 (right, p = 1) in byte-transposed order
-    const uint32_t L = p ? M : (M << 8) | ((M >> 23) & 0xFEu) | e;
-    const uint32_t R = p ? (M >> 8) | ((M << 23) & 0x7F000000u) | (e << 31) : M;
-    // n = L + R + U + D in bit-planes n0, n1, n2 (n2 set only for n = 4)
-    const uint32_t s1 = L ^ R, c1 = L & R, s2 = U ^ D, c2 = U & D;
-    const uint32_t n0 = s1 ^ s2, t = s1 & s2;
-    const uint32_t n1 = c1 ^ c2 ^ t, n2 = (c1 & c2) | (t & (c1 | c2));
-    auto tbit = [&](int row) -> uint32_t {  // the threshold bit of every site, from its count
-      const uint4 a = *reinterpret_cast<const uint4*>(&MS[row][0]);
-      const uint32_t m4 = MS[row][4];
-      const uint32_t lo = (n0 & a.y) | (~n0 & a.x), hi = (n0 & a.w) | (~n0 & a.z);
-      const uint32_t g = (n1 & hi) | (~n1 & lo);
-      return (n2 & m4) | (~n2 & g);
-    };
-    uint32_t lt = tbit(0);  // decided "m < T" (only T = 2^23 so far)
-    uint32_t eq = ~lt;      // still tied with T
+    const uint32_t L = p ? M : sites_minus1(M, e);
+    const uint32_t R = p ? sites_plus1(M, e) : M;
     const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + j0) >> 5);
-    auto planes4 = [&](int ch) {
-      const u32x4 r = philox4x32_10(u32x4{(uint32_t)chain, g32, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int b = 4 * ch + q;
-        if (b < 23) {
-          const uint32_t tb = tbit(b + 1), ub = word_of(r, q);
-          lt |= eq & tb & ~ub;
-          eq &= ~(tb ^ ub);
-        }
-      }
-    };
-    // planes 0..11 unconditionally (nearly every warp needs them; the three calls overlap), then on demand
-#pragma unroll
-    for (int ch = 0; ch < TTHRML_PLANES_EAGER; ++ch) planes4(ch);
-#pragma unroll 1
-    for (int ch = TTHRML_PLANES_EAGER; ch < 6 && eq; ++ch) planes4(ch);
-    const uint32_t dn = ~lt;  // bit set: the site samples -1
+    const uint32_t dn = planes_decide(L, R, U, D, MS, (uint32_t)chain, g32, sweep, keys);  // bit set: -1
     uint32_t outw[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) outw[j] = ((dn >> j) & 0x01010101u) * 0xFEu + 0x01010101u;  // +1: 0x01, -1: 0xFF
@@ -342,6 +308,128 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
       if (colour == 1) atomicAdd(trace + 2 * (int64_t)sweep + 1, (unsigned long long)red[1]);
     }
   }
+}
+
+// The bit-sliced half-sweep on bit-packed rows: colour c of the strip is a
+// uint32 array [rows][W/64], word w of a row holding sites 32w .. 32w + 31 in
+// the byte-transposed order of k_ising2d_planes (site s at bit 8 (s % 4) +
+// s / 4), bit set = -1.  A thread updates one word: the other colour's words
+// at rows i - 1, i, i + 1 are the up, middle and down masks, the left or right
+// edge bit comes from the neighbouring word of the middle row, and the
+// decision and random bits are those of k_ising2d_planes, so both kernels
+// produce the same lattice.  Rows are 8x smaller than int8 rows and need no
+// sign gathering; the halo export stores words.
+template <bool TRACE>
+__global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS) k_ising2d_bits(
+    uint32_t* __restrict__ cc, const uint32_t* __restrict__ co, int64_t words, FastDiv div_words, int64_t rows_local,
+    int32_t wrap, int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
+    int64_t block_row0, const uint32_t* __restrict__ thresholds, int64_t chain, uint64_t seed, uint32_t sweep_base,
+    const tthrml_run_ctl* __restrict__ ctl, int64_t count_lo, int64_t count_hi, unsigned long long* __restrict__ trace,
+    int64_t trace_len, tthrml_halo_export ex) {
+  __shared__ __align__(16) uint32_t MS[24][8];
+  __shared__ long long red[2];
+  planes_masks(MS, thresholds);
+  if (TRACE && threadIdx.x < 2) red[threadIdx.x] = 0;
+  __syncthreads();
+
+  const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
+  const uint64_t sd = ctl ? ctl->seed : seed;
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
+  const int64_t half_w = words * 32;
+  const uint32_t items = (uint32_t)(row_hi - row_lo) * (uint32_t)words;  // < 2^31, checked by the host
+  long long mag = 0, bonds = 0;
+
+  for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+    const uint32_t ri = fdiv(it, div_words);
+    const int64_t i = row_lo + ri;
+    const int64_t w = (int64_t)(it - ri * (uint32_t)words);
+    int64_t Y = global_row0 + i;
+    if (Y >= height) Y -= height;
+    if (Y >= height) Y -= height;
+    const int p = (int)((Y + colour) & 1);
+    const int64_t iu = i == 0 ? (wrap ? rows_local - 1 : 0) : i - 1;
+    const int64_t id = i == rows_local - 1 ? (wrap ? 0 : i) : i + 1;
+    const uint32_t* rowc = co + i * words;
+    const uint32_t M = __ldg(rowc + w);
+    const uint32_t U = __ldg(co + iu * words + w), D = __ldg(co + id * words + w);
+    uint32_t L, R;
+    if (p) {  // right neighbours: site 0 of the next word (bit 0) is the edge
+      L = M;
+      R = sites_plus1(M, __ldg(rowc + (w + 1 == words ? 0 : w + 1)) & 1u);
+    } else {  // left neighbours: site 31 of the previous word (bit 31) is the edge
+      L = sites_minus1(M, __ldg(rowc + (w == 0 ? words - 1 : w - 1)) >> 31);
+      R = M;
+    }
+    const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + 32 * w) >> 5);
+    const uint32_t dn = planes_decide(L, R, U, D, MS, (uint32_t)chain, g32, sweep, keys);  // bit set: -1
+    if (TRACE && i >= count_lo && i < count_hi) {
+      const int nd = __popc(dn);
+      mag += 32 - 2 * nd;
+      if (colour == 1) {
+        const int ksum = __popc(L) + __popc(R) + __popc(U) + __popc(D);
+        const int mk = __popc(dn & L) + __popc(dn & R) + __popc(dn & U) + __popc(dn & D);
+        bonds += 4 * (32 - 2 * nd) - 2 * ksum + 4 * mk;
+      }
+    }
+    cc[i * words + w] = dn;
+    if (ex.rows) {  // boundary rows also go straight to the neighbours' mailboxes (peer memory)
+      const int64_t slot = (int64_t)(((sweep / ex.sweeps_per_period) + 1u) & 1u) * ex.slot_bytes;
+      bool sent = false;
+      if (ex.up && i >= ex.up_row0 && i < ex.up_row0 + ex.rows) {
+        reinterpret_cast<uint32_t*>(ex.up + slot)[(i - ex.up_row0) * words + w] = dn;
+        sent = true;
+      }
+      if (ex.down && i >= ex.down_row0 && i < ex.down_row0 + ex.rows) {
+        reinterpret_cast<uint32_t*>(ex.down + slot)[(i - ex.down_row0) * words + w] = dn;
+        sent = true;
+      }
+      if (sent) __threadfence_system();
+    }
+  }
+  if (TRACE) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mag += __shfl_xor_sync(0xffffffffu, mag, o);
+      bonds += __shfl_xor_sync(0xffffffffu, bonds, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red[0]), (unsigned long long)mag);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&red[1]), (unsigned long long)bonds);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && (int64_t)sweep < trace_len) {
+      atomicAdd(trace + 2 * (int64_t)sweep, (unsigned long long)red[0]);
+      if (colour == 1) atomicAdd(trace + 2 * (int64_t)sweep + 1, (unsigned long long)red[1]);
+    }
+  }
+}
+
+template <bool TRACE>
+int launch_ising_bits(uint32_t* cc, const uint32_t* co, int64_t words, int64_t rows_local, int32_t wrap,
+                      int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
+                      int64_t block_row0, const uint32_t* thresholds, int64_t chain, uint64_t seed, uint32_t sweep,
+                      const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi, unsigned long long* trace,
+                      int64_t trace_len, const tthrml_halo_export& ex, cudaStream_t s) {
+  static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
+  if (!per_sm) {
+    int dev = 0, n = 0, b = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_ising2d_bits<TRACE>, kIsingThreads, 0);
+    if (e != cudaSuccess) return cuda_status(e, "k_ising2d_bits set-up");
+    sms = n;
+    per_sm = b > 0 ? b : 1;
+  }
+  const int64_t items = (row_hi - row_lo) * words;
+  const int64_t need = (items + kIsingThreads - 1) / kIsingThreads;
+  const int64_t full = (int64_t)sms * per_sm;
+  const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
+  k_ising2d_bits<TRACE><<<grid, kIsingThreads, 0, s>>>(cc, co, words, make_fastdiv((uint32_t)words), rows_local, wrap,
+                                                      row_lo, row_hi, global_row0, height, colour, block_row0,
+                                                      thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace,
+                                                      trace_len, ex);
+  return launch_status("k_ising2d_bits launch");
 }
 
 template <bool TRACE>
@@ -524,4 +612,68 @@ extern "C" int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* othe
                                     global_row0, height, colour, block_row0, thresholds, fields, variates,
                                     variates_sweeps, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len,
                                     nullptr, stream);
+}
+
+extern "C" int tthrml_ising2d_halfsweep_bits(uint32_t* colour_state, const uint32_t* other_state, int64_t width,
+                                             int64_t rows_local, int32_t wrap_rows, int64_t row_lo, int64_t row_hi,
+                                             int64_t global_row0, int64_t height, int32_t colour, int64_t block_row0,
+                                             const uint32_t* thresholds, int64_t chain, uint64_t seed, uint32_t sweep,
+                                             const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi,
+                                             int64_t* trace, int64_t trace_len,
+                                             const tthrml_halo_export* export_host, void* stream) {
+  using namespace tthrml;
+  const int64_t words = width / 64;
+  tthrml_halo_export ex{};
+  if (export_host) {
+    ex = *export_host;
+    if (ex.rows < 0 || (ex.rows && (ex.sweeps_per_period == 0 || ex.slot_bytes < ex.rows * words * 4 ||
+                                    ((uintptr_t)ex.up % 4) || ((uintptr_t)ex.down % 4) || ex.slot_bytes % 4 ||
+                                    ex.up_row0 < 0 || ex.down_row0 < 0 || ex.up_row0 + ex.rows > rows_local ||
+                                    ex.down_row0 + ex.rows > rows_local))) {
+      set_error("tthrml_ising2d_halfsweep_bits: invalid halo export descriptor");
+      return TTHRML_ERR_ARG;
+    }
+  }
+  if (!colour_state || !other_state || !thresholds || (colour != 0 && colour != 1)) {
+    set_error("tthrml_ising2d_halfsweep_bits: invalid arguments");
+    return TTHRML_ERR_ARG;
+  }
+  if (width <= 0 || width % 64 || height <= 0 || height % 2 || rows_local <= 0 || block_row0 % 32) {
+    set_error("tthrml_ising2d_halfsweep_bits: width must be a positive multiple of 64, height positive and even, "
+              "block_row0 a multiple of 32 (got %lld x %lld, %lld)", (long long)height, (long long)width,
+              (long long)block_row0);
+    return TTHRML_ERR_ARG;
+  }
+  if (row_lo < 0 || row_hi > rows_local || row_lo > row_hi || global_row0 < 0 || global_row0 >= height ||
+      rows_local > 2 * height) {
+    set_error("tthrml_ising2d_halfsweep_bits: row range [%lld, %lld) outside the %lld local rows",
+              (long long)row_lo, (long long)row_hi, (long long)rows_local);
+    return TTHRML_ERR_ARG;
+  }
+  if (!wrap_rows && (row_lo < 1 || row_hi > rows_local - 1)) {
+    set_error("tthrml_ising2d_halfsweep_bits: without wrapping, updated rows need a halo row on both sides");
+    return TTHRML_ERR_ARG;
+  }
+  if (wrap_rows && rows_local != height) {
+    set_error("tthrml_ising2d_halfsweep_bits: wrapping rows needs the whole lattice (rows_local == height)");
+    return TTHRML_ERR_ARG;
+  }
+  if (((uintptr_t)colour_state % 4) || ((uintptr_t)other_state % 4)) {
+    set_error("tthrml_ising2d_halfsweep_bits: buffers must be 4-byte aligned");
+    return TTHRML_ERR_ARG;
+  }
+  if ((row_hi - row_lo) * words >= (1ll << 31)) {
+    set_error("tthrml_ising2d_halfsweep_bits: more than 2^31 words in one launch");
+    return TTHRML_ERR_UNSUPPORTED;
+  }
+  if (row_hi == row_lo) return TTHRML_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned long long* tr = reinterpret_cast<unsigned long long*>(trace);
+  if (trace)
+    return launch_ising_bits<true>(colour_state, other_state, words, rows_local, wrap_rows, row_lo, row_hi,
+                                   global_row0, height, colour, block_row0, thresholds, chain, seed, sweep, ctl,
+                                   count_lo, count_hi, tr, trace_len, ex, s);
+  return launch_ising_bits<false>(colour_state, other_state, words, rows_local, wrap_rows, row_lo, row_hi,
+                                  global_row0, height, colour, block_row0, thresholds, chain, seed, sweep, ctl,
+                                  count_lo, count_hi, tr, trace_len, ex, s);
 }

@@ -58,11 +58,7 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     TH[threadIdx.x] = (int32_t)(thresholds[threadIdx.x] >> 7);
     TL[threadIdx.x] = thresholds[threadIdx.x] & 127u;
   }
-  if (PLANES && threadIdx.x < 24 * 5) {
-    const int i = threadIdx.x / 5, n = threadIdx.x - 5 * i;
-    const uint32_t t = thresholds[(1u << n) - 1u];  // the pattern with the n lowest neighbours at -1
-    MS[i][n] = ((t >> (23 - i)) & 1u) ? 0xFFFFFFFFu : 0u;
-  }
+  if (PLANES) planes_masks(MS, thresholds);
   for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
     const int c = i / half_sites, r = i - c * half_sites;
     const int64_t row = (c ? row0_c1 : row0_c0) + r;
@@ -101,36 +97,8 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
           L = __funnelshift_l(ow[Y * qw + (wq == 0 ? qw - 1 : wq - 1)], M, 8);
           R = M;
         }
-        const uint32_t s1 = L ^ R, c1 = L & R, s2 = U ^ D, c2 = U & D;
-        const uint32_t n0 = s1 ^ s2, tt = s1 & s2;
-        const uint32_t n1 = c1 ^ c2 ^ tt, n2 = (c1 & c2) | (tt & (c1 | c2));
-        auto tbit = [&](int i) -> uint32_t {
-          const uint4 a = *reinterpret_cast<const uint4*>(&MS[i][0]);
-          const uint32_t m4 = MS[i][4];
-          const uint32_t lo = (n0 & a.y) | (~n0 & a.x), hi = (n0 & a.w) | (~n0 & a.z);
-          const uint32_t g2 = (n1 & hi) | (~n1 & lo);
-          return (n2 & m4) | (~n2 & g2);
-        };
-        uint32_t lt = tbit(0), eq = ~lt;
         const uint32_t quad = (uint32_t)((row0 + r) >> 2);
-        auto planes4 = [&](int ch) {
-          const u32x4 rr = philox4x32_10(u32x4{gc0 >> 3, quad, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int b = 4 * ch + k;
-            if (b < 23) {
-              const uint32_t tb = tbit(b + 1), ub = word_of(rr, k);
-              lt |= eq & tb & ~ub;
-              eq &= ~(tb ^ ub);
-            }
-          }
-        };
-        // planes 0..11 unconditionally (nearly every warp needs them; the calls overlap), then on demand
-#pragma unroll
-        for (int ch = 0; ch < TTHRML_PLANES_EAGER; ++ch) planes4(ch);
-#pragma unroll 1
-        for (int ch = TTHRML_PLANES_EAGER; ch < 6 && eq; ++ch) planes4(ch);
-        mw[q] = ~lt;  // bit set: the chain's site samples -1
+        mw[q] = planes_decide(L, R, U, D, MS, gc0 >> 3, quad, sweep, keys);  // bit set: the chain's site samples -1
       }
     }
     for (int r = threadIdx.x; !PLANES && r < half_sites; r += blockDim.x) {

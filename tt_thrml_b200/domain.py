@@ -67,6 +67,11 @@ class LatticeStrips:
     halfsweep: the half-sweep implementation (default: the CUDA kernel
     tthrml_ising2d_halfsweep); tests substitute a host restatement to check
     the decomposition logic on CPU ranks.
+    storage: "int8" (one byte per site, [rows][W/2] per colour) or "bits" (32
+    sites per 32-bit word, [rows][W/64] per colour, site s of a word at bit
+    8 (s % 4) + s / 4, bit set = -1; the bit-sliced kernel reads and writes
+    them directly, 8x fewer bytes).  Default: "bits" for a count-symmetric
+    lattice of width % 256 == 0 with the CUDA kernel, else "int8".
     exchange: "p2p" (default with the CUDA kernel): the last two half-sweeps
     of a period store the boundary rows straight into the neighbours'
     mailboxes in peer memory (CUDA IPC over NVLink), a flag publishes the
@@ -76,7 +81,8 @@ class LatticeStrips:
     """
 
     def __init__(self, program, *, device=None, halo: int = 32, process_group=None,
-                 halfsweep: Callable | None = None, cuda_graphs: bool = True, exchange: str = "p2p"):
+                 halfsweep: Callable | None = None, cuda_graphs: bool = True, exchange: str = "p2p",
+                 storage: str | None = None):
         torch = _torch()
         st = program.tt_stencil()
         if st.get("kind") != "ising2d":
@@ -116,8 +122,20 @@ class LatticeStrips:
         self.fields_host, self.thresholds_host = fields, thr
         # Philox layout of the half-sweeps, the same as the executor's single-chain lattice plan
         self.rng_layout = ising_stencil_layout(thr, self.W)
-        self.colours = [torch.empty((self.rows_local, self.W // 2), dtype=torch.int8, device=self.device)
-                        for _ in range(2)]
+        bits_ok = self.rng_layout == "planes" and self.W % 256 == 0
+        if storage is None:
+            storage = "bits" if bits_ok and not self._custom else "int8"
+        if storage not in ("int8", "bits") or (storage == "bits" and not bits_ok):
+            raise ValueError(f"storage must be 'int8' or, for a count-symmetric lattice of width % 256 == 0, "
+                             f"'bits' (got {storage!r})")
+        self.storage = storage
+        self.row_bytes = self.W // 2 if storage == "int8" else self.W // 16
+        if storage == "int8":
+            self.colours = [torch.empty((self.rows_local, self.W // 2), dtype=torch.int8, device=self.device)
+                            for _ in range(2)]
+        else:
+            self.colours = [torch.empty((self.rows_local, self.W // 64), dtype=torch.int32, device=self.device)
+                            for _ in range(2)]
         self.fields = torch.from_numpy(fields).to(self.device)
         self.thresholds = torch.from_numpy(thr.view(np.int32)).to(self.device)
         self.seed = 0
@@ -146,8 +164,54 @@ class LatticeStrips:
         for c in range(2):
             cols = (np.arange(self.W // 2)[None, :] * 2) + ((rows[:, None] + c) & 1)
             part = np.take_along_axis(s[rows], cols, axis=1)
-            self.colours[c].copy_(torch.from_numpy(np.ascontiguousarray(part)))
+            self._store_rows(c, 0, torch.from_numpy(np.ascontiguousarray(part)))
         self._after_load()
+
+    # bit-packed rows: site s of a 32-site group at bit 8 (s % 4) + s / 4, bit set = -1
+    _PACK_ROWS = 1024  # rows per packing chunk (bounds the int64 temporaries)
+
+    @staticmethod
+    def _bit_shifts(device):
+        torch = _torch()
+        j = torch.arange(8, device=device, dtype=torch.int64)[:, None]
+        k = torch.arange(4, device=device, dtype=torch.int64)[None, :]
+        return 8 * k + j  # [j][k] for site 4j + k
+
+    @classmethod
+    def pack_rows(cls, rows):
+        """int8 +-1 rows [n][W/2] -> int32 words [n][W/64] (bit-packed storage order)."""
+        torch = _torch()
+        n, half = rows.shape
+        b = (rows < 0).reshape(n, half // 32, 8, 4).to(torch.int64)
+        words = (b << cls._bit_shifts(rows.device)).sum(dim=(-1, -2))
+        return torch.where(words >= 2**31, words - 2**32, words).to(torch.int32)
+
+    @classmethod
+    def unpack_rows(cls, words):
+        """int32 words [n][W/64] -> int8 +-1 rows [n][W/2]."""
+        torch = _torch()
+        n, nw = words.shape
+        w = words.to(torch.int64) & 0xFFFFFFFF
+        bits = (w[:, :, None, None] >> cls._bit_shifts(words.device)) & 1
+        return (1 - 2 * bits).to(torch.int8).reshape(n, nw * 32)
+
+    def _store_rows(self, c: int, row0: int, rows) -> None:
+        """Writes int8 +-1 rows [n][W/2] (any device) into local rows [row0, row0 + n) of colour c."""
+        if self.storage == "int8":
+            self.colours[c][row0 : row0 + rows.shape[0]].copy_(rows, non_blocking=True)
+            return
+        for a in range(0, rows.shape[0], self._PACK_ROWS):
+            part = rows[a : a + self._PACK_ROWS].to(self.device, non_blocking=True)
+            self.colours[c][row0 + a : row0 + a + part.shape[0]].copy_(self.pack_rows(part))
+
+    def _own_rows(self, c: int):
+        """The own rows [D, D + h) of colour c as int8 +-1 rows [h][W/2] on the device."""
+        torch = _torch()
+        own = self.colours[c][self.D : self.D + self.h]
+        if self.storage == "int8":
+            return own
+        return torch.cat([self.unpack_rows(own[a : a + self._PACK_ROWS])
+                          for a in range(0, self.h, self._PACK_ROWS)])
 
     def load_split_colours(self, colour0, colour1) -> None:
         """Loads the lattice from its two split-colour arrays [H][W/2] (host, ideally pinned, or device)."""
@@ -164,22 +228,24 @@ class LatticeStrips:
                     raise ValueError(f"expected an int8 ({self.H}, {self.W // 2}) array, got {tuple(t.shape)}")
                 for run in runs:
                     y = int(rows[run[0]])
-                    self.colours[c][run[0] : run[-1] + 1].copy_(t[y : y + len(run)], non_blocking=True)
+                    self._store_rows(c, int(run[0]), t[y : y + len(run)])
         self._after_load()
 
     def load_random(self, seed: int) -> None:
         """Uniform +-1 spins from a hash of (seed, site): identical for every strip decomposition."""
         torch = _torch()
-        rows = torch.from_numpy(self._rows_of_local().astype(np.int64)).to(self.device)
+        all_rows = torch.from_numpy(self._rows_of_local().astype(np.int64)).to(self.device)
+        j = torch.arange(self.W // 2, device=self.device, dtype=torch.int64)
         for c in range(2):
-            j = torch.arange(self.W // 2, device=self.device, dtype=torch.int64)
-            x = 2 * j[None, :] + ((rows[:, None] + c) & 1)
-            z = rows[:, None] * self.W + x + (int(seed) & 0x3FFFFFFF) * 0x9E3779B1
-            # 64-bit mix (splitmix64 finaliser constants), wrapping arithmetic
-            z = (z ^ (z >> 30)) * -4658895280553007687
-            z = (z ^ (z >> 27)) * -7723592293110705685
-            z = z ^ (z >> 31)
-            self.colours[c].copy_(torch.where((z & 1) == 1, 1, -1).to(torch.int8))
+            for a in range(0, self.rows_local, self._PACK_ROWS):
+                rows = all_rows[a : a + self._PACK_ROWS]
+                x = 2 * j[None, :] + ((rows[:, None] + c) & 1)
+                z = rows[:, None] * self.W + x + (int(seed) & 0x3FFFFFFF) * 0x9E3779B1
+                # 64-bit mix (splitmix64 finaliser constants), wrapping arithmetic
+                z = (z ^ (z >> 30)) * -4658895280553007687
+                z = (z ^ (z >> 27)) * -7723592293110705685
+                z = z ^ (z >> 31)
+                self._store_rows(c, a, torch.where((z & 1) == 1, 1, -1).to(torch.int8))
         self._after_load()
 
     def _after_load(self) -> None:
@@ -190,7 +256,7 @@ class LatticeStrips:
         """The full lattice [H][W] of +-1 spins (all-gathered over ranks)."""
         torch = _torch()
         self._sync()
-        own = [self.colours[c][self.D : self.D + self.h].cpu().numpy() for c in range(2)]
+        own = [self._own_rows(c).cpu().numpy() for c in range(2)]
         strip = np.empty((self.h, self.W), dtype=np.int8)
         rows = self.y0 + np.arange(self.h)
         for c in range(2):
@@ -229,6 +295,18 @@ class LatticeStrips:
                         export=None) -> None:
         c, o = self.colours[colour], self.colours[1 - colour]
         trace = self._trace
+        if self.storage == "bits":
+            nat.check(
+                self._lib.tthrml_ising2d_halfsweep_bits(
+                    c.data_ptr(), o.data_ptr(), self.W, self.rows_local, 0, row_lo, row_hi, self.global_row0, self.H,
+                    colour, self.block_rows[colour], self.thresholds.data_ptr(), 0, self.seed, sweep, ctl_ptr,
+                    self.D, self.D + self.h, None if trace is None else trace.data_ptr(),
+                    0 if trace is None else trace.shape[0], None if export is None else ctypes.byref(export),
+                    nat.stream_handle(stream),
+                ),
+                "tthrml_ising2d_halfsweep_bits",
+            )
+            return
         if self.rng_layout == "planes":
             nat.check(
                 self._lib.tthrml_ising2d_halfsweep_planes(
@@ -262,8 +340,9 @@ class LatticeStrips:
         if p2p:
             m = self._p2p
             nat.check(
-                self._lib.tthrml_halo_import(
-                    self.colours[0].data_ptr(), self.colours[1].data_ptr(), self.W, self.D, 0, self.h + self.D,
+                self._lib.tthrml_halo_import(  # rows of row_bytes bytes: "width" 2 * row_bytes
+                    self.colours[0].data_ptr(), self.colours[1].data_ptr(), 2 * self.row_bytes, self.D, 0,
+                    self.h + self.D,
                     m["own"], m["own"] + m["flags_off"], per, sweep0, ctl_ptr, m["error"].data_ptr(), h,
                 ),
                 "tthrml_halo_import",
@@ -289,9 +368,9 @@ class LatticeStrips:
         if self._p2p is not None:
             return
         nat.bind_device(self.device.index)
-        D, hw = self.D, self.W // 2
-        plane = D * hw
-        mb_bytes = 8 * plane  # [2 slots][2 directions][2 colours][D][W/2]
+        D = self.D
+        plane = D * self.row_bytes
+        mb_bytes = 8 * plane  # [2 slots][2 directions][2 colours][D][row bytes]
         flags_off = (mb_bytes + 255) // 256 * 256
         own = ctypes.c_void_p()
         handle = (ctypes.c_char * 64)()
@@ -347,14 +426,13 @@ class LatticeStrips:
         if self.sweep > 0:
             p_done = self.sweep // per
             slot = (p_done & 1) * 4 * m["plane"]
-            hw = self.W // 2
             for c in range(2):
                 ex = m["export"][c]
                 top = self.colours[c][self.D : 2 * self.D]
                 bottom = self.colours[c][self.h : self.h + self.D]
                 for dst, src in ((ex.up + slot, top.data_ptr()), (ex.down + slot, bottom.data_ptr())):
-                    nat.check(self._lib.tthrml_memcpy(ctypes.c_void_p(dst), ctypes.c_void_p(src), self.D * hw, None),
-                              "tthrml_memcpy")
+                    nat.check(self._lib.tthrml_memcpy(ctypes.c_void_p(dst), ctypes.c_void_p(src),
+                                                      self.D * self.row_bytes, None), "tthrml_memcpy")
             nat.check(
                 self._lib.tthrml_halo_signal(m["up"] + m["flags_off"] + 4, m["down"] + m["flags_off"], per,
                                              self.sweep - per, None, None),
@@ -501,6 +579,7 @@ class LatticeStrips:
             "strips": self.world,
             "rank": self.rank,
             "halo": self.D,
+            "storage": self.storage,
             "colours": [c.cpu().numpy() for c in self.colours],
             "sweep": int(self.sweep),
             "seed": int(self.seed),
@@ -509,8 +588,9 @@ class LatticeStrips:
 
     def restore(self, ckpt: dict) -> None:
         torch = _torch()
-        want = ("tt_thrml_b200.strips/1", (self.H, self.W), self.world, self.rank, self.D)
-        got = (ckpt.get("format"), tuple(ckpt["dims"]), ckpt["strips"], ckpt["rank"], ckpt["halo"])
+        want = ("tt_thrml_b200.strips/1", (self.H, self.W), self.world, self.rank, self.D, self.storage)
+        got = (ckpt.get("format"), tuple(ckpt["dims"]), ckpt["strips"], ckpt["rank"], ckpt["halo"],
+               ckpt.get("storage", "int8"))
         if want != got:
             raise ValueError(f"checkpoint {got} does not match this decomposition {want}")
         for dst, src in zip(self.colours, ckpt["colours"]):
