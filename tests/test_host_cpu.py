@@ -421,3 +421,55 @@ def test_merge_rows_concatenates_terms_row_by_row():
     assert rp.tolist() == [0, 3, 5, 6]
     assert vals.tolist() == [1.0, 2.0, 4.0, 5.0, 6.0, 3.0]
     assert cols.tolist() == [10, 11, 20, 21, 22, 12]
+
+
+def _device_categorical_rule(theta, q, qmax, u, ref):
+    """float32 restatement of the kernels' inverse-CDF draw (csrc/common.cuh): weights relative to `ref`,
+    categories reversed for u >= 1/2 over qmax slots (zeros past q), one running sum, one compare per
+    boundary, mirrored count; None when the sum overflows (the kernels then retry relative to the max)."""
+    f32 = np.float32
+    c = f32(1.44269502162933349609375)
+    ml = f32(f32(ref) * c)
+    with np.errstate(over="ignore"):  # ex2 of a large argument is +inf, as on the device
+        # fma(theta, c, -ml): one rounding of the exact product minus ml
+        e = [f32(np.exp2(np.float64(f32(np.float64(theta[k]) * np.float64(c) - np.float64(ml)))))
+             if k < q else f32(0.0) for k in range(qmax)]
+    low = u < 0.5
+    order = e if low else e[::-1]
+    s, h = f32(0.0), []
+    for j, x in enumerate(order):
+        s = x if j == 0 else f32(s + x)
+        h.append(s)
+    if not s <= f32(3.0e38):
+        return None
+    t = f32(f32(u if low else f32(1.0) - f32(u)) * s)
+    cnt = sum(1 for j in range(qmax - 1) if h[j] <= t)
+    return cnt if low else qmax - 1 - cnt
+
+
+def test_categorical_draw_rule_matches_exact_decision():
+    """The kernels' categorical rule agrees with the exact decision (double precision inverse CDF)
+    wherever the draw is more than 1e-5 from a boundary in logit units, for q <= qmax, both halves
+    of u, and large fields that take the overflow fallback."""
+    rng = np.random.default_rng(12)
+    checked = 0
+    for trial in range(4000):
+        q = int(rng.integers(1, 9))
+        qmax = 8 if trial % 2 else q
+        scale = 3.0 if trial % 5 else 60.0
+        theta = (rng.standard_normal(q) * scale).astype(np.float32)
+        theta[0] = theta[0] if trial % 7 else np.float32(-80.0)  # first category far below: overflow path
+        u = float((2 * int(rng.integers(0, 2**23)) + 1) * 2.0**-24)
+        got = _device_categorical_rule(theta, q, qmax, u, theta[0])
+        if got is None:
+            got = _device_categorical_rule(theta, q, qmax, u, theta.max())
+        ex = np.exp(theta.astype(np.float64) - theta.max())
+        head = np.cumsum(ex)
+        tail = np.cumsum(ex[::-1])[::-1]
+        want = int(np.sum(head[:-1] <= u * head[-1]))
+        lu = np.log(u) - np.log1p(-u)
+        margin = min((abs(lu - (np.log(head[k]) - np.log(tail[k + 1]))) for k in range(q - 1)), default=np.inf)
+        if margin > 1e-5:
+            assert got == want, (trial, q, qmax, theta, u, got, want)
+            checked += 1
+    assert checked > 3900
