@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
   const uint32_t words = div_words.d;
   const int64_t half = (int64_t)X * Y * Z / 2;
   const uint32_t items = (uint32_t)(half * words);  // < 2^31, checked by the host
-  const int64_t XY = (int64_t)X * Y;
+  const uint32_t XY = (uint32_t)X * (uint32_t)Y;  // sites < 2^31, checked by the host: 32-bit coordinates
   const int64_t vs = VARIATES ? (int64_t)(sweep % (uint32_t)(variates_sweeps > 0 ? variates_sweeps : 1)) : 0;
 
   for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
@@ -78,22 +78,29 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     const int32_t xm = x == 0 ? X - 1 : x - 1, xp = x == X - 1 ? 0 : x + 1;
     const int32_t ym = y == 0 ? Y - 1 : y - 1, yp = y == Y - 1 ? 0 : y + 1;
     const int32_t zm = z == 0 ? Z - 1 : z - 1, zp = z == Z - 1 ? 0 : z + 1;
-    const int64_t zy = (int64_t)z * XY + (int64_t)y * X;
-    int64_t nb[6];
-    nb[0] = (zy + xm) >> 1;
-    nb[1] = (zy + xp) >> 1;
-    nb[2] = ((int64_t)z * XY + (int64_t)ym * X + x) >> 1;
-    nb[3] = ((int64_t)z * XY + (int64_t)yp * X + x) >> 1;
-    nb[4] = ((int64_t)zm * XY + (int64_t)y * X + x) >> 1;
-    nb[5] = ((int64_t)zp * XY + (int64_t)y * X + x) >> 1;
+    const uint32_t zXY = (uint32_t)z * XY, yX = (uint32_t)y * (uint32_t)X;
+    uint32_t nb[6];  // neighbour block rows
+    nb[0] = (zXY + yX + (uint32_t)xm) >> 1;
+    nb[1] = (zXY + yX + (uint32_t)xp) >> 1;
+    nb[2] = (zXY + (uint32_t)ym * (uint32_t)X + (uint32_t)x) >> 1;
+    nb[3] = (zXY + (uint32_t)yp * (uint32_t)X + (uint32_t)x) >> 1;
+    nb[4] = ((uint32_t)zm * XY + yX + (uint32_t)x) >> 1;
+    nb[5] = ((uint32_t)zp * XY + yX + (uint32_t)x) >> 1;
     uint32_t nw[6];
 #pragma unroll
     for (int j = 0; j < 6; ++j)
-      nw[j] = __ldg(reinterpret_cast<const uint32_t*>(state + (source_row0 + nb[j]) * C) + w);
+      nw[j] = __ldg(reinterpret_cast<const uint32_t*>(state + (uint64_t)((uint32_t)source_row0 + nb[j]) *
+                                                                  (uint32_t)C) + w);
 
     float b[kPottsQ];
+    if (QC == kPottsQ) {  // the site's bias row as two 16-byte loads (the host checks the alignment)
+      const float4* bp = reinterpret_cast<const float4*>(bias + (size_t)r * kPottsQ);
+      const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+      b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+    } else {
 #pragma unroll
-    for (int k = 0; k < kPottsQ; ++k) b[k] = k < q ? __ldg(bias + r * q + k) : 0.0f;
+      for (int k = 0; k < kPottsQ; ++k) b[k] = k < q ? __ldg(bias + r * q + k) : 0.0f;
+    }
 
     const int64_t row = target_row0 + r;
     uint32_t out = 0u;
@@ -197,6 +204,10 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
     set_error("tthrml_potts3d_step: sites x chain words must stay below 2^31 per launch");
     return TTHRML_ERR_UNSUPPORTED;
   }
+  if (source_row0 + half >= (1ll << 31) || target_row0 + half >= (1ll << 31)) {
+    set_error("tthrml_potts3d_step: block rows must stay below 2^31");
+    return TTHRML_ERR_UNSUPPORTED;
+  }
   if (target_row0 < 0 || source_row0 < 0 || (target_row0 < source_row0 + half && source_row0 < target_row0 + half)) {
     set_error("tthrml_potts3d_step: target and source blocks must be disjoint row ranges");
     return TTHRML_ERR_ARG;
@@ -205,11 +216,12 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
 #define TTHRML_POTTS_LAUNCH(V, QC)                                                                          \
   return launch_potts<V, QC>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset, \
                              variates, variates_sweeps, seed, sweep, ctl, s)
+  const bool q8 = q == kPottsQ && (uintptr_t)bias % 16 == 0;  // the q = 8 kernel reads 16-byte bias vectors
   if (variates) {
-    if (q == kPottsQ) TTHRML_POTTS_LAUNCH(true, kPottsQ);
+    if (q8) TTHRML_POTTS_LAUNCH(true, kPottsQ);
     TTHRML_POTTS_LAUNCH(true, 0);
   }
-  if (q == kPottsQ) TTHRML_POTTS_LAUNCH(false, kPottsQ);
+  if (q8) TTHRML_POTTS_LAUNCH(false, kPottsQ);
   TTHRML_POTTS_LAUNCH(false, 0);
 #undef TTHRML_POTTS_LAUNCH
 }
