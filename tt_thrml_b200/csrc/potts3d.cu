@@ -36,10 +36,15 @@ constexpr int kRows = kPottsQ + 1;  // matrix rows per neighbour category, the l
 // a pair-sum row holds kPottsQ floats padded to kRowFloats: rows 48 bytes apart
 // spread the random per-lane row reads over all shared-memory banks
 constexpr int kRowFloats = TTHRML_POTTS_ROW_FLOATS;
+#ifndef TTHRML_POTTS_WIDE
+#define TTHRML_POTTS_WIDE 1
+#endif
 
 // QC: the category count as a compile-time constant (8, the common case: no
 // per-category predicates) or 0 (any q <= 8, read from the argument).
-template <bool VARIATES, int QC>
+// WPT: chain words (4 chains each) per thread; 2 shares a site's coordinates,
+// neighbour addresses and bias row between 8 chains.
+template <bool VARIATES, int QC, int WPT>
 __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
     int32_t colour, int64_t target_row0, int64_t source_row0, const float* __restrict__ J,
@@ -61,7 +66,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
   const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
   const uint64_t sd = ctl ? ctl->seed : seed;
   const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
-  const uint32_t words = div_words.d;
+  const uint32_t words = div_words.d;  // thread items per site
   const int64_t half = (int64_t)X * Y * Z / 2;
   const uint32_t items = (uint32_t)(half * words);  // < 2^31, checked by the host
   const uint32_t XY = (uint32_t)X * (uint32_t)Y;  // sites < 2^31, checked by the host: 32-bit coordinates
@@ -69,7 +74,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
 
   for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
     const uint32_t r = fdiv(it, div_words);
-    const uint32_t w = it - r * words;
+    const uint32_t w = (it - r * words) * WPT;  // first chain word of this thread
     const uint32_t even = 2 * r;
     const uint32_t yz = fdiv(even, div_x);
     const int32_t z = (int32_t)fdiv(yz, div_y);
@@ -86,11 +91,19 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     nb[3] = (zXY + (uint32_t)yp * (uint32_t)X + (uint32_t)x) >> 1;
     nb[4] = ((uint32_t)zm * XY + yX + (uint32_t)x) >> 1;
     nb[5] = ((uint32_t)zp * XY + yX + (uint32_t)x) >> 1;
-    uint32_t nw[6];
+    uint32_t nw[6][WPT];
 #pragma unroll
-    for (int j = 0; j < 6; ++j)
-      nw[j] = __ldg(reinterpret_cast<const uint32_t*>(state + (uint64_t)((uint32_t)source_row0 + nb[j]) *
-                                                                  (uint32_t)C) + w);
+    for (int j = 0; j < 6; ++j) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(state + (uint64_t)((uint32_t)source_row0 + nb[j]) *
+                                                                          (uint32_t)C) + w;
+      if (WPT == 2) {
+        const uint2 v2 = __ldg(reinterpret_cast<const uint2*>(src));
+        nw[j][0] = v2.x;
+        nw[j][WPT - 1] = v2.y;
+      } else {
+        nw[j][0] = __ldg(src);
+      }
+    }
 
     float b[kPottsQ];
     if (QC == kPottsQ) {  // the site's bias row as two 16-byte loads (the host checks the alignment)
@@ -103,10 +116,13 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     }
 
     const int64_t row = target_row0 + r;
-    uint32_t out = 0u;
+    uint32_t out[WPT];
+#pragma unroll
+    for (int ww = 0; ww < WPT; ++ww) {
+    out[ww] = 0u;
     u32x4 rr{0u, 0u, 0u, 0u};
     if (!VARIATES)
-      rr = philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w), (uint32_t)row, sweep, kSaltCat}, keys);
+      rr = philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w + ww), (uint32_t)row, sweep, kSaltCat}, keys);
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       float theta[kPottsQ];
@@ -114,8 +130,8 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
       for (int k = 0; k < kPottsQ; ++k) theta[k] = b[k];
 #pragma unroll
       for (int a = 0; a < 3; ++a) {
-        const uint32_t s0 = min(__byte_perm(nw[2 * a], 0u, 0x4440u + v), (uint32_t)kPottsQ);
-        const uint32_t s1 = min(__byte_perm(nw[2 * a + 1], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+        const uint32_t s0 = min(__byte_perm(nw[2 * a][ww], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+        const uint32_t s1 = min(__byte_perm(nw[2 * a + 1][ww], 0u, 0x4440u + v), (uint32_t)kPottsQ);
         const float4* pp = reinterpret_cast<const float4*>(&P[a][s0][s1][0]);
         const float4 p0 = pp[0], p1 = pp[1];
         theta[0] = __fadd_rn(theta[0], p0.x);
@@ -129,7 +145,7 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
       }
       int cat;
       if (VARIATES) {
-        const float* g = variates + ((vs * half + r) * q) * C + 4 * w + v;
+        const float* g = variates + ((vs * half + r) * q) * C + 4 * (w + ww) + v;
         cat = 0;
         float best = 0.0f;
 #pragma unroll
@@ -145,13 +161,18 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
       } else {
         cat = categorical_icdf(theta, q, uniform_open(word_of(rr, v)));
       }
-      out |= (uint32_t)cat << (8 * v);
+      out[ww] |= (uint32_t)cat << (8 * v);
     }
-    reinterpret_cast<uint32_t*>(state + row * C)[w] = out;
+    }
+    uint32_t* dst = reinterpret_cast<uint32_t*>(state + row * C) + w;
+    if (WPT == 2)
+      *reinterpret_cast<uint2*>(dst) = make_uint2(out[0], out[WPT - 1]);
+    else
+      *dst = out[0];
   }
 }
 
-template <bool VARIATES, int QC>
+template <bool VARIATES, int QC, int WPT>
 int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int32_t colour, int64_t target_row0,
                  int64_t source_row0, const float* J, const float* bias, int32_t q, int64_t chain_offset,
                  const float* variates, int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
@@ -162,16 +183,17 @@ int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int3
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_potts3d<VARIATES, QC>, kPottsThreads, 0);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_potts3d<VARIATES, QC, WPT>, kPottsThreads, 0);
     if (e != cudaSuccess) return cuda_status(e, "k_potts3d set-up");
     sms = n;
     per_sm = b > 0 ? b : 1;
   }
-  const int64_t items = (int64_t)X * Y * Z / 2 * (C / 4);
+  const int64_t items = (int64_t)X * Y * Z / 2 * (C / (4 * WPT));
   const int64_t need = (items + kPottsThreads - 1) / kPottsThreads;
   const int64_t full = (int64_t)sms * per_sm;
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
-  k_potts3d<VARIATES, QC><<<grid, kPottsThreads, 0, s>>>(state, C, X, Y, Z, make_fastdiv((uint32_t)(C / 4)),
+  k_potts3d<VARIATES, QC, WPT><<<grid, kPottsThreads, 0, s>>>(state, C, X, Y, Z,
+                                                     make_fastdiv((uint32_t)(C / (4 * WPT))),
                                                      make_fastdiv((uint32_t)X), make_fastdiv((uint32_t)Y), colour,
                                                      target_row0, source_row0, J, bias, q, chain_offset, variates,
                                                      variates_sweeps, seed, sweep, ctl);
@@ -213,10 +235,12 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
     return TTHRML_ERR_ARG;
   }
   cudaStream_t s = (cudaStream_t)stream;
-#define TTHRML_POTTS_LAUNCH(V, QC)                                                                          \
-  return launch_potts<V, QC>(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset, \
-                             variates, variates_sweeps, seed, sweep, ctl, s)
+#define TTHRML_POTTS_LAUNCH(V, QC)                                                                              \
+  return (wide ? launch_potts<V, QC, 2> : launch_potts<V, QC, 1>)(state, n_chains, X, Y, Z, colour, target_row0,    \
+                                                                  source_row0, J, bias, q, chain_offset, variates, \
+                                                                  variates_sweeps, seed, sweep, ctl, s)
   const bool q8 = q == kPottsQ && (uintptr_t)bias % 16 == 0;  // the q = 8 kernel reads 16-byte bias vectors
+  const bool wide = TTHRML_POTTS_WIDE && n_chains % 8 == 0;   // 8 chains per thread
   if (variates) {
     if (q8) TTHRML_POTTS_LAUNCH(true, kPottsQ);
     TTHRML_POTTS_LAUNCH(true, 0);
