@@ -39,6 +39,9 @@ constexpr int kRowFloats = TTHRML_POTTS_ROW_FLOATS;
 #ifndef TTHRML_POTTS_WIDE
 #define TTHRML_POTTS_WIDE 1
 #endif
+#ifndef TTHRML_POTTS_WPT
+#define TTHRML_POTTS_WPT 2  // chain words per thread when n_chains allows
+#endif
 
 // QC: the category count as a compile-time constant (8, the common case: no
 // per-category predicates) or 0 (any q <= 8, read from the argument).
@@ -96,7 +99,13 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     for (int j = 0; j < 6; ++j) {
       const uint32_t* src = reinterpret_cast<const uint32_t*>(state + (uint64_t)((uint32_t)source_row0 + nb[j]) *
                                                                           (uint32_t)C) + w;
-      if (WPT == 2) {
+      if (WPT == 4) {
+        const uint4 v4 = __ldg(reinterpret_cast<const uint4*>(src));
+        nw[j][0] = v4.x;
+        nw[j][1 % WPT] = v4.y;
+        nw[j][2 % WPT] = v4.z;
+        nw[j][3 % WPT] = v4.w;
+      } else if (WPT == 2) {
         const uint2 v2 = __ldg(reinterpret_cast<const uint2*>(src));
         nw[j][0] = v2.x;
         nw[j][WPT - 1] = v2.y;
@@ -165,7 +174,9 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
     }
     }
     uint32_t* dst = reinterpret_cast<uint32_t*>(state + row * C) + w;
-    if (WPT == 2)
+    if (WPT == 4)
+      *reinterpret_cast<uint4*>(dst) = make_uint4(out[0], out[1 % WPT], out[2 % WPT], out[3 % WPT]);
+    else if (WPT == 2)
       *reinterpret_cast<uint2*>(dst) = make_uint2(out[0], out[WPT - 1]);
     else
       *dst = out[0];
@@ -236,11 +247,12 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
   }
   cudaStream_t s = (cudaStream_t)stream;
 #define TTHRML_POTTS_LAUNCH(V, QC)                                                                              \
-  return (wide ? launch_potts<V, QC, 2> : launch_potts<V, QC, 1>)(state, n_chains, X, Y, Z, colour, target_row0,    \
+  return (wide ? launch_potts<V, QC, TTHRML_POTTS_WPT> : launch_potts<V, QC, 1>)(state, n_chains, X, Y, Z, colour,  \
+                                                                  target_row0,                                    \
                                                                   source_row0, J, bias, q, chain_offset, variates, \
                                                                   variates_sweeps, seed, sweep, ctl, s)
   const bool q8 = q == kPottsQ && (uintptr_t)bias % 16 == 0;  // the q = 8 kernel reads 16-byte bias vectors
-  const bool wide = TTHRML_POTTS_WIDE && n_chains % 8 == 0;   // 8 chains per thread
+  const bool wide = TTHRML_POTTS_WIDE && n_chains % (4 * TTHRML_POTTS_WPT) == 0;  // several chain words per thread
   if (variates) {
     if (q8) TTHRML_POTTS_LAUNCH(true, kPottsQ);
     TTHRML_POTTS_LAUNCH(true, 0);
