@@ -24,6 +24,11 @@
 // of a row per call -- and the low 7 bits from the per-site refill counter,
 // read only when the top bits tie with the threshold's.
 //
+// Uniform lattices (the threshold depends only on the number of -1
+// neighbours) run the bit-sliced kernels below instead: k_ising2d_planes on
+// the same int8 rows and k_ising2d_bits on bit-packed rows (32 sites per
+// uint32), 32 sites per thread in both, with bit-plane draws.
+//
 // Observables (optional, for the energy/magnetisation trace): the sum of the
 // new spins over the counted rows, and in the colour-1 half-sweep the bond
 // sum sum_i s_i (s_left + s_right + s_up + s_down), which counts every bond

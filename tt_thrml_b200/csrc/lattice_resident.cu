@@ -10,7 +10,9 @@
 // 8g..8g+7, i.e. byte g % 4 of word g / 4 of every row, and keeps it as one
 // byte per site in shared memory, [2 colours][H][W/2] bytes.
 //
-// Decision: the four neighbour bytes (left, right, up, down) of a site form
+// Decision (count-symmetric tables, the uniform lattice): bit-sliced over 4
+// sites x 8 chains per 32-bit word with bit-plane draws (PLANES below).
+// Otherwise: the four neighbour bytes (left, right, up, down) of a site form
 // a word N whose bit 8k + v is neighbour k of chain v; a bit-matrix transpose
 // of N (the 8x8 transpose of Warren, "Hacker's Delight" 7-3, with the upper
 // four rows zero) turns it into one 4-bit sign pattern per chain, which decides
