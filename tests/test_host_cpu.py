@@ -471,3 +471,25 @@ def test_categorical_draw_rule_matches_exact_decision():
             assert got == want, (trial, q, qmax, theta, u, got, want)
             checked += 1
     assert checked > 3900
+
+
+def test_lattice_layout_selection():
+    """Uniform lattices take the bit-sliced kernels ("planes" from width % 64 == 0, bit-packed strips from
+    width % 256 == 0); a table that is not count-symmetric keeps the per-site kernels."""
+    from tt_thrml_b200 import workloads
+    from tt_thrml_b200.compiler import ising_count_symmetric, ising_pattern_tables, ising_stencil_layout
+    from tt_thrml_b200.domain import LatticeStrips
+
+    _, thr = ising_pattern_tables(np.float32(0.4407), np.float32(0.0))
+    assert ising_count_symmetric(thr)
+    assert ising_stencil_layout(thr, 64) == "planes" and ising_stencil_layout(thr, 96) == "row8s"
+    skew = thr.copy()
+    skew[1] += 1  # left neighbour at -1 no longer equals right neighbour at -1
+    assert not ising_count_symmetric(skew) and ising_stencil_layout(skew, 64) == "row8s"
+    none = lambda *a: None  # noqa: E731
+    for W, storage in ((64, "int8"), (256, "int8")):  # a host half-sweep keeps int8 rows by default
+        st = LatticeStrips(workloads.IsingLattice2D(8, W, beta=0.4407), device="cpu", halo=2, halfsweep=none)
+        assert st.storage == storage and st.row_bytes == W // 2
+    st = LatticeStrips(workloads.IsingLattice2D(8, 256, beta=0.4407), device="cpu", halo=2, halfsweep=none,
+                       storage="bits")
+    assert st.row_bytes == 256 // 16 and tuple(st.colours[0].shape) == (8 + 4, 256 // 64)
