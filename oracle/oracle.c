@@ -176,6 +176,48 @@ static int or_categorical_icdf(const float* theta, int q, double u, double* marg
   return cat;
 }
 
+/* Philox-mode uniform of a spin draw at (global chain gc, flat row, sweep) in the kernel's counter layout
+ * (see or_block.rng_layout). */
+static double or_spin_uniform(int layout, int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
+  if (layout == 4) return or_uniform(or_plane_bits(gc, row, sweep, k0, k1));
+  if (layout == 5) return or_uniform(or_plane8_bits(gc, row, sweep, k0, k1));
+  if (layout == 2 || layout == 3) return or_uniform(or_split_bits(layout, gc, row, sweep, k0, k1));
+  if (layout == 1) return or_uniform(or_philox((uint32_t)gc, (uint32_t)(row >> 2), sweep, SALT_DENSE_SPIN, k0, k1).v[row & 3]);
+  return or_uniform(or_philox((uint32_t)(gc >> 2), (uint32_t)row, sweep, SALT_SPIN, k0, k1).v[gc & 3]);
+}
+
+/* Philox-mode standard normal of a gaussian draw (Box-Muller on two uniforms of one counter). */
+static double or_gauss_normal(int layout, int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
+  const int dense = layout == 1;
+  const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 1), sweep, SALT_DENSE_GAUSS, k0, k1)
+                           : or_philox((uint32_t)gc, (uint32_t)row, sweep, SALT_GAUSS, k0, k1);
+  const int w = dense ? (int)(row & 1) * 2 : 0;
+  return sqrt(-2.0 * log(or_uniform(r.v[w]))) * cos(2.0 * M_PI * or_uniform(r.v[w + 1]));
+}
+
+/* Philox-mode uniform of a categorical draw: counter (chain/4, row, sweep), word chain % 4. */
+static double or_cat_uniform(int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
+  return or_uniform(or_philox((uint32_t)(gc >> 2), (uint32_t)row, sweep, SALT_CAT, k0, k1).v[gc & 3]);
+}
+
+/* Gumbel-max over theta + g (first maximum), margin = best - second best (compiler.py:327-344). */
+static int or_categorical_argmax(const float* theta, const float* g, int64_t g_stride, int q, double* margin) {
+  int best = 0;
+  double bv = 0.0, second = -INFINITY;
+  for (int k = 0; k < q; ++k) {
+    const double pk = (float)(theta[k] + g[k * g_stride]);
+    if (k == 0 || pk > bv) {
+      if (k) second = bv;
+      bv = pk;
+      best = k;
+    } else if (pk > second) {
+      second = pk;
+    }
+  }
+  *margin = q > 1 ? bv - second : INFINITY;
+  return best;
+}
+
 /* ---- field ---- */
 
 static float st(const float* s, int64_t row, int64_t C, int64_t c) { return s[row * C + c]; }
@@ -291,19 +333,7 @@ static void* run_rows(void* arg) {
           v = two_g > l ? 1.0f : -1.0f;
           m = (double)two_g - (double)l;
         } else {
-          const int dense = B->rng_layout == 1;
-          double u;
-          if (B->rng_layout == 4) {
-            u = or_uniform(or_plane_bits(gc, row, t->sweep, t->k0, t->k1));
-          } else if (B->rng_layout == 5) {
-            u = or_uniform(or_plane8_bits(gc, row, t->sweep, t->k0, t->k1));
-          } else if (B->rng_layout == 2 || B->rng_layout == 3) {
-            u = or_uniform(or_split_bits(B->rng_layout, gc, row, t->sweep, t->k0, t->k1));
-          } else {
-            const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 2), t->sweep, SALT_DENSE_SPIN, t->k0, t->k1)
-                                     : or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_SPIN, t->k0, t->k1);
-            u = or_uniform(r.v[dense ? (row & 3) : (gc & 3)]);
-          }
+          const double u = or_spin_uniform(B->rng_layout, gc, row, t->sweep, t->k0, t->k1);
           const double l = log(u) - log1p(-u);
           m = (double)two_g - l;
           v = m > 0.0 ? 1.0f : -1.0f;
@@ -313,23 +343,9 @@ static void* run_rows(void* arg) {
         theta_of(B, state, C, c, i, theta);
         const int q = B->q;
         if (t->use_variates) {
-          int best = 0;
-          double bv = 0.0, second = -INFINITY;
-          for (int k = 0; k < q; ++k) {
-            const double pk = (float)(theta[k] + B->variates[((int64_t)i * q + k) * C + c]);
-            if (k == 0 || pk > bv) {
-              if (k) second = bv;
-              bv = pk;
-              best = k;
-            } else if (pk > second) {
-              second = pk;
-            }
-          }
-          v = (float)best;
-          m = q > 1 ? bv - second : INFINITY;
+          v = (float)or_categorical_argmax(theta, B->variates + (int64_t)i * q * C + c, C, q, &m);
         } else {
-          const or_u32x4 r = or_philox((uint32_t)(gc >> 2), (uint32_t)row, t->sweep, SALT_CAT, t->k0, t->k1);
-          v = (float)or_categorical_icdf(theta, q, or_uniform(r.v[gc & 3]), &m);
+          v = (float)or_categorical_icdf(theta, q, or_cat_uniform(gc, row, t->sweep, t->k0, t->k1), &m);
         }
       } else {
         int any_l, any_p;
@@ -345,11 +361,7 @@ static void* run_rows(void* arg) {
           const float tt = sd * B->variates[i * C + c];
           v = mean + tt;
         } else {
-          const int dense = B->rng_layout == 1;
-          const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 1), t->sweep, SALT_DENSE_GAUSS, t->k0, t->k1)
-                                   : or_philox((uint32_t)gc, (uint32_t)row, t->sweep, SALT_GAUSS, t->k0, t->k1);
-          const int w = dense ? (int)(row & 1) * 2 : 0;
-          const double xi = sqrt(-2.0 * log(or_uniform(r.v[w]))) * cos(2.0 * M_PI * or_uniform(r.v[w + 1]));
+          const double xi = or_gauss_normal(B->rng_layout, gc, row, t->sweep, t->k0, t->k1);
           v = (float)((double)mean + (double)sd * xi);
         }
       }
@@ -418,3 +430,361 @@ int oracle_group_step(const or_block* blocks, int32_t n_blocks, float* state, in
 }
 
 int oracle_abi_version(void) { return 1; }
+
+/* ======================================================================
+ * Model paths without per-term tables.  Each restates, for one model family
+ * built from its raw parameters, the same group math as the table path above
+ * (the tests check both paths against each other on small models), so the
+ * configurations too large for per-term tables are checked at full size.
+ * ====================================================================== */
+
+/* Runs fn(arg, i0, i1) over [0, n) split across n_threads threads. */
+typedef struct {
+  void (*fn)(const void*, int64_t, int64_t);
+  const void* arg;
+  int64_t i0, i1;
+} or_span;
+
+static void* or_span_main(void* p) {
+  const or_span* s = (const or_span*)p;
+  s->fn(s->arg, s->i0, s->i1);
+  return NULL;
+}
+
+static void or_parallel(void (*fn)(const void*, int64_t, int64_t), const void* arg, int64_t n, int n_threads) {
+  if (n_threads < 1) n_threads = 1;
+  if (n_threads > 256) n_threads = 256;
+  if (n < n_threads) n_threads = (int)(n > 0 ? n : 1);
+  pthread_t th[256];
+  or_span sp[256];
+  for (int k = 0; k < n_threads; ++k) {
+    sp[k].fn = fn;
+    sp[k].arg = arg;
+    sp[k].i0 = n * k / n_threads;
+    sp[k].i1 = n * (k + 1) / n_threads;
+  }
+  int started = 0;
+  for (int k = 1; k < n_threads; ++k) {
+    if (pthread_create(&th[k], NULL, or_span_main, &sp[k]) != 0) break;
+    started = k;
+  }
+  or_span_main(&sp[0]);
+  for (int k = 1; k <= started; ++k) pthread_join(th[k], NULL);
+  for (int k = started + 1; k < n_threads; ++k) or_span_main(&sp[k]);
+}
+
+/* ---- 2-D Ising lattice ----
+ * Periodic height x width lattice (both even), site (y, x) at L = y*width + x
+ * with colour (x + y) % 2.  Block c holds the colour-c sites in increasing L,
+ * so site L sits at block row L / 2 and flat row c*n/2 + L/2.  A site's field
+ * is the bias interaction followed by the pair interaction over its
+ * neighbours in the order (left, right, up, down), each term weight x spin:
+ *   gamma = b + (((w*s_l + w*s_r) + w*s_u) + w*s_d)
+ * in float32 (w = beta*J, b = beta*h), the order the table path sums the
+ * lattice's per-edge tables in. */
+typedef struct {
+  int64_t height, width;
+  float edge_weight, site_bias;
+} or_lattice2d;
+
+typedef struct {
+  const or_lattice2d* L;
+  int32_t colour, rng_layout, use_variates;
+  float* state;
+  const float* variates;
+  double* margin;
+  int64_t C, chain_offset;
+  uint32_t sweep, k0, k1;
+} or_ising_task;
+
+static void or_ising_rows(const void* arg, int64_t r0, int64_t r1) {
+  const or_ising_task* t = (const or_ising_task*)arg;
+  const int64_t H = t->L->height, W = t->L->width, half = H * W / 2, C = t->C;
+  const float w = t->L->edge_weight, b = t->L->site_bias;
+  const int64_t own0 = (int64_t)t->colour * half, oth0 = (int64_t)(1 - t->colour) * half;
+  for (int64_t r = r0; r < r1; ++r) {
+    const int64_t y = (2 * r) / W;
+    const int64_t x = (2 * r) % W + ((y + t->colour) & 1);
+    const int64_t nb[4] = {y * W + (x + W - 1) % W, y * W + (x + 1) % W, ((y + H - 1) % H) * W + x,
+                           ((y + 1) % H) * W + x};
+    const int64_t row = own0 + r;
+    for (int64_t c = 0; c < C; ++c) {
+      float acc = w * t->state[(oth0 + nb[0] / 2) * C + c];
+      for (int k = 1; k < 4; ++k) {
+        const float term = w * t->state[(oth0 + nb[k] / 2) * C + c];
+        acc = acc + term;
+      }
+      const float gamma = b + acc;
+      const float two_g = 2.0f * gamma;
+      double m;
+      if (t->use_variates) {
+        const float lf = t->variates[r * C + c];
+        m = (double)two_g - (double)lf;
+        t->state[row * C + c] = two_g > lf ? 1.0f : -1.0f;
+      } else {
+        const double u = or_spin_uniform(t->rng_layout, t->chain_offset + c, row, t->sweep, t->k0, t->k1);
+        m = (double)two_g - (log(u) - log1p(-u));
+        t->state[row * C + c] = m > 0.0 ? 1.0f : -1.0f;
+      }
+      if (t->margin) t->margin[r * C + c] = m;
+    }
+  }
+}
+
+/* One colour half-sweep of the lattice on the float32 state [n][C] (block rows as above).  The colour's
+ * sites read only the other colour, so they are written in place.  variates: [n/2][C] logits or NULL
+ * (Philox, rng_layout as in or_block).  margin: [n/2][C] or NULL. */
+int oracle_ising2d_step(const or_lattice2d* L, int32_t colour, float* state, int64_t C, int64_t chain_offset,
+                        const float* variates, int32_t rng_layout, uint64_t seed, uint32_t sweep, double* margin,
+                        int32_t n_threads) {
+  if (!L || L->height % 2 || L->width % 2 || L->height <= 0 || L->width <= 0 || (colour & ~1)) return -1;
+  or_ising_task t = {L, colour, rng_layout, variates != NULL, state, variates, margin, C, chain_offset, sweep,
+                     (uint32_t)seed, (uint32_t)(seed >> 32)};
+  or_parallel(or_ising_rows, &t, L->height * L->width / 2, n_threads);
+  return 0;
+}
+
+/* ---- 3-D Potts lattice ----
+ * Periodic X x Y x Z lattice (all even), site (x, y, z) at L = (z*Y + y)*X + x
+ * with colour (x + y + z) % 2, block c = colour-c sites in increasing L, block
+ * row L / 2.  Field of category k: the bias interaction, then per axis a in
+ * (x, y, z) the pair interaction over the two neighbours (minus, plus), each
+ * term selecting J[a][k][s_neighbour]:
+ *   theta_k = ((b_k + (Jx[k][s_x-] + Jx[k][s_x+])) + (Jy[k][s_y-] + Jy[k][s_y+]))
+ *             + (Jz[k][s_z-] + Jz[k][s_z+])
+ * in float32.  A neighbour category outside [0, q) selects weight 0. */
+typedef struct {
+  int64_t dims[3];
+  int32_t q;
+  const float* J;      /* [3][q][q] */
+  const float* bias0;  /* [n/2][q], block 0 in row order */
+  const float* bias1;  /* [n/2][q], block 1 */
+} or_potts3d;
+
+typedef struct {
+  const or_potts3d* P;
+  int32_t colour, use_variates;
+  float* state;
+  const float* variates;
+  double* margin;
+  int64_t C, chain_offset;
+  uint32_t sweep, k0, k1;
+} or_potts_task;
+
+static void or_potts_rows(const void* arg, int64_t r0, int64_t r1) {
+  const or_potts_task* t = (const or_potts_task*)arg;
+  const int64_t X = t->P->dims[0], Y = t->P->dims[1], Z = t->P->dims[2], half = X * Y * Z / 2, C = t->C;
+  const int q = t->P->q;
+  const float* bias = t->colour ? t->P->bias1 : t->P->bias0;
+  const int64_t own0 = (int64_t)t->colour * half, oth0 = (int64_t)(1 - t->colour) * half;
+  for (int64_t r = r0; r < r1; ++r) {
+    const int64_t even = 2 * r;
+    const int64_t y0 = (even / X) % Y, z = even / (X * Y);
+    const int64_t Ls = even + ((y0 + z + t->colour) & 1);
+    const int64_t x = Ls % X, y = (Ls / X) % Y;
+    int64_t nb[6];
+    nb[0] = (z * Y + y) * X + (x + X - 1) % X;
+    nb[1] = (z * Y + y) * X + (x + 1) % X;
+    nb[2] = (z * Y + (y + Y - 1) % Y) * X + x;
+    nb[3] = (z * Y + (y + 1) % Y) * X + x;
+    nb[4] = (((z + Z - 1) % Z) * Y + y) * X + x;
+    nb[5] = (((z + 1) % Z) * Y + y) * X + x;
+    const int64_t row = own0 + r;
+    for (int64_t c = 0; c < C; ++c) {
+      int sn[6];
+      for (int j = 0; j < 6; ++j) {
+        const float v = t->state[(oth0 + nb[j] / 2) * C + c];
+        const int k = (int)v;
+        sn[j] = (v == (float)k && k >= 0 && k < q) ? k : -1;
+      }
+      float theta[OR_MAXQ];
+      for (int k = 0; k < q; ++k) {
+        float acc = bias[r * q + k];
+        for (int a = 0; a < 3; ++a) {
+          const float* Ja = t->P->J + (int64_t)a * q * q + (int64_t)k * q;
+          const float lo = sn[2 * a] < 0 ? 0.0f : Ja[sn[2 * a]];
+          const float hi = sn[2 * a + 1] < 0 ? 0.0f : Ja[sn[2 * a + 1]];
+          const float pair = lo + hi;
+          acc = acc + pair;
+        }
+        theta[k] = acc;
+      }
+      double m;
+      int cat;
+      if (t->use_variates) {
+        cat = or_categorical_argmax(theta, t->variates + r * q * C + c, C, q, &m);
+      } else {
+        cat = or_categorical_icdf(theta, q, or_cat_uniform(t->chain_offset + c, row, t->sweep, t->k0, t->k1), &m);
+      }
+      t->state[row * C + c] = (float)cat;
+      if (t->margin) t->margin[r * C + c] = m;
+    }
+  }
+}
+
+/* One colour half-sweep of the Potts lattice on the float32 state [n][C] (categories as floats), in place.
+ * variates: [n/2][q][C] Gumbel noise or NULL (Philox, chain4 counters, inverse-CDF draw). */
+int oracle_potts3d_step(const or_potts3d* P, int32_t colour, float* state, int64_t C, int64_t chain_offset,
+                        const float* variates, uint64_t seed, uint32_t sweep, double* margin, int32_t n_threads) {
+  if (!P || P->q < 1 || P->q > OR_MAXQ || (colour & ~1)) return -1;
+  for (int a = 0; a < 3; ++a)
+    if (P->dims[a] <= 0 || P->dims[a] % 2) return -1;
+  or_potts_task t = {P, colour, variates != NULL, state, variates, margin, C, chain_offset, sweep, (uint32_t)seed,
+                     (uint32_t)(seed >> 32)};
+  or_parallel(or_potts_rows, &t, P->dims[0] * P->dims[1] * P->dims[2] / 2, n_threads);
+  return 0;
+}
+
+/* ---- dense bipartite (restricted Boltzmann machine) ----
+ * Visible block rows [0, V), hidden block rows [V, V + H).  Field of hidden
+ * unit j: b_h[j] + sum_i W[i][j] v_i; of visible unit i: b_v[i] + sum_j
+ * W[i][j] h_j.  The fields are summed in double precision: the exact value
+ * every float32 summation order approximates, so a kernel's decision can be
+ * judged against it with the threshold band (its float32 rounding, about
+ * 1e-6 at these sizes, is well inside 1e-5).  Spin units: +1 where 2*gamma >
+ * logit(u); gaussian units (precision 1, the reference's default): mean =
+ * gamma / (1 + 1e-6), sd = sqrt(1 / (1 + 1e-6)), value = mean + sd * xi,
+ * rounded to bfloat16 (nearest even) when store_bf16 is set (the kernels'
+ * bf16 operand storage). */
+typedef struct {
+  int64_t n_visible, n_hidden;
+  const float* W;   /* [V][H] */
+  const float* b_v; /* [V] */
+  const float* b_h; /* [H] */
+  int32_t visible_family, store_bf16;
+} or_dense;
+
+typedef struct {
+  const or_dense* D;
+  int32_t block, family, rng_layout, use_variates;
+  float* state;
+  const float* variates;
+  double* margin;
+  float* out;
+  int64_t C, chain_offset;
+  uint32_t sweep, k0, k1;
+} or_dense_task;
+
+static float or_bf16_round(float x) {
+  uint32_t b;
+  memcpy(&b, &x, 4);
+  if ((b & 0x7F800000u) == 0x7F800000u) return x; /* inf / nan */
+  b = (b + 0x7FFFu + ((b >> 16) & 1u)) & 0xFFFF0000u;
+  float y;
+  memcpy(&y, &b, 4);
+  return y;
+}
+
+#define OR_DENSE_TILE 32
+
+static void or_dense_units(const void* arg, int64_t t0, int64_t t1) {
+  const or_dense_task* t = (const or_dense_task*)arg;
+  const int64_t V = t->D->n_visible, Hh = t->D->n_hidden, C = t->C;
+  const int hidden = t->block == 1;
+  const int64_t n_units = hidden ? Hh : V, n_src = hidden ? V : Hh;
+  const int64_t src0 = hidden ? 0 : V, row0 = hidden ? V : 0;
+  const float* bias = hidden ? t->D->b_h : t->D->b_v;
+  double* acc = (double*)malloc(sizeof(double) * OR_DENSE_TILE * (size_t)C);
+  if (!acc) return;
+  for (int64_t tile = t0; tile < t1; ++tile) {
+    const int64_t u0 = tile * OR_DENSE_TILE;
+    const int64_t nu = n_units - u0 < OR_DENSE_TILE ? n_units - u0 : OR_DENSE_TILE;
+    for (int64_t a = 0; a < nu; ++a)
+      for (int64_t c = 0; c < C; ++c) acc[a * C + c] = bias[u0 + a];
+    for (int64_t s = 0; s < n_src; ++s) {
+      const float* src = t->state + (src0 + s) * C;
+      for (int64_t a = 0; a < nu; ++a) {
+        const double w = hidden ? t->D->W[s * Hh + u0 + a] : t->D->W[(u0 + a) * Hh + s];
+        double* ac = acc + a * C;
+        for (int64_t c = 0; c < C; ++c) ac[c] += w * (double)src[c];
+      }
+    }
+    for (int64_t a = 0; a < nu; ++a) {
+      const int64_t unit = u0 + a, row = row0 + unit;
+      for (int64_t c = 0; c < C; ++c) {
+        const double gamma = acc[a * C + c];
+        const int64_t gc = t->chain_offset + c;
+        double m = 0.0;
+        float v;
+        if (t->family == OR_SPIN) {
+          double l;
+          if (t->use_variates) {
+            l = t->variates[unit * C + c];
+          } else {
+            const double u = or_spin_uniform(t->rng_layout, gc, row, t->sweep, t->k0, t->k1);
+            l = log(u) - log1p(-u);
+          }
+          m = 2.0 * gamma - l;
+          v = m > 0.0 ? 1.0f : -1.0f;
+        } else {
+          const float pe = 1.0f + 1e-6f;
+          const float inv = 1.0f / pe;
+          const double xi = t->use_variates ? (double)t->variates[unit * C + c]
+                                            : or_gauss_normal(t->rng_layout, gc, row, t->sweep, t->k0, t->k1);
+          v = (float)(gamma * (double)inv + (double)sqrtf(inv) * xi);
+          if (t->D->store_bf16) v = or_bf16_round(v);
+        }
+        t->out[unit * C + c] = v;
+        if (t->margin) t->margin[unit * C + c] = m;
+      }
+    }
+  }
+  free(acc);
+}
+
+/* Samples one block (0 visible, 1 hidden) of the dense bipartite model on the float32 state [V+H][C] and
+ * writes it in place (the block reads only the other block).  variates: [n_units][C] (spin logits or
+ * standard normals) or NULL (Philox, rng_layout as in or_block).  margin: [n_units][C] or NULL. */
+int oracle_dense_step(const or_dense* D, int32_t block, float* state, int64_t C, int64_t chain_offset,
+                      const float* variates, int32_t rng_layout, uint64_t seed, uint32_t sweep, double* margin,
+                      int32_t n_threads) {
+  if (!D || (block & ~1)) return -1;
+  const int64_t n_units = block ? D->n_hidden : D->n_visible;
+  float* out = (float*)malloc(sizeof(float) * (size_t)(n_units > 0 ? n_units : 1) * (size_t)C);
+  if (!out) return -1;
+  or_dense_task t = {D, block, block ? OR_SPIN : D->visible_family, rng_layout, variates != NULL, state, variates,
+                     margin, out, C, chain_offset, sweep, (uint32_t)seed, (uint32_t)(seed >> 32)};
+  or_parallel(or_dense_units, &t, (n_units + OR_DENSE_TILE - 1) / OR_DENSE_TILE, n_threads);
+  memcpy(state + (block ? D->n_visible : 0) * C, out, sizeof(float) * (size_t)(n_units * C));
+  free(out);
+  return 0;
+}
+
+/* ---- greedy colouring ----
+ * Nodes in index order; each takes the smallest colour that none of its
+ * already-coloured neighbours has (the colouring that defines the sparse
+ * random-graph configuration's blocks).  colour: [n]; *n_colours = k. */
+int oracle_greedy_colouring(int64_t n, const int64_t* row_ptr, const int32_t* cols, int32_t* colour,
+                            int32_t* n_colours) {
+  int64_t cap = 64;
+  int64_t* seen = (int64_t*)malloc(sizeof(int64_t) * (size_t)cap); /* seen[k] == v: colour k is next to v */
+  if (!seen) return -1;
+  for (int64_t k = 0; k < cap; ++k) seen[k] = -1;
+  int32_t k_max = 0;
+  for (int64_t v = 0; v < n; ++v) {
+    int64_t deg = row_ptr[v + 1] - row_ptr[v];
+    if (deg + 1 > cap) {
+      int64_t nc = cap;
+      while (nc < deg + 1) nc *= 2;
+      int64_t* ns = (int64_t*)realloc(seen, sizeof(int64_t) * (size_t)nc);
+      if (!ns) {
+        free(seen);
+        return -1;
+      }
+      for (int64_t k = cap; k < nc; ++k) ns[k] = -1;
+      seen = ns;
+      cap = nc;
+    }
+    for (int64_t e = row_ptr[v]; e < row_ptr[v + 1]; ++e) {
+      const int64_t u = cols[e];
+      if (u < v && colour[u] < cap) seen[colour[u]] = v; /* lower-indexed neighbours are coloured */
+    }
+    int32_t k = 0;
+    while (seen[k] == v) ++k;
+    colour[v] = k;
+    if (k + 1 > k_max) k_max = k + 1;
+  }
+  free(seen);
+  *n_colours = k_max;
+  return 0;
+}

@@ -93,6 +93,16 @@ def lib():
         ]
         _lib.oracle_philox4x32_10.restype = None
         _lib.oracle_philox4x32_10.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        # (model, colour/block, state, C, chain_offset, variates, [rng_layout], seed, sweep, margin, threads)
+        i64, i32, vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p
+        _lib.oracle_ising2d_step.restype = i32
+        _lib.oracle_ising2d_step.argtypes = [vp, i32, vp, i64, i64, vp, i32, ctypes.c_uint64, ctypes.c_uint32, vp, i32]
+        _lib.oracle_potts3d_step.restype = i32
+        _lib.oracle_potts3d_step.argtypes = [vp, i32, vp, i64, i64, vp, ctypes.c_uint64, ctypes.c_uint32, vp, i32]
+        _lib.oracle_dense_step.restype = i32
+        _lib.oracle_dense_step.argtypes = [vp, i32, vp, i64, i64, vp, i32, ctypes.c_uint64, ctypes.c_uint32, vp, i32]
+        _lib.oracle_greedy_colouring.restype = i32
+        _lib.oracle_greedy_colouring.argtypes = [i64, vp, vp, vp, vp]
     return _lib
 
 
@@ -137,6 +147,23 @@ class OProgram:
     sampling_order: list
     n_free: int
     total: int
+    model: object = None  # a model path of oracle/models.py (stencil / dense), or None for the table path
+
+
+class Lattice2D(ctypes.Structure):
+    _fields_ = [("height", ctypes.c_int64), ("width", ctypes.c_int64), ("edge_weight", ctypes.c_float),
+                ("site_bias", ctypes.c_float)]
+
+
+class Potts3D(ctypes.Structure):
+    _fields_ = [("dims", ctypes.c_int64 * 3), ("q", ctypes.c_int32), ("J", ctypes.c_void_p), ("bias0", ctypes.c_void_p),
+                ("bias1", ctypes.c_void_p)]
+
+
+class Dense(ctypes.Structure):
+    _fields_ = [("n_visible", ctypes.c_int64), ("n_hidden", ctypes.c_int64), ("W", ctypes.c_void_p),
+                ("b_v", ctypes.c_void_p), ("b_h", ctypes.c_void_p), ("visible_family", ctypes.c_int32),
+                ("store_bf16", ctypes.c_int32)]
 
 
 def _family_of(block, gibbs_spec) -> str:
@@ -268,13 +295,21 @@ def _from_spec(spec) -> OBlock:
     return OBlock(spec.block_index, fam, spec.n_nodes, q, spec.block_global_start, inters)
 
 
-def lower_program(program) -> OProgram:
+def lower_program(program, *, tables: bool = False) -> OProgram:
+    """The oracle's program.  Synthetic models (lattices, random graphs, RBMs) are built from their raw
+    parameters by oracle/models.py (stencil / dense paths unless `tables`); a program given directly as
+    block tables (a plain table program) is read as given; a thrml program is lowered as the reference
+    lowers it."""
+    from . import models
+
+    own = models.from_raw_parameters(program, tables=tables)
+    if own is not None:
+        return own
     gs = program.gibbs_spec
     order = [list(map(int, g)) for g in gs.sampling_order]
     n_free = len(gs.free_blocks)
-    native = getattr(program, "tt_lower_blocks", None)
-    if callable(native):
-        specs = list(native())
+    specs = getattr(program, "specs", None)
+    if isinstance(specs, (list, tuple)) and callable(getattr(program, "tt_lower_blocks", None)):
         blocks = [_from_spec(s) for s in specs]
         return OProgram(blocks, order, n_free, specs[0].total_nodes if specs else 0)
     starts, maps, total = layout_of(gs)
@@ -302,6 +337,13 @@ def lower_program(program) -> OProgram:
     return OProgram(blocks, order, n_free, total)
 
 
+def bf16_round(x) -> np.ndarray:
+    """float32 values rounded to the nearest bfloat16 (ties to even), as float32."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
 # ----------------------------------------------------------------------------
 # Sampler.
 # ----------------------------------------------------------------------------
@@ -311,7 +353,7 @@ class OracleSampler:
     """Runs lowered programs on the CPU over a float32 [rows, chains] state."""
 
     def __init__(self, program, n_chains: int = 1, chain_offset: int = 0, n_threads: int | None = None,
-                 rng_layout="chain4"):
+                 rng_layout="chain4", gaussian_storage: str = "f32", tables: bool = False):
         """rng_layout: Philox counter layout of Philox-mode draws, one name for
         every block or a dict block index -> name.  "chain4": counter (chain/4,
         row, sweep), word chain % 4 (the sparse, generic and Potts kernels);
@@ -324,7 +366,11 @@ class OracleSampler:
         of the draw of row r: bit 8 (r % 4) + (r % 32) / 4 of word b % 4 of
         counter (chain, r / 32, sweep, "LPL0" + b / 4)); "planes8": those of the
         bit-sliced resident kernel (bit 8 (r % 4) + chain % 8 of word b % 4 of
-        counter (chain / 8, r / 4, sweep, "LPL0" + b / 4))."""
+        counter (chain / 8, r / 4, sweep, "LPL0" + b / 4)).
+        gaussian_storage: "f32", or "bf16" for a dense model whose gaussian
+        block is stored as bfloat16 (the tensor-core kernel's operand).
+        tables: build synthetic models as per-term tables instead of the
+        stencil / dense paths."""
         names = {"chain4": 0, "row4": 1, "row8s": 2, "chain8s": 3, "planes": 4, "planes8": 5}
         layouts = rng_layout if isinstance(rng_layout, dict) else None
         for v in (layouts.values() if layouts is not None else [rng_layout]):
@@ -332,7 +378,10 @@ class OracleSampler:
                 raise ValueError(f"rng_layout must be one of {sorted(names)}, got {v!r}")
         self._rng_layout = {int(k): names[v] for k, v in layouts.items()} if layouts is not None else {}
         self._rng_default = 0 if layouts is not None else names[rng_layout]
-        self.prog = program if isinstance(program, OProgram) else lower_program(program)
+        if gaussian_storage not in ("f32", "bf16"):
+            raise ValueError(f"gaussian_storage must be 'f32' or 'bf16', got {gaussian_storage!r}")
+        self.gaussian_storage = gaussian_storage
+        self.prog = program if isinstance(program, OProgram) else lower_program(program, tables=tables)
         self.program = program
         self.C = int(n_chains)
         self.chain_offset = int(chain_offset)
@@ -355,6 +404,10 @@ class OracleSampler:
                     d.cat_q[j] = q
             self._inter_structs[b.index] = arr
 
+    def layout_of(self, block_index: int) -> int:
+        """Philox counter layout code of a block's draws."""
+        return self._rng_layout.get(int(block_index), self._rng_default)
+
     # state -----------------------------------------------------------------
     def load_state(self, state_free, state_clamp=()):
         states = list(state_free) + list(state_clamp)
@@ -363,6 +416,8 @@ class OracleSampler:
             if b.family == "spin":
                 a = np.where(a.astype(np.float32) > 0, 1.0, -1.0)
             a = a.astype(np.float32).reshape(-1, b.n_nodes)
+            if b.family == "gaussian" and self.gaussian_storage == "bf16":
+                a = bf16_round(a)
             if a.shape[0] == 1:
                 a = np.broadcast_to(a, (self.C, b.n_nodes))
             self.state[b.start : b.start + b.n_nodes] = a.T
@@ -382,6 +437,11 @@ class OracleSampler:
                    return_margin: bool = False):
         """One sampling group; variates: block index -> [n, qv, C] float32 for this sweep."""
         group = self.prog.sampling_order[group_index]
+        if self.prog.model is not None:
+            rows = sum(self.prog.blocks[bi].n_nodes for bi in group)
+            margin = np.zeros((rows, self.C), dtype=np.float64) if return_margin else None
+            self.prog.model.group_step(self, group_index, sweep, seed, variates, margin)
+            return margin
         arr = (_Block * len(group))()
         keep = []
         rows = 0

@@ -37,6 +37,14 @@ def rng_layouts(compiled) -> dict:
     return out
 
 
+def gaussian_storage(compiled) -> str:
+    """"bf16" when the tensor-core plans hold gaussian blocks as single bf16 operands, else "f32"."""
+    plans = [g.kernel_artifact for g in compiled.sampling_groups]
+    if plans and all(p.kind == "dense" and p.source_pieces == 1 and p.out_pieces == 1 for p in plans):
+        return "bf16"
+    return "f32"
+
+
 def random_init(program, C, seed=0, clamp=None):
     rng = np.random.default_rng(seed)
     out = []
@@ -126,7 +134,8 @@ def run_parity(program, C: int, n_sweeps: int, *, mode: str, seed: int = 11, ini
                            dense_precision=dense_precision, stencil=stencil)
     compiled = compile_program(None, 0, program, cfg, n_sweeps=n_sweeps, n_chains=C, force_generic=force_generic)
     ex = Executor(None, 0, program, cfg, compiled, n_sweeps=n_sweeps, n_chains=C)
-    o = orc.OracleSampler(program, n_chains=C, rng_layout=rng_layouts(compiled))
+    o = orc.OracleSampler(program, n_chains=C, rng_layout=rng_layouts(compiled),
+                          gaussian_storage=gaussian_storage(compiled))
     init = init if init is not None else random_init(program, C, seed)
     ex.load_state(init, clamp)
     o.load_state(init, clamp)

@@ -124,7 +124,10 @@ def spin_graph_program(row_ptr, cols, J, h, colours, *, beta: float = 1.0, name:
         blocks.append(IndexBlock(int(counts[b]), Family.SPIN, name=f"colour{b}:"))
         specs.append(spec)
     gspec = TableGibbsSpec(free_blocks=blocks, clamped_blocks=[], sampling_order=[[b] for b in range(k)])
-    meta = {"name": name, "n_nodes": n, "n_edges": int(row_ptr[-1]) // 2, "n_blocks": k, "flat_of": flat_of}
+    meta = {"name": name, "n_nodes": n, "n_edges": int(row_ptr[-1]) // 2, "n_blocks": k, "flat_of": flat_of,
+            # the model's raw parameters (before beta and the block renumbering), for independent checkers
+            "graph": {"row_ptr": row_ptr, "cols": cols, "J": np.asarray(J, dtype=np.float32),
+                      "h": np.asarray(h, dtype=np.float32), "beta": float(beta), "colours": colours}}
     return TableProgram(gspec, specs, meta)
 
 
@@ -308,6 +311,7 @@ def erdos_renyi_ising(
     colours = greedy_colouring(row_ptr, cols)
     prog = spin_graph_program(row_ptr, cols, vals, h, colours, beta=beta, name=f"er-ising-{n}")
     prog.meta.update(mean_degree=mean_degree, seed=seed, beta=beta, j_variance=j_variance, h_variance=h_variance)
+    prog.meta["graph"]["colouring"] = "greedy"
     return prog
 
 
