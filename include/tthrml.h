@@ -147,18 +147,24 @@ int tthrml_group_step(const tthrml_group* group_host, void* stream);
  * lend, or a running control loop that must not call cudaMalloc (it can
  * synchronise the whole device), use this entry point instead: `scratch` in
  * the descriptor is ignored and the staging area is a device array inside
- * this library of TTHRML_STATIC_SCRATCH_BYTES, which every GPU that loads the
- * library holds until the process exits.  Groups needing more
- * (group_rows * n_chains * element size) are rejected with TTHRML_ERR_ARG.
- * No memory is allocated and no allocating routine is called.
+ * this library of TTHRML_STATIC_SCRATCH_BYTES.  A device reserves the array
+ * when the library's generic group kernels are first used on it (lazy module
+ * loading, the CUDA 12 default) and keeps it until the process exits.  Groups
+ * that stage more than that (group_rows * n_chains * element size) are
+ * rejected with TTHRML_ERR_ARG before anything is launched; groups with
+ * `in_place` set stage nothing and are never rejected for their size.  No
+ * memory is allocated and no allocating routine is called.
  *
- * The first call on a device looks up the array's device address there
- * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture.  Every call shares the one array and the array
- * keeps the last call's contents; nothing has to start at zero because the
- * step writes every scratch element before it reads it back.  Calls whose
- * kernels overlap on the GPU race on the array: serialise them (one stream,
- * or events) per device.
+ * The array's device address belongs to the CUDA context that loaded the
+ * library's module.  Every call made outside stream capture looks it up in
+ * the current context (cudaGetSymbolAddress); a call made while its stream is
+ * being captured uses the address its context's last uncaptured call found,
+ * so the first call in each context (including the new context after a
+ * cudaDeviceReset) must come before any stream capture.  Every call shares
+ * the one array and the array keeps the last call's contents; nothing has to
+ * start at zero because the step writes every scratch element before it reads
+ * it back.  Calls whose kernels overlap on the GPU race on the array:
+ * serialise them (one stream, or events) per device.
  */
 #define TTHRML_STATIC_SCRATCH_BYTES (16u << 20)
 int tthrml_group_step_static_scratch(const tthrml_group* group_host, void* stream);

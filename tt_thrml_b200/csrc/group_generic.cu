@@ -273,11 +273,13 @@ extern "C" int tthrml_group_step(const tthrml_group* g, void* stream) {
 // a plugin or FFI host that gives the library only the buffers it owns and has
 // no device allocator to lend, or a control loop that must not call cudaMalloc
 // (which can synchronise the whole device) once it is running.  For them the
-// staging area is this library's own file-scope device array, reserved on
-// every GPU when the library's device code is loaded and kept until exit.
-// Each call resolves the array's device address for the current device (once
-// per device, on the first call there) and runs the same kernels as
-// tthrml_group_step with it.
+// staging area is this library's own file-scope device array.  With lazy module
+// loading (the CUDA 12 default) a device reserves it when this file's kernels
+// are first used there, and keeps it until the process exits.  The array's
+// device address belongs to the CUDA context that loaded the module: it is
+// looked up again on every call made outside stream capture (so a new context,
+// e.g. after cudaDeviceReset, gets its own address) and cached per context for
+// calls made while the stream is being captured.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -286,30 +288,74 @@ namespace {
 
 __device__ __align__(256) unsigned char g_static_scratch[TTHRML_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxScratchDevices = 256;
+constexpr int kMaxScratchContexts = 64;
 std::mutex g_static_scratch_mutex;
-void* g_static_scratch_addr[kMaxScratchDevices];  // device address per device ordinal, resolved once
+struct ScratchAddr {
+  void* ctx;
+  void* addr;
+};
+ScratchAddr g_static_scratch_addr[kMaxScratchContexts];  // device address per CUDA context
+int g_static_scratch_n = 0;
 
-// Device address of g_static_scratch on the current device.  Host code only
-// sees a host-side stand-in under the array's name, so the address must come
-// from cudaGetSymbolAddress with that device current.
-int static_scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_status(e, "tthrml_group_step_static_scratch: cudaGetDevice");
-  if (dev < 0 || dev >= kMaxScratchDevices) {
-    set_error("tthrml_group_step_static_scratch: device ordinal %d is beyond the %d supported", dev,
-              kMaxScratchDevices);
-    return TTHRML_ERR_UNSUPPORTED;
+typedef int (*cu_ctx_get_current_fn)(void**);
+
+// Current CUDA context handle (driver API through the runtime's entry-point
+// query, so the library needs no link against libcuda).
+int current_context(void** ctx) {
+  static cu_ctx_get_current_fn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) {
+      set_error("tthrml_group_step_static_scratch: cuCtxGetCurrent is unavailable (%s)", cudaGetErrorString(e));
+      return TTHRML_ERR_CUDA;
+    }
+    fn = (cu_ctx_get_current_fn)p;
   }
+  *ctx = nullptr;
+  const int r = fn(ctx);
+  if (r != 0 || !*ctx) {
+    set_error("tthrml_group_step_static_scratch: no current CUDA context (driver status %d)", r);
+    return TTHRML_ERR_CUDA;
+  }
+  return TTHRML_OK;
+}
+
+// Device address of g_static_scratch in the current context.  Host code only
+// sees a host-side stand-in under the array's name, so the address must come
+// from cudaGetSymbolAddress with that context current.
+int static_scratch_address(cudaStream_t stream, void** out) {
+  // a runtime call first: it makes the device's primary context current when no context is
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) return cuda_status(e, "tthrml_group_step_static_scratch: cudaStreamIsCapturing");
+  void* ctx = nullptr;
+  const int rc = current_context(&ctx);
+  if (rc) return rc;
   std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
-  if (!g_static_scratch_addr[dev]) {
+  int slot = -1;
+  for (int i = 0; i < g_static_scratch_n; ++i)
+    if (g_static_scratch_addr[i].ctx == ctx) slot = i;
+  if (cap == cudaStreamCaptureStatusNone || slot < 0) {
+    if (cap != cudaStreamCaptureStatusNone) {
+      set_error("tthrml_group_step_static_scratch: the first call in a CUDA context must come before stream capture");
+      return TTHRML_ERR_ARG;
+    }
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return cuda_status(e, "tthrml_group_step_static_scratch: cudaGetSymbolAddress");
-    g_static_scratch_addr[dev] = p;
+    if (slot < 0) {
+      if (g_static_scratch_n == kMaxScratchContexts) {  // table full: forget the oldest context
+        for (int i = 1; i < kMaxScratchContexts; ++i) g_static_scratch_addr[i - 1] = g_static_scratch_addr[i];
+        --g_static_scratch_n;
+      }
+      slot = g_static_scratch_n++;
+      g_static_scratch_addr[slot].ctx = ctx;
+    }
+    g_static_scratch_addr[slot].addr = p;
   }
-  *out = g_static_scratch_addr[dev];
+  *out = g_static_scratch_addr[slot].addr;
   return TTHRML_OK;
 }
 
@@ -333,19 +379,22 @@ extern "C" int tthrml_group_step_static_scratch(const tthrml_group* g, void* str
     set_error("tthrml_group_step_static_scratch: unknown state dtype %d", g->state_dtype);
     return TTHRML_ERR_ARG;
   }
-  const int64_t need = g->group_rows * g->n_chains * elem;
-  if (g->group_rows > 0 && (need / g->group_rows / g->n_chains != elem || need > (int64_t)TTHRML_STATIC_SCRATCH_BYTES)) {
-    set_error("tthrml_group_step_static_scratch: the group needs %lld bytes of scratch (%lld rows x %lld chains x "
-              "%lld B) but the static scratch holds %lld bytes; use tthrml_group_step with a caller buffer",
-              (long long)need, (long long)g->group_rows, (long long)g->n_chains, (long long)elem,
-              (long long)TTHRML_STATIC_SCRATCH_BYTES);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (g->in_place) return elem == 4 ? launch_group<float>(*g, s) : launch_group<int8_t>(*g, s);  // no staging
+  // rows that fit, tested before any product is formed (no signed overflow)
+  const int64_t max_rows = (int64_t)TTHRML_STATIC_SCRATCH_BYTES / elem / g->n_chains;
+  if (g->group_rows > max_rows) {
+    set_error("tthrml_group_step_static_scratch: the group needs %lld rows x %lld chains x %lld B of scratch but "
+              "the static scratch holds %lld bytes (%lld rows at this chain count); use tthrml_group_step with a "
+              "caller buffer",
+              (long long)g->group_rows, (long long)g->n_chains, (long long)elem,
+              (long long)TTHRML_STATIC_SCRATCH_BYTES, (long long)max_rows);
     return TTHRML_ERR_ARG;
   }
   void* scratch = nullptr;
-  const int rc = static_scratch_address(&scratch);
+  const int rc = static_scratch_address(s, &scratch);
   if (rc) return rc;
   tthrml_group local = *g;
   local.scratch = scratch;
-  cudaStream_t s = (cudaStream_t)stream;
   return elem == 4 ? launch_group<float>(local, s) : launch_group<int8_t>(local, s);
 }
