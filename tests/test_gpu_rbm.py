@@ -5,7 +5,7 @@ repeated along K) meets the float32 criteria: spins bit-exact outside the
 1e-5 threshold band, gaussians within 1e-4 relative.  dense_precision "bf16"
 (gaussian blocks stored as bf16, the throughput configuration) meets them for
 spins against an oracle that stores its gaussian block as bf16 as well, and
-stays within bf16 rounding (2^-8 relative) for gaussians.
+stays within bf16 rounding (one bf16 unit in the last place: 2^-7 relative at most) for gaussians.
 """
 
 from __future__ import annotations
@@ -18,6 +18,10 @@ from tt_thrml_b200 import Executor, make_cuda_config, workloads
 from tt_thrml_b200.compiler import compile_program
 
 pytestmark = pytest.mark.gpu
+
+# a value the GPU and the oracle round to neighbouring bf16 numbers differs by one unit in the last place:
+# 2^-7 relative just above a power of two
+BF16_ULP = 2.0**-7
 
 V, H, C = 256, 512, 128
 
@@ -50,7 +54,7 @@ def test_rbm_fp32_dense_matches_oracle(cuda_device, mode):
 @pytest.mark.parametrize("mode", ["variates", "philox"])
 def test_rbm_bf16_dense_matches_oracle_within_bf16(cuda_device, mode):
     prog = _rbm(seed=2)
-    rtol = 2.0**-8
+    rtol = BF16_ULP
     rep, ex, o = gh.run_parity(prog, C, 4, mode=mode, init=_init(3), dense_precision="bf16", gauss_rtol=rtol)
     assert all(g.kernel_artifact.source_pieces == 1 for g in ex.compiled.sampling_groups)
     assert o.gaussian_storage == "bf16"  # the oracle stores its gaussian block as bf16 too

@@ -272,8 +272,12 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
           }
           mbar_expect_tx(&full[s], STAGE_BYTES);
           unsigned char* a = tiles + s * STAGE_BYTES;
-          tma_load_2d(a, &map_a, &full[s], kb * BK, mb * BM);
-          tma_load_2d(a + A_BYTES, &map_b, &full[s], kb * BK, nb * BN);
+          // K blocks from the last to the first: with several bf16 pieces per source value ([hi | mid | lo]
+          // along K) the small remainders are summed while the accumulator is still small, so the float32
+          // rounding of the accumulation is that of the hi pieces alone
+          const int kc = (num_k - 1 - kb) * BK;
+          tma_load_2d(a, &map_a, &full[s], kc, mb * BM);
+          tma_load_2d(a + A_BYTES, &map_b, &full[s], kc, nb * BN);
           ++issued;
         }
       }
