@@ -1,36 +1,47 @@
 """Benchmark of the block-Gibbs sweep path (node-updates/s).
 
-Default workload (`--workload er`, the headline: the sparse random-graph
-Ising configuration): Erdos-Renyi graph with N = 2^20 nodes and mean degree 8,
-J_ij ~ N(0, 1/8) symmetric, h_i ~ N(0, 0.1) (variances), beta = 1, greedy
-colouring into k blocks (one sampling group each), 256 chains per GPU, seeded
-synthetic data.  One bench step = one run of 200 sweeps over all k groups for
-all chains of every GPU.  Other workloads: `--workload rbm` (Gauss-Bernoulli
-RBM, 4096 gaussian visible x 8192 spin hidden, 8192 chains, 100 sweeps per
-step; tensor-core roofline) and `--workload lattice` (64x64 Ising, 1024
-chains, the schedule n_warmup=32 n_samples=64 steps_per_sample=2 per step).
+One default run (`python bench.py`) prints one JSON line: the headline
+configuration at top level and the other four configurations under
+`workloads`, each with its own value, e2e, roofline, clocks and CPU baseline.
+
+* er (headline): sparse random-graph Ising, Erdos-Renyi N = 2^20 nodes, mean
+  degree 8, J_ij ~ N(0, 1/8) symmetric, h_i ~ N(0, 0.1) (variances), beta = 1,
+  greedy colouring into k blocks (one sampling group each), 256 chains per
+  GPU, one step = 200 sweeps over all k groups;
+* lattice: 64x64 periodic Ising, J = 1, h = 0, beta = 0.44, 1024 chains per
+  GPU, one step = the schedule n_warmup = 32, n_samples = 64,
+  steps_per_sample = 2 with the per-chain magnetisation observed on device;
+* rbm: Gauss-Bernoulli RBM, 4096 gaussian visible x 8192 spin hidden,
+  W ~ N(0, 0.01^2), 8192 chains per GPU, one step = 100 sweeps;
+* potts: 3-D q = 8 Potts 128^3 periodic, per-axis symmetric couplings, bias
+  variance 0.5, 64 chains per GPU, one step = 100 sweeps;
+* ising: single-chain 2-D Ising 32768^2, beta = 0.4407, one step = 1000
+  sweeps, row strips over the GPUs with the halo exchange fused into the
+  half-sweep kernel (strong scaling).
+
+`--workload NAME` runs one configuration alone.  Chain-sharded workloads
+keep their chains per GPU fixed (weak scaling) and run through
+`make_mesh_executor` (one process per GPU, no collective inside a sweep).
 
 * `value`: steps on device-resident state (CUDA-graph replay of the step's
   sweeps), one CUDA event pair per step on the executor's stream, barrier +
   synchronize on both sides, max over ranks.  L2 is flushed (256 MiB write)
   before every step, outside the timed windows.
-* `e2e`: the same metric through the public API: each step is one
-  `Executor.sample_states` call (pinned host initial state -> the sweeps ->
-  final state back on the host; for the lattice, `sample_with_observation`
-  with the magnetisation observed on device), wall clock with synchronize on
-  both sides.
-* `roofline`: the step's dominant kernel over per-launch CUDA events of eager
-  sweeps: algorithmic bytes (sparse spin kernel: neighbour state rows read,
-  own row written, CSR tables read once) against the measured HBM copy
-  bandwidth, or algorithmic FLOPs (dense kernel: 2 x chains x visible x
-  hidden per GEMM, two per sweep) against the measured bf16 GEMM peak.
-* `cpu_baseline`: the CPU oracle (C restatement of the reference's group
-  math) on this host's cores over a bounded sample of the same workload.
+* `e2e`: the same metric through the public API with pinned host buffers:
+  `sample_states` (initial state in, final state out), the lattice's
+  `sample_with_observation` with the magnetisation observed on device, the
+  strips' `load_split_colours` + `run_sweeps` + `energy_magnetisation`.
+* `roofline`: the dominant kernel over per-launch CUDA events on its launch
+  stream: algorithmic bytes against the measured HBM copy bandwidth, or
+  algorithmic FLOPs against the measured bf16 GEMM peak; `traffic` from the
+  committed ncu summaries.
+* `cpu_baseline`: the CPU oracle (a C restatement of the reference's group
+  math, built from the configuration's raw parameters) on this host's cores
+  over a bounded sample of the same configuration.
 
-`--impl reference` times only the CPU oracle (the reference itself needs JAX,
-thrml and Tenstorrent hardware, none of which exist here) on all host cores.
-Multi-GPU: launched by torchrun, one rank per GPU; chains are sharded (weak
-scaling, no collective inside the timed loop).
+`--impl reference` runs only the CPU oracle (the reference itself needs JAX,
+thrml and Tenstorrent hardware; neither JAX nor thrml exists on these hosts)
+on all host cores; it loads nothing of the product package.
 """
 
 from __future__ import annotations
@@ -48,32 +59,70 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 SEED = 0
+L2_FLUSH = "flushed before every timed step (256 MiB write)"
 
 
-class ErIsing:
+def _orc():
+    sys.path.insert(0, str(ROOT))
+    from oracle import models
+    from oracle import oracle as orc
+
+    return orc, models
+
+
+def _spin_init(blocks_nodes, C, seed):
+    rng = np.random.default_rng(seed)
+    return [rng.integers(0, 2, (C, n)).astype(bool) for n in blocks_nodes]
+
+
+class Workload:
+    name = ""
+    workload = ""
+    metric = "node-updates/sec (sites x chains x sweeps / s)"
+    scaling = "weak"
+    chains = 1
+    sweeps = 1
+    steps_alone = 5   # default timed steps when run alone
+    steps_extra = 5   # timed steps as an entry of the default run's `workloads`
+    e2e_steps = 5
+    data = ""
+
+    def free_nodes(self, prog):
+        return [len(b.nodes) for b in prog.gibbs_spec.free_blocks]
+
+    def init(self, prog, C, seed):
+        return _spin_init(self.free_nodes(prog), C, seed)
+
+    def host_inputs(self, init):
+        import torch
+
+        return [torch.from_numpy(s.astype(np.int8) * 2 - 1).pin_memory() for s in init]
+
+    # CPU sample of the configuration for the oracle: (program, chains, sweeps, description)
+    def cpu_sample(self):
+        raise NotImplementedError
+
+
+class ErIsing(Workload):
     """Sparse random-graph Ising: N = 2^20, Erdos-Renyi mean degree 8, greedy colouring, 256 chains/GPU, 200 sweeps."""
 
     name = "er"
     workload = "er-ising-n1048576-deg8-c256pergpu-s200"
-    metric = "node-updates/sec (sites x chains x sweeps / s)"
     chains = 256
     sweeps = 200
+    steps_alone = 20  # 2.4 s of timed work
     data = "synthetic (seeded Erdos-Renyi graph, random init)"
-    cpu_chains, cpu_sweeps = 32, 1
 
     def build(self):
         from tt_thrml_b200 import workloads
 
         return workloads.erdos_renyi_ising(1 << 20, 8.0, seed=SEED)
 
-    def init(self, prog, C, seed):
-        rng = np.random.default_rng(seed)
-        return [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
-
-    def host_inputs(self, init):
-        import torch
-
-        return [torch.from_numpy(s.astype(np.int8) * 2 - 1).pin_memory() for s in init]
+    def cpu_sample(self):
+        _, models = _orc()
+        raw = models.er_ising_raw(1 << 20, 8.0, seed=SEED)
+        prog = models.graph_ising(raw["row_ptr"], raw["cols"], raw["J"], raw["h"], raw["colours"], raw["beta"])
+        return prog, 256, 1, "the configuration's graph (own construction), all 256 chains x 1 sweep per sample"
 
     def check(self, ex):
         kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
@@ -89,17 +138,17 @@ class ErIsing:
             "sweeps_per_step": self.sweeps,
             "rng": "philox4x32-10 on device",
             "state_layout": ex.compiled.state_dtype,
-            "l2": "flushed before every timed step (256 MiB write)",
+            "l2": L2_FLUSH,
             "parallelism": f"chain-sharded x{world}",
         }
 
     def dtype(self, ex):
         return "u32 bit-packed spins, f32 fields" if ex.compiled.state_dtype == "bits" else "int8 spins, f32 fields"
 
-    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof):
+    def roofline(self, ex, prog, C, kernel_ms, n_prof, step_ms):
         layout = ex.compiled.state_dtype
         per_block = algorithmic_bytes(prog, C, layout)
-        achieved = sum(per_block) * n_prof / (sum(kernel_ms_per_group) / 1000.0) / 1e9
+        achieved = sum(per_block) * n_prof / (sum(kernel_ms) / 1000.0) / 1e9
         peak, kind = _peaks()["hbm"]
         traffic = _traffic_per_launch(sum(per_block) / len(per_block)) if layout == "bits" else None
         return {
@@ -112,25 +161,32 @@ class ErIsing:
             "peak_source": kind,
             "traffic": traffic,
             "algorithmic_bytes_per_update": sum(per_block) / (_n_nodes(prog) * C),
+            "issue": _issue_ceiling("spin_bits_er1m_c256.md", _n_nodes(prog) * C * n_prof / (sum(kernel_ms) / 1e3)),
         }
 
 
-class GaussBernoulliRBM:
+class GaussBernoulliRBM(Workload):
     """Gauss-Bernoulli RBM: 4096 gaussian visible x 8192 spin hidden, W ~ N(0, 0.01^2), 8192 chains, 100 sweeps."""
 
     name = "rbm"
     workload = "gauss-bernoulli-rbm-v4096-h8192-c8192-s100"
-    metric = "node-updates/sec (sites x chains x sweeps / s)"
     chains = 8192
     sweeps = 100
+    steps_alone = 20  # a 100 ms step: 2 s of timed work
+    steps_extra = 20
     data = "synthetic (seeded RBM weights rounded to bf16, random init)"
-    cpu_chains, cpu_sweeps = 8, 1
     V, H = 4096, 8192
 
     def build(self):
         from tt_thrml_b200 import workloads
 
         return workloads.gaussian_bernoulli_rbm(self.V, self.H, seed=SEED)
+
+    def cpu_sample(self):
+        _, models = _orc()
+        raw = models.rbm_raw(self.V, self.H, seed=SEED)
+        prog = models.dense_bipartite(raw["W"], raw["b_v"], raw["b_h"])
+        return prog, 64, 1, "the configuration's RBM (own construction), 64 of 8192 chains x 1 sweep per sample"
 
     def init(self, prog, C, seed):
         rng = np.random.default_rng(seed)
@@ -154,16 +210,16 @@ class GaussBernoulliRBM:
             "sweeps_per_step": self.sweeps,
             "rng": "philox4x32-10 on device",
             "state_layout": "bf16 chain-major blocks (tcgen05 GEMM operands)",
-            "l2": "operands (64-128 MiB per launch) exceed L2; flushed before every timed step (256 MiB write)",
+            "l2": "operands (64-128 MiB per launch) exceed L2; " + L2_FLUSH,
             "parallelism": f"chain-sharded x{world}",
         }
 
     def dtype(self, ex):
         return "bf16 operands, f32 accumulate (tcgen05)"
 
-    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof):
+    def roofline(self, ex, prog, C, kernel_ms, n_prof, step_ms):
         flops = 2.0 * 2.0 * C * self.V * self.H * n_prof  # two GEMMs per sweep
-        achieved = flops / (sum(kernel_ms_per_group) / 1000.0) / 1e12
+        achieved = flops / (sum(kernel_ms) / 1000.0) / 1e12
         peaks = _peaks()
         peak, kind = peaks["bf16"]
         return {
@@ -180,31 +236,28 @@ class GaussBernoulliRBM:
         }
 
 
-class Lattice2D:
+class Lattice2D(Workload):
     """2-D Ising 64x64 periodic, J=1, h=0, beta=0.44, 1024 chains; one step = the sampling schedule
     n_warmup=32, n_samples=64, steps_per_sample=2 with the per-chain magnetisation observed on device."""
 
     name = "lattice"
     workload = "ising2d-64x64-c1024-w32-n64-s2"
-    metric = "node-updates/sec (sites x chains x sweeps / s)"
     chains = 1024
     sweeps = 32 + 63 * 2
+    steps_alone = 4000
+    steps_extra = 4000  # a 0.5 ms step: 2 s of timed work, 10 clock samples
+    e2e_steps = 500
     data = "synthetic (uniform +-1 init from seed 0)"
-    cpu_chains, cpu_sweeps = 1024, 4
 
     def build(self):
         from tt_thrml_b200 import workloads
 
         return workloads.ising_lattice_2d(64, 64, J=1.0, h=0.0, beta=0.44)
 
-    def init(self, prog, C, seed):
-        rng = np.random.default_rng(seed)
-        return [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
-
-    def host_inputs(self, init):
-        import torch
-
-        return [torch.from_numpy(s.astype(np.int8) * 2 - 1).pin_memory() for s in init]
+    def cpu_sample(self):
+        _, models = _orc()
+        prog = models.ising2d(64, 64, J=1.0, h=0.0, beta=0.44)
+        return prog, 1024, 8, "the configuration's lattice (own construction), all 1024 chains x 8 sweeps per sample"
 
     def check(self, ex):
         kinds = {g.kernel_artifact.kind for g in ex.compiled.sampling_groups}
@@ -219,20 +272,21 @@ class Lattice2D:
             "sweeps_per_step": self.sweeps,
             "observable": "per-chain magnetisation, 64 samples, summed on device",
             "state_layout": ex.compiled.state_dtype,
-            "l2": "state (512 KiB) is L2-resident by design; flushed before every timed step (256 MiB write)",
+            "l2": "state (512 KiB) is L2-resident by design; " + L2_FLUSH,
             "parallelism": f"chain-sharded x{world}",
         }
 
     def dtype(self, ex):
         return ErIsing.dtype(self, ex)
 
-    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof, step_ms=None):
+    def roofline(self, ex, prog, C, kernel_ms, n_prof, step_ms):
         if ex.compiled.sampling_groups[0].kernel_artifact.kind != "ising2d_resident":
-            return ErIsing.roofline(self, ex, prog, C, kernel_ms_per_group, n_prof) | {"traffic": None}
+            return ErIsing.roofline(self, ex, prog, C, kernel_ms, n_prof, step_ms) | {"traffic": None}
         # shared-memory resident: one launch runs every sweep of a step; state bits read and written once per
         # half-sweep as if from memory (the algorithmic bytes), over the device time of the timed steps
         per_update = 2.0 / 8.0
-        achieved = _n_nodes(prog) * C * self.sweeps * per_update / (step_ms / 1000.0) / 1e9
+        rate = _n_nodes(prog) * C * self.sweeps / (step_ms / 1000.0)
+        achieved = rate * per_update / 1e9
         peak, kind = _peaks()["hbm"]
         return {
             "kernel": "k_ising2d_resident",
@@ -245,37 +299,37 @@ class Lattice2D:
             "traffic": _profile_traffic("ising2d_resident_64x64_c1024.md"),
             "algorithmic_bytes_per_update": per_update,
             "note": "state resident in shared memory for the whole step; DRAM is touched only at launch start/end",
+            "issue": _issue_ceiling("ising2d_resident_64x64_c1024.md", rate),
         }
 
 
-class Potts3D:
+class Potts3D(Workload):
     """3-D q=8 Potts 128^3 periodic, per-axis symmetric 8x8 couplings ~ N(0, 1), bias ~ N(0, 0.5), 64 chains,
     100 sweeps per step."""
 
     name = "potts"
     workload = "potts3d-128cube-q8-c64-s100"
-    metric = "node-updates/sec (sites x chains x sweeps / s)"
     chains = 64
     sweeps = 100
     data = "synthetic (seeded couplings and biases, uniform random categories)"
-    cpu_chains, cpu_sweeps = 64, 1
     side, q = 128, 8
+    steps_alone = 40  # a 70 ms step: 2.8 s of timed work
+    steps_extra = 40
 
     def build(self):
         from tt_thrml_b200 import workloads
 
         return workloads.potts_lattice_3d(self.side, self.q, seed=SEED)
 
-    def cpu_program(self, prog):
-        # the oracle runs on per-term tables, which a 128^3 lattice cannot afford: a 32^3 lattice of the
-        # same model family gives the per-update CPU rate
-        from tt_thrml_b200 import workloads
-
-        return workloads.potts_lattice_3d(32, self.q, seed=SEED)
+    def cpu_sample(self):
+        _, models = _orc()
+        raw = models.potts_raw(self.side, self.q, seed=SEED)
+        prog = models.potts3d(raw["dims"], raw["J"], raw["bias"])
+        return prog, 16, 1, "the configuration's lattice (own construction), 16 of 64 chains x 1 sweep per sample"
 
     def init(self, prog, C, seed):
         rng = np.random.default_rng(seed)
-        return [rng.integers(0, self.q, (C, len(b.nodes))).astype(np.int8) for b in prog.gibbs_spec.free_blocks]
+        return [rng.integers(0, self.q, (C, n)).astype(np.int8) for n in self.free_nodes(prog)]
 
     def host_inputs(self, init):
         import torch
@@ -295,17 +349,18 @@ class Potts3D:
             "sweeps_per_step": self.sweeps,
             "rng": "philox4x32-10 on device, inverse-CDF draw",
             "state_layout": "int8 categories [rows][chains]",
-            "l2": "state 128 MiB + bias 32 MiB exceed L2; flushed before every timed step (256 MiB write)",
+            "l2": "state 128 MiB + bias 32 MiB exceed L2; " + L2_FLUSH,
             "parallelism": f"chain-sharded x{world}",
         }
 
     def dtype(self, ex):
         return "int8 categories, f32 fields"
 
-    def roofline(self, ex, prog, C, kernel_ms_per_group, n_prof):
+    def roofline(self, ex, prog, C, kernel_ms, n_prof, step_ms):
         half = prog.n_sites // 2
         per_block = half * C * 2 + half * self.q * 4  # source rows read once, target rows written, bias read
-        achieved = per_block * len(kernel_ms_per_group) / (sum(kernel_ms_per_group) / 1000.0) / 1e9
+        achieved = per_block * len(kernel_ms) / (sum(kernel_ms) / 1000.0) / 1e9
+        rate = half * C * len(kernel_ms) / (sum(kernel_ms) / 1000.0)
         peak, kind = _peaks()["hbm"]
         return {
             "kernel": "k_potts3d",
@@ -317,206 +372,40 @@ class Potts3D:
             "peak_source": kind,
             "traffic": _profile_traffic("potts3d_128cube_q8_c64.md") if C == self.chains else None,
             "algorithmic_bytes_per_update": per_block / (half * C),
+            "issue": _issue_ceiling("potts3d_128cube_q8_c64.md", rate),
+            "sfu": _sfu_ceiling("potts3d_128cube_q8_c64.md", rate),
         }
 
 
-class BigIsing:
-    """Single-chain 2-D Ising 32768^2 periodic, J=1, h=0, beta=0.4407, int8 spins, 1000 sweeps per step,
-    domain-decomposed into row strips over the GPUs (deep halos exchanged every halo/2 sweeps)."""
+class BigIsing(Workload):
+    """Single-chain 2-D Ising 32768^2 periodic, J=1, h=0, beta=0.4407, 1000 sweeps per step, domain-decomposed
+    into row strips over the GPUs (deep halos exchanged every halo/2 sweeps)."""
 
     name = "ising"
     scaling = "strong"
     workload = "ising2d-32768sq-1chain-s1000-strips"
-    metric = "node-updates/sec (sites x chains x sweeps / s)"
     side = 32768
     sweeps = 1000
+    steps_alone = 5
+    steps_extra = 5
+    e2e_steps = 3
     halo = 40  # 20 sweeps per exchange, 1000 = 50 exchanges
     data = "synthetic (uniform +-1 spins from a seeded hash of the site)"
-    cpu_chains, cpu_sweeps = 1, 2
 
     def build(self):
         from tt_thrml_b200 import workloads
 
         return workloads.IsingLattice2D(self.side, self.side, beta=0.4407)
 
-    def cpu_program(self, prog):
-        # per-edge tables of the full lattice would take ~48 GB: a 1024^2 lattice gives the per-update rate
-        from tt_thrml_b200 import workloads
-
-        return workloads.IsingLattice2D(1024, 1024, beta=0.4407)
-
-    def init(self, prog, C, seed):
-        rng = np.random.default_rng(seed)
-        return [rng.integers(0, 2, (C, len(b.nodes))).astype(bool) for b in prog.gibbs_spec.free_blocks]
+    def cpu_sample(self):
+        _, models = _orc()
+        prog = models.ising2d(1024, self.side, J=1.0, h=0.0, beta=0.4407)
+        return prog, 1, 2, ("1024 of the 32768 rows (full 32768-wide rows, same couplings; own construction) x "
+                            "2 sweeps per sample")
 
 
-WORKLOADS = {w.name: w for w in (ErIsing(), GaussBernoulliRBM(), Lattice2D(), Potts3D(), BigIsing())}
-
-
-def run_ising(args, W):
-    """The domain-decomposed lattice: strong scaling (the lattice is fixed, the strips shrink with N)."""
-    import torch
-
-    from tt_thrml_b200.domain import LatticeStrips
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    prog = W.build()
-    S = W.sweeps
-    st = LatticeStrips(prog, device=dev, halo=W.halo)
-    st.load_random(SEED)
-    st.prepare_rng(SEED, S * (args.steps + args.warmup) + S)
-    stream = st._stream
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
-        st.run_sweeps(S)
-    barrier()
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    with ClockSampler(local) as clocks:
-        for e0, e1 in events:
-            with torch.cuda.stream(stream):
-                flush.fill_(1)
-            e0.record(stream)
-            st.run_sweeps(S)
-            e1.record(stream)
-        barrier()
-    del flush
-    st.check_errors()
-    dt_ms = sum(e0.elapsed_time(e1) for e0, e1 in events)
-    if dist is not None:
-        t = torch.tensor([dt_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dt_ms = float(t.item())
-    n_sites = W.side * W.side
-    updates = n_sites * S * args.steps
-    value = updates / (dt_ms / 1000.0)
-    periods = S // (W.halo // 2)
-    gpu_launches = args.steps * (periods * (W.halo + 2) + 1)  # import + half-sweeps + signal per period, ctl advance
-    em = st.energy_magnetisation()
-
-    # roofline: one eager half-sweep of the own rows, CUDA events on the launch stream
-    hw = W.side // 2
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    n_prof = 10
-    nat_bytes = 0
-    st.cuda_graphs = False
-    from tt_thrml_b200 import _native as nat
-
-    nat.bind_device(local)
-    with torch.cuda.stream(stream):
-        ev[0].record(stream)
-        for k in range(n_prof):
-            st._cuda_halfsweep(k & 1, st.D, st.D + st.h, st.sweep, stream)
-            nat_bytes += 2 * st.h * st.row_bytes  # other colour read once + own colour written once
-        ev[1].record(stream)
-    stream.synchronize()
-    kms = ev[0].elapsed_time(ev[1]) / n_prof
-    achieved = nat_bytes / n_prof / (kms / 1000.0) / 1e9
-    peak, kind = _peaks()["hbm"]
-
-    # end to end: pinned host split-colour lattice in, 1000 sweeps, energy/magnetisation trace out
-    host = [torch.empty((W.side, hw), dtype=torch.int8).pin_memory() for _ in range(2)]
-    for c in range(2):
-        host[c].copy_(st._own_rows(c).cpu().repeat(W.side // st.h, 1))
-    st.cuda_graphs = True
-    e2e_times = []
-    for s in range(args.steps):
-        barrier()
-        t0 = time.perf_counter()
-        st.load_split_colours(host[0], host[1])
-        st.prepare_rng(SEED + 1 + s, S)
-        st.run_sweeps(S)
-        trace = st.energy_magnetisation()
-        torch.cuda.synchronize(dev)
-        e2e_times.append(time.perf_counter() - t0)
-    e2e_s = sum(e2e_times)
-    if dist is not None:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    h2d = st.rows_local * hw * 2
-    d2h = int(trace.nbytes)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        v, _ = cpu_oracle_sample(W, prog, W.cpu_chains, W.cpu_sweeps, threads)
-        cpu = {"value": v, "unit": "node-updates/s", "cores": threads, "kind": "port",
-               "sample": _cpu_sample_text(W, prog, W.cpu_chains, W.cpu_sweeps)}
-    if rank == 0:
-        line = {
-            "metric": W.metric,
-            "value": value,
-            "unit": "node-updates/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": dt_ms / args.steps,
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "int8 spins" if st.storage == "int8" else "bit-packed spins (32 sites per uint32)",
-            "data": W.data,
-            "config": {
-                "workload": W.workload,
-                "lattice": f"{W.side}x{W.side} periodic, 1 chain",
-                "sweeps_per_step": S,
-                "strips": world,
-                "halo_rows": W.halo,
-                "exchange": "boundary rows stored into the neighbours' mailboxes by the half-sweep kernel (peer "
-                            "memory over NVLink), flag per period, every halo/2 sweeps",
-                "rng": "philox4x32-10 on device",
-                "l2": "state 1 GiB exceeds L2; flushed before every timed step (256 MiB write)",
-                "parallelism": f"row strips x{world}",
-                "final_energy_per_site": float(em[-1, 0]),
-                "final_magnetisation_per_site": float(em[-1, 1]),
-            },
-            "roofline": {
-                "kernel": ("k_ising2d_bits" if st.storage == "bits" else
-                           "k_ising2d_planes" if st.rng_layout == "planes" else "k_ising2d"),
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": peak,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "peak_source": kind,
-                "traffic": _profile_traffic("ising2d_32768.md") if st.storage == "bits" and world == 1 else None,
-                "algorithmic_bytes_per_update": 2.0 * st.row_bytes / hw,
-                "note": ("bit-packed rows move 0.25 B per update; the kernel is bound by instruction issue "
-                         "(bit-sliced decision), not by HBM" if st.storage == "bits" else None),
-            },
-            "e2e": {"value": updates / e2e_s, "unit": "node-updates/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": gpu_launches,
-            "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
-
-
-
-def _n_nodes(prog):
-    return sum(len(b.nodes) for b in prog.gibbs_spec.blocks)
+WORKLOADS = {w.name: w for w in (ErIsing(), Lattice2D(), GaussBernoulliRBM(), Potts3D(), BigIsing())}
+HEADLINE = "er"
 
 
 def _peaks():
@@ -649,142 +538,166 @@ def algorithmic_bytes(prog, n_chains: int, layout: str):
     return out
 
 
-def cpu_oracle_sample(W, prog, n_chains: int, n_sweeps: int, threads: int):
-    """Times the CPU oracle on `n_sweeps` full sweeps of `n_chains` chains; returns (updates/s, seconds)."""
-    sys.path.insert(0, str(ROOT))
-    from oracle import oracle as orc
+def _issue_figures(name: str):
+    return _profile_figures(name, ("thread_instructions_per_update",))
 
-    prog = W.cpu_program(prog) if hasattr(W, "cpu_program") else prog
-    o = orc.OracleSampler(prog, n_chains=n_chains, n_threads=threads)
-    o.load_state(W.init(prog, n_chains, 1))
-    o.sweep(0, seed=7)  # warm
+
+def _issue_ceiling(profile: str, rate: float):
+    """Instruction-issue ceiling of a kernel from its committed ncu summary: 148 SMs x 4 schedulers x 32
+    lanes per cycle at the maximum SM clock, over the thread instructions one update executes."""
+    vals = _issue_figures(profile)
+    if vals is None:
+        return None
+    per = vals["thread_instructions_per_update"]
+    ceiling = 148 * 4 * 32 * 1.965e9 / per
+    return {"thread_instructions_per_update": per, "ceiling_updates_per_s": ceiling, "frac": rate / ceiling,
+            "source": f"profiles/{profile}"}
+
+
+def _sfu_ceiling(profile: str, rate: float):
+    """Special-function (XU) ceiling: 16 results per SM per cycle at the maximum SM clock over the XU
+    instructions (ex2) one update executes, from the committed ncu summary."""
+    vals = _profile_figures(profile, ("xu_instructions_per_update",))
+    if vals is None:
+        return None
+    per = vals["xu_instructions_per_update"]
+    if per <= 0:
+        return {"xu_instructions_per_update": 0.0, "ceiling_updates_per_s": None, "frac": 0.0,
+                "source": f"profiles/{profile}"}
+    ceiling = 148 * 16 * 1.965e9 / per
+    return {"xu_instructions_per_update": per, "ceiling_updates_per_s": ceiling, "frac": rate / ceiling,
+            "source": f"profiles/{profile}"}
+
+
+def _n_nodes(prog):
+    return sum(len(b.nodes) for b in prog.gibbs_spec.blocks)
+
+
+class DistCtx:
+    """One process per GPU (torchrun env) or a single process."""
+
+    def __init__(self, backend_ok: bool = True):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dist = None
+        if not backend_ok:
+            return
+        import torch
+
+        self.dev = torch.device("cuda", self.local)
+        torch.cuda.set_device(self.dev)
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
+            self.dist = dist
+
+    def barrier(self):
+        import torch
+
+        if self.dist is not None:
+            self.dist.barrier()
+        torch.cuda.synchronize(self.dev)
+
+    def max(self, x: float) -> float:
+        if self.dist is None:
+            return float(x)
+        import torch
+
+        t = torch.tensor([float(x)], device=self.dev, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def _oracle_init(oprog, C, seed):
+    rng = np.random.default_rng(seed)
+    out = []
+    for b in oprog.blocks[: oprog.n_free]:
+        if b.family == "spin":
+            out.append(rng.integers(0, 2, (C, b.n_nodes)).astype(bool))
+        elif b.family == "categorical":
+            out.append(rng.integers(0, b.q, (C, b.n_nodes)))
+        else:
+            out.append(rng.standard_normal((C, b.n_nodes)).astype(np.float32))
+    return out
+
+
+def cpu_oracle_time(oprog, C, n_sweeps, threads, seed=1):
+    """Seconds of `n_sweeps` sweeps of the CPU oracle over C chains (after one untimed sweep)."""
+    orc, _ = _orc()
+    o = orc.OracleSampler(oprog, n_chains=C, n_threads=threads)
+    o.load_state(_oracle_init(oprog, C, seed))
+    o.sweep(0, seed=7)
     t0 = time.perf_counter()
     for s in range(n_sweeps):
         o.sweep(1 + s, seed=7)
-    dt = time.perf_counter() - t0
-    return _n_nodes(prog) * n_chains * n_sweeps / dt, dt
+    return time.perf_counter() - t0
 
 
-def _cpu_sample_text(W, prog, chains, sweeps):
-    prog = W.cpu_program(prog) if hasattr(W, "cpu_program") else prog
-    return (f"CPU oracle (C restatement, float32 state), {_n_nodes(prog)} nodes x {chains} chains x "
-            f"{sweeps} sweep(s) per sample")
-
-
-def run_reference(args, W):
-    """CPU arm: the oracle restatement of the reference's group kernel on all host cores."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return 0
+def cpu_baseline(W):
     threads = os.cpu_count() or 1
-    prog = W.build()
-    cprog = W.cpu_program(prog) if hasattr(W, "cpu_program") else prog
-    chains, sweeps = W.cpu_chains, W.cpu_sweeps  # bounded sample of the workload per step
-    for _ in range(args.warmup):
-        cpu_oracle_sample(W, prog, chains, sweeps, threads)
-    times = []
-    for _ in range(args.steps):
-        _, dt = cpu_oracle_sample(W, prog, chains, sweeps, threads)
-        times.append(dt)
-    tot = sum(times)
-    value = _n_nodes(cprog) * chains * sweeps * args.steps / tot
-    line = {
-        "impl": "reference",
-        "metric": W.metric,
-        "value": value,
-        "unit": "node-updates/s",
-        "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": 1000.0 * tot / args.steps,
-        "higher_is_better": True,
-        "scaling": getattr(W, "scaling", "weak"),
-        "vs_baseline": None,
-        "dtype": "f32",
-        "data": W.data,
-        "config": {"workload": W.workload, "sample": f"all {_n_nodes(cprog)} nodes x {chains} chains x {sweeps} "
-                                                      "sweep(s) per step"},
-        "cpu_baseline": {
-            "value": value,
-            "unit": "node-updates/s",
-            "cores": threads,
-            "kind": "port",
-            "sample": _cpu_sample_text(W, prog, chains, sweeps),
-        },
-        "e2e": {"value": value, "unit": "node-updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    oprog, C, S, what = W.cpu_sample()
+    dt = cpu_oracle_time(oprog, C, S, threads)
+    return {"value": oprog.total * C * S / dt, "unit": "node-updates/s", "cores": threads, "kind": "port",
+            "sample": f"CPU oracle (C restatement of the reference's group math, float32 state): {what}"}
 
 
-def run_ours(args, W):
+def run_chain_sharded(ctx, args, W, steps, warmup, cpu):
+    """Chains sharded over the GPUs (weak scaling: W.chains per GPU), through make_mesh_executor."""
     import torch
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-
-    from tt_thrml_b200 import Executor, make_cuda_config
+    from tt_thrml_b200 import make_cuda_config, make_mesh_executor
     from tt_thrml_b200.backend import CudaDevice
     from tt_thrml_b200.observers import MagnetizationObserver
 
+    dev = ctx.dev
     prog = W.build()
     n_nodes = _n_nodes(prog)
     C, S = W.chains, W.sweeps
-    device = CudaDevice(local)
-    cfg = make_cuda_config(n_chains=C, cuda_graphs=True)
-    total_sweeps = S * (args.steps + args.warmup) + 16
-    ex = Executor(None, device, prog, cfg, n_sweeps=total_sweeps, n_chains=C, chain_offset=rank * C)
+    cfg = make_cuda_config(n_chains=C * ctx.world, cuda_graphs=True)
+    total_sweeps = S * (steps + warmup) + 16
+    mesh = make_mesh_executor(None, CudaDevice(ctx.local), prog, cfg, n_sweeps=total_sweeps, n_chains=C * ctx.world,
+                              gather=False)
+    ex = mesh.shards[0]  # this process's chains
+    assert ex.n_chains == C and ex.chain_offset == ctx.rank * C
     W.check(ex)
     n_groups = len(ex.compiled.sampling_groups)
-    init = W.init(prog, C, 100 + rank)
-    ex.load_state(init, [])
-    ex.prepare_rng(SEED)
+    init = W.init(prog, C, 100 + ctx.rank)
+    mesh.load_state(init, [])
+    mesh.prepare_rng(SEED)
     stream = ex.stream
 
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    # ---- device-resident steps: warmup, then K timed steps
-    for _ in range(args.warmup):
-        ex.run_sweeps(S)
-    barrier()
-    # Each step is timed by its own event pair; between steps a 256 MiB buffer is
-    # written so every step starts with a cold L2 (126 MB).
+    # ---- device-resident steps: warmup, then `steps` timed steps, each with its own event pair; a 256 MiB
+    # write between steps starts every step with a cold L2 (126 MB)
+    for _ in range(warmup):
+        mesh.run_sweeps(S)
+    ctx.barrier()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with ClockSampler(local) as clocks:
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    with ClockSampler(ctx.local) as clocks:
         for e0, e1 in events:
             with torch.cuda.stream(stream):
                 flush.fill_(1)
             e0.record(stream)
-            ex.run_sweeps(S)
+            mesh.run_sweeps(S)
             e1.record(stream)
-        barrier()
+        ctx.barrier()
     ex.check_device_errors()
-    dt_ms = sum(e0.elapsed_time(e1) for e0, e1 in events)
+    dt_ms = ctx.max(sum(e0.elapsed_time(e1) for e0, e1 in events))
     del flush
-    if dist is not None:
-        t = torch.tensor([dt_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dt_ms = float(t.item())
-    updates = world * n_nodes * C * S * args.steps
+    updates = ctx.world * n_nodes * C * S * steps
     value = updates / (dt_ms / 1000.0)
     resident = ex._resident_plans() is not None
     # group kernels + the run-control advance of each graph, or one launch per step (resident lattice)
-    gpu_launches = args.steps * (1 if resident else S * n_groups + 1)
+    gpu_launches = steps * (1 if resident else S * n_groups + 1)
 
     # ---- roofline: per-launch CUDA events on the launch stream (eager sweeps)
     ex.profile = True
@@ -794,8 +707,7 @@ def run_ours(args, W):
         ex.run_sweep()
     ex.profile = False
     kernel_ms = [kms for _, _, kms in ex._timing_log]
-    roofline = (W.roofline(ex, prog, C, kernel_ms, n_prof, step_ms=dt_ms / args.steps) if W.name == "lattice"
-                else W.roofline(ex, prog, C, kernel_ms, n_prof))
+    roofline = W.roofline(ex, prog, C, kernel_ms, n_prof, dt_ms / steps)
 
     # ---- end to end through the public API (pinned host state in, results out)
     host_init = W.host_inputs(init)
@@ -808,19 +720,20 @@ def run_ours(args, W):
         obs = MagnetizationObserver(nodes)
 
         def e2e_call(key):
-            _, m = ex.sample_with_observation(key, sched, obs, init_state_free=host_init)
+            _, m = mesh.sample_with_observation(key, sched, obs, init_state_free=host_init)
             return [m]  # float64 magnetisation per chain per sample
     else:
         sched = SimpleNamespace(n_warmup=S, n_samples=1, steps_per_sample=1)
 
         def e2e_call(key):
-            return ex.sample_states(key, sched, nodes, init_state_free=host_init)
+            return mesh.sample_states(key, sched, nodes, init_state_free=host_init)
 
     e2e_call(SEED + 1)  # warm the graph for this schedule
-    barrier()
+    ctx.barrier()
+    n_e2e = min(steps, W.e2e_steps)
     e2e_times = []
-    for s in range(args.steps):
-        barrier()
+    for s in range(n_e2e):
+        ctx.barrier()
         t0 = time.perf_counter()
         out = e2e_call(SEED + 2 + s)
         torch.cuda.synchronize(dev)
@@ -828,87 +741,222 @@ def run_ours(args, W):
     d2h = int(sum(np.asarray(a).nbytes for a in out))  # bytes the call returned to the host
     del out
     ex.check_device_errors()
-    e2e_s = sum(e2e_times)
-    if dist is not None:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_value = updates / e2e_s
+    e2e_s = ctx.max(sum(e2e_times))
+    e2e_value = ctx.world * n_nodes * C * S * n_e2e / e2e_s
+    dtype, config = W.dtype(ex), W.config(prog, ex, ctx.world)
+    del mesh, ex
+    torch.cuda.empty_cache()
+    if ctx.rank != 0:
+        return None
+    return {
+        "metric": W.metric,
+        "value": value,
+        "unit": "node-updates/s",
+        "n_gpus": ctx.world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": dt_ms / steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": dtype,
+        "data": W.data,
+        "config": config,
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": "node-updates/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": n_e2e,
+                "api": "make_mesh_executor(...).sample_with_observation" if W.name == "lattice"
+                       else "make_mesh_executor(...).sample_states"},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        v, _ = cpu_oracle_sample(W, prog, W.cpu_chains, W.cpu_sweeps, threads)
-        cpu = {
-            "value": v,
-            "unit": "node-updates/s",
-            "cores": threads,
-            "kind": "port",
-            "sample": _cpu_sample_text(W, prog, W.cpu_chains, W.cpu_sweeps),
-        }
 
-    if rank == 0:
-        line = {
-            "metric": W.metric,
-            "value": value,
-            "unit": "node-updates/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": dt_ms / args.steps,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": W.dtype(ex),
-            "data": W.data,
-            "config": W.config(prog, ex, world),
-            "roofline": roofline,
-            "e2e": {
-                "value": e2e_value,
-                "unit": "node-updates/s",
-                "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-            },
-            "gpu_launches": gpu_launches,
-            "clocks": clocks.summary(),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+def run_strips(ctx, args, W, steps, warmup, cpu):
+    """The domain-decomposed lattice: strong scaling (the lattice is fixed, the strips shrink with N)."""
+    import torch
+
+    from tt_thrml_b200 import _native as nat
+    from tt_thrml_b200.domain import LatticeStrips
+
+    dev = ctx.dev
+    prog = W.build()
+    S = W.sweeps
+    st = LatticeStrips(prog, device=dev, halo=W.halo)
+    st.load_random(SEED)
+    st.prepare_rng(SEED, S * (steps + warmup) + S)
+    stream = st._stream
+    for _ in range(warmup):
+        st.run_sweeps(S)
+    ctx.barrier()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    with ClockSampler(ctx.local) as clocks:
+        for e0, e1 in events:
+            with torch.cuda.stream(stream):
+                flush.fill_(1)
+            e0.record(stream)
+            st.run_sweeps(S)
+            e1.record(stream)
+        ctx.barrier()
+    del flush
+    st.check_errors()
+    dt_ms = ctx.max(sum(e0.elapsed_time(e1) for e0, e1 in events))
+    n_sites = W.side * W.side
+    updates = n_sites * S * steps
+    value = updates / (dt_ms / 1000.0)
+    periods = S // (W.halo // 2)
+    gpu_launches = steps * (periods * (W.halo + 2) + 1)  # import + half-sweeps + signal per period, ctl advance
+    em = st.energy_magnetisation()
+
+    # roofline: eager half-sweeps of the own rows, CUDA events on the launch stream
+    hw = W.side // 2
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    n_prof = 10
+    nat_bytes = 0
+    st.cuda_graphs = False
+    nat.bind_device(ctx.local)
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        for k in range(n_prof):
+            st._cuda_halfsweep(k & 1, st.D, st.D + st.h, st.sweep, stream)
+            nat_bytes += 2 * st.h * st.row_bytes  # other colour read once + own colour written once
+        ev[1].record(stream)
+    stream.synchronize()
+    kms = ev[0].elapsed_time(ev[1]) / n_prof
+    achieved = nat_bytes / n_prof / (kms / 1000.0) / 1e9
+    rate = st.h * W.side / 2 / (kms / 1000.0)
+    peak, kind = _peaks()["hbm"]
+
+    # end to end: pinned host split-colour lattice in, 1000 sweeps, energy/magnetisation trace out
+    host = [torch.empty((W.side, hw), dtype=torch.int8).pin_memory() for _ in range(2)]
+    for c in range(2):
+        host[c].copy_(st._own_rows(c).cpu().repeat(W.side // st.h, 1))
+    st.cuda_graphs = True
+    n_e2e = min(steps, W.e2e_steps)
+    e2e_times = []
+    for s in range(n_e2e):
+        ctx.barrier()
+        t0 = time.perf_counter()
+        st.load_split_colours(host[0], host[1])
+        st.prepare_rng(SEED + 1 + s, S)
+        st.run_sweeps(S)
+        trace = st.energy_magnetisation()
+        torch.cuda.synchronize(dev)
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_s = ctx.max(sum(e2e_times))
+    h2d = st.rows_local * hw * 2
+    d2h = int(trace.nbytes)
+    storage, layout, h_rows, row_bytes = st.storage, st.rng_layout, st.h, st.row_bytes
+    st.close()
+    del st, host
+    torch.cuda.empty_cache()
+    if ctx.rank != 0:
+        return None
+    return {
+        "metric": W.metric,
+        "value": value,
+        "unit": "node-updates/s",
+        "n_gpus": ctx.world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": dt_ms / steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8 spins" if storage == "int8" else "bit-packed spins (32 sites per uint32)",
+        "data": W.data,
+        "config": {
+            "workload": W.workload,
+            "lattice": f"{W.side}x{W.side} periodic, 1 chain",
+            "sweeps_per_step": S,
+            "strips": ctx.world,
+            "rows_per_strip": h_rows,
+            "halo_rows": W.halo,
+            "exchange": "boundary rows stored into the neighbours' mailboxes by the half-sweep kernel (peer "
+                        "memory over NVLink), flag per period, every halo/2 sweeps",
+            "rng": "philox4x32-10 on device",
+            "l2": "state 1 GiB exceeds L2; " + L2_FLUSH,
+            "parallelism": f"row strips x{ctx.world}",
+            "final_energy_per_site": float(em[-1, 0]),
+            "final_magnetisation_per_site": float(em[-1, 1]),
+        },
+        "roofline": {
+            "kernel": ("k_ising2d_bits" if storage == "bits" else
+                       "k_ising2d_planes" if layout == "planes" else "k_ising2d"),
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_source": kind,
+            "traffic": _profile_traffic("ising2d_32768.md") * h_rows / W.side
+                       if storage == "bits" and _profile_traffic("ising2d_32768.md") else None,
+            "algorithmic_bytes_per_update": 2.0 * row_bytes / hw,
+            "note": ("bit-packed rows move 0.25 B per update; the kernel is bound by instruction issue "
+                     "(bit-sliced decision), not by HBM" if storage == "bits" else None),
+            "issue": _issue_ceiling("ising2d_32768.md", rate) if storage == "bits" else None,
+        },
+        "e2e": {"value": updates / steps * n_e2e / e2e_s, "unit": "node-updates/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": n_e2e,
+                "api": "LatticeStrips.load_split_colours + run_sweeps + energy_magnetisation"},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }
+
+
+def run_reference(args, W):
+    """CPU arm: the oracle restatement of the reference's group math on all host cores, built from the
+    configuration's raw parameters by the oracle itself (nothing of the product package is loaded)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    oprog, C, S, what = W.cpu_sample()
+    orc, _ = _orc()
+    o = orc.OracleSampler(oprog, n_chains=C, n_threads=threads)
+    o.load_state(_oracle_init(oprog, C, 1))
+    sweep = 0
+
+    def step():
+        nonlocal sweep
+        t0 = time.perf_counter()
+        for _ in range(S):
+            o.sweep(sweep, seed=7)
+            sweep += 1
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        step()
+    times = [step() for _ in range(args.steps)]
+    tot = sum(times)
+    value = oprog.total * C * S * args.steps / tot
+    loaded = sorted({Path(m.__file__).name for m in list(sys.modules.values())
+                     if getattr(m, "__file__", None) and "tt_thrml_b200" in str(m.__file__)})
+    assert not loaded, f"the reference arm imported the product: {loaded}"
+    line = {
+        "impl": "reference",
+        "metric": W.metric,
+        "value": value,
+        "unit": "node-updates/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * tot / args.steps,
+        "higher_is_better": True,
+        "scaling": W.scaling,
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": W.data,
+        "config": {"workload": W.workload, "sample": what},
+        "cpu_baseline": {"value": value, "unit": "node-updates/s", "cores": threads, "kind": "port",
+                         "sample": f"CPU oracle (C restatement of the reference's group math): {what}"},
+        "e2e": {"value": value, "unit": "node-updates/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
     return 0
-
-
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None,
-                    help="timed steps (default 5; 2000 for the lattice workload, whose 0.5 ms step would otherwise "
-                         "give a timed region shorter than the clock sampler's period)")
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="er",
-                    help="er: sparse random-graph Ising (default, the headline); rbm: Gauss-Bernoulli RBM; "
-                         "lattice: 64x64 Ising with magnetisation samples; potts: 3-D q=8 Potts 128^3; "
-                         "ising: one-chain 32768^2 Ising in row strips over the GPUs")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-sweeps", type=int, default=0,
-                    help="run this many eager sweeps of the workload and exit (profiler target, no timing)")
-    ap.add_argument("--chains", type=int, default=0, help="profiler target only: chains (default: the workload's)")
-    args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
-    W = WORKLOADS[args.workload]
-    if args.steps is None:
-        args.steps = 2000 if W.name == "lattice" and args.impl != "reference" else 5
-    if args.impl == "reference":
-        return run_reference(args, W)
-    if W.name == "ising" and not args.profile_sweeps:
-        return run_ising(args, W)
-    if args.profile_sweeps:
-        return run_profile_target(args, W)
-    return run_ours(args, W)
 
 
 def run_profile_target(args, W) -> int:
@@ -941,6 +989,53 @@ def run_profile_target(args, W) -> int:
     torch.cuda.synchronize()
     ex.check_device_errors()
     print(f"profile target: {W.workload}, {C} chains, {n} sweeps x {len(ex.compiled.sampling_groups)} groups", flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps of the headline workload (default 5); the other workloads of the default "
+                         "run use their own step counts (about 2-4 s of timed work each)")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["all", *WORKLOADS], default="all",
+                    help="all (default): er as the headline plus lattice, rbm, potts and ising under 'workloads'; "
+                         "or one of them alone")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-sweeps", type=int, default=0,
+                    help="run this many eager sweeps of the workload and exit (profiler target, no timing)")
+    ap.add_argument("--chains", type=int, default=0, help="profiler target only: chains (default: the workload's)")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    names = list(WORKLOADS) if args.workload == "all" else [args.workload]
+    if args.impl == "reference":
+        W = WORKLOADS[HEADLINE if args.workload == "all" else args.workload]
+        if args.steps is None:
+            args.steps = 5
+        return run_reference(args, W)
+    if args.profile_sweeps:
+        return run_profile_target(args, WORKLOADS[HEADLINE if args.workload == "all" else args.workload])
+    ctx = DistCtx()
+    lines = {}
+    for i, name in enumerate(names):
+        W = WORKLOADS[name]
+        if i == 0:
+            steps = args.steps if args.steps is not None else W.steps_alone
+        else:
+            steps = W.steps_extra
+        cpu = None
+        if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(W)
+        run = run_strips if W.name == "ising" else run_chain_sharded
+        lines[name] = run(ctx, args, W, steps, args.warmup, cpu)
+    if ctx.rank == 0:
+        out = lines[names[0]]
+        if len(names) > 1:
+            out["workloads"] = {n: lines[n] for n in names[1:]}
+        print(json.dumps(out), flush=True)
+    ctx.close()
     return 0
 
 

@@ -81,6 +81,26 @@ def er_ising_raw(n: int = 1 << 20, mean_degree: float = 8.0, *, seed: int = 0, b
             "colours": greedy_colouring(row_ptr, cols)}
 
 
+def rbm_raw(n_visible: int = 4096, n_hidden: int = 8192, *, seed: int = 0, w_std: float = 0.01,
+            visible_bias_variance: float = 0.1) -> dict:
+    """Raw parameters of the Gauss-Bernoulli RBM configuration: W ~ N(0, w_std^2) rounded to bf16, visible
+    bias ~ N(0, visible_bias_variance), no hidden bias."""
+    rng = np.random.default_rng(seed)
+    W = orc.bf16_round((rng.standard_normal((n_visible, n_hidden)) * w_std).astype(np.float32))
+    b_v = (rng.standard_normal(n_visible) * np.sqrt(visible_bias_variance)).astype(np.float32)
+    return {"W": W, "b_v": b_v, "b_h": np.zeros(n_hidden, dtype=np.float32)}
+
+
+def potts_raw(side: int = 128, q: int = 8, *, seed: int = 0, j_std: float = 1.0, bias_variance: float = 0.5) -> dict:
+    """Raw parameters of the 3-D Potts configuration: per axis (A + A^T) / 2 with A ~ N(0, j_std^2), site
+    biases ~ N(0, bias_variance)."""
+    rng = np.random.default_rng(seed)
+    A = (rng.standard_normal((3, q, q)) * j_std).astype(np.float32)
+    J = ((A + A.transpose(0, 2, 1)) * np.float32(0.5)).astype(np.float32)
+    bias = (rng.standard_normal((side**3, q)) * np.sqrt(bias_variance)).astype(np.float32)
+    return {"dims": (side, side, side), "J": J, "bias": bias}
+
+
 def greedy_colouring(row_ptr, cols) -> np.ndarray:
     rp = np.ascontiguousarray(row_ptr, dtype=np.int64)
     cc = np.ascontiguousarray(cols, dtype=np.int32)

@@ -183,3 +183,16 @@ def test_lattice_programs_use_the_model_paths_by_default():
     assert isinstance(orc.lower_program(workloads.IsingLattice2D(4, 4)).model, models.Ising2DModel)
     assert isinstance(orc.lower_program(workloads.potts_lattice_3d(4, 3)).model, models.Potts3DModel)
     assert isinstance(orc.lower_program(workloads.gaussian_bernoulli_rbm(8, 8)).model, models.DenseModel)
+
+
+def test_rbm_and_potts_generators_reproduce_the_configuration_inputs():
+    raw = models.rbm_raw(64, 96, seed=3)
+    prog = workloads.gaussian_bernoulli_rbm(64, 96, seed=3)
+    np.testing.assert_array_equal(raw["W"], prog.W)
+    np.testing.assert_array_equal(raw["b_v"], prog.b_v)
+    np.testing.assert_array_equal(raw["b_h"], prog.b_h)
+    raw = models.potts_raw(6, 5, seed=4)
+    prog = workloads.potts_lattice_3d(6, 5, seed=4)
+    np.testing.assert_array_equal(raw["J"], prog.J)
+    np.testing.assert_array_equal(raw["bias"], prog.site_bias)
+    assert raw["dims"] == prog.dims

@@ -8,8 +8,10 @@ Philox counters keyed by the global chain index so the samples of a chain do
 not depend on how many GPUs share the run.  Two drivers:
 
 * one process per GPU (torch.distributed initialised, world size > 1): this
-  process owns chains [rank*C/W, (rank+1)*C/W); host read-backs are
-  all-gathered so every rank sees all chains;
+  process owns chains [rank*C/W, (rank+1)*C/W); initial states are given for
+  all C chains or for this rank's chains only; host read-backs are
+  all-gathered so every rank sees all chains (or, with gather=False, each
+  rank gets its own chains);
 * one process driving a `CudaMeshDevice` of G GPUs: one shard executor per
   GPU, all launched from this thread on per-GPU streams.
 
@@ -73,8 +75,13 @@ class MeshExecutor(Executor):
         profile: bool = False,
         n_chains: int | None = None,
         process_group=None,
+        gather: bool = True,
     ):
+        """gather: with one process per GPU, host read-backs (observe, sample_states, block_sums) return
+        every chain on every rank (all-gathered, like the reference's replicated state); False returns
+        this rank's own chains only (no collective: for outputs too large to replicate)."""
         total = int(n_chains if n_chains is not None else config.n_chains)
+        self.gather = bool(gather)
         self.ttnn, self.device, self.program, self.config = ttnn, device, program, config
         self.n_sweeps, self.profile = n_sweeps, profile
         self.total_chains = total
@@ -129,6 +136,9 @@ class MeshExecutor(Executor):
                     out[k].append(a)
                 continue
             a = a.reshape(-1, n)
+            if self._mode == "ranks" and a.shape[0] == self.n_chains != self.total_chains:
+                out[0].append(a)  # this rank's own chains only
+                continue
             if a.shape[0] != self.total_chains:
                 raise ValueError(f"block {bi}: expected ({n},) or ({self.total_chains}, {n}) states, got {a.shape}")
             for k, sh in enumerate(self.shards):
@@ -147,7 +157,7 @@ class MeshExecutor(Executor):
     def _gather_chains(self, arrays: list[np.ndarray]) -> np.ndarray:
         """Concatenates per-shard (C_local, ...) arrays along the chain axis, across ranks too."""
         local = np.concatenate(arrays, axis=0)
-        if self._mode != "ranks":
+        if self._mode != "ranks" or not self.gather:
             return local
         dist = _dist()
         parts: list = [None] * self._world
@@ -232,6 +242,15 @@ class MeshExecutor(Executor):
     def sample_with_observation(
         self, key, schedule, f_observe, *, init_state_free, state_clamp=(), observation_carry_init=None
     ):
+        if len(self.shards) == 1 and (self._mode == "single" or not self.gather):
+            # this process's chains only: the shard's own schedule (one CUDA graph, fused device observers)
+            sh = self.shards[0]
+            n_free = len(list(init_state_free))
+            part = self._split_state(list(init_state_free) + list(state_clamp))[0]
+            k = key if self.config.rng_mode == "philox" else \
+                self._chain_keys(key)[sh.chain_offset : sh.chain_offset + sh.n_chains]
+            return sh.sample_with_observation(k, schedule, f_observe, init_state_free=part[:n_free],
+                                              state_clamp=part[n_free:], observation_carry_init=observation_carry_init)
         n_total = schedule.n_warmup + max(0, schedule.n_samples - 1) * schedule.steps_per_sample
         self.load_state(list(init_state_free), list(state_clamp))
         self._prepare_rng_thrml_compat(key, schedule, n_total)
@@ -261,5 +280,6 @@ class MeshExecutor(Executor):
         return self.shards[0].timing_summary()
 
 
-def make_mesh_executor(ttnn, device, program, config: CUDAConfig, *, n_sweeps: int = 100, n_chains: int | None = None):
-    return MeshExecutor(ttnn, device, program, config, n_sweeps=n_sweeps, n_chains=n_chains)
+def make_mesh_executor(ttnn, device, program, config: CUDAConfig, *, n_sweeps: int = 100, n_chains: int | None = None,
+                       gather: bool = True):
+    return MeshExecutor(ttnn, device, program, config, n_sweeps=n_sweeps, n_chains=n_chains, gather=gather)
