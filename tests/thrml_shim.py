@@ -392,3 +392,26 @@ def two_spin_superblock_program():
         [SpinEBMFactor([Block([nodes[0]]), Block([nodes[1]])], [-1.0])],
         [],
     )
+
+
+def ising_grid_program(height: int, width: int, *, J: float = 1.0, h: float = 0.0, beta: float = 0.44,
+                       periodic: bool = True, colour_blocks: bool = True):
+    """An IsingEBM over a height x width grid (edges to the right and lower neighbours, wrapping when
+    periodic; J a scalar or one coupling per edge), free blocks = the two checkerboard colours with sites
+    in row-major order."""
+    nodes = [SpinNode() for _ in range(height * width)]
+    edges = []
+    for y in range(height):
+        for x in range(width):
+            if periodic or x + 1 < width:
+                edges.append((nodes[y * width + x], nodes[y * width + (x + 1) % width]))
+            if periodic or y + 1 < height:
+                edges.append((nodes[y * width + x], nodes[((y + 1) % height) * width + x]))
+    Jv = np.broadcast_to(np.asarray(J, np.float32), (len(edges),)).copy()
+    model = IsingEBM(nodes, edges, np.full(len(nodes), h, np.float32), Jv, beta)
+    colour = [(i // width + i % width) % 2 for i in range(len(nodes))]
+    if colour_blocks:
+        free = [Block([nd for nd, c in zip(nodes, colour) if c == k]) for k in range(2)]
+    else:  # rows split in halves: not a checkerboard
+        free = [Block(nodes[: len(nodes) // 2]), Block(nodes[len(nodes) // 2 :])]
+    return IsingSamplingProgram(model, free, []), nodes

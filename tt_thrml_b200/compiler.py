@@ -21,7 +21,13 @@ synthetic workloads in `tt_thrml_b200.workloads`) by providing
 
 from __future__ import annotations
 
+import dataclasses
+import hashlib
+import threading
+import weakref
+from collections import OrderedDict
 from dataclasses import dataclass
+from enum import Enum
 from typing import Any
 
 import numpy as np
@@ -1005,6 +1011,80 @@ def _plan_stencil(program, device, n_chains: int = 1):
     return plans
 
 
+def detect_ising_lattice(lowered) -> dict | None:
+    """The stencil description of a lowered program that is a periodic 2-D Ising lattice, else None.
+
+    A thrml program of a lattice (e.g. an IsingEBM over an H x W grid with periodic edges) lowers to
+    per-term tables; the stencil kernels run it when: two free spin blocks of n/2 nodes, block 0 the
+    colour-0 sites (x + y even) in row-major order and block 1 the colour-1 sites, one sampling group
+    each; every node with a bias (the same value everywhere) and exactly four non-zero pair terms of one
+    common weight whose sources are its four lattice neighbours.  Then the field of every node is
+    bias + weight * (sum of the neighbours' spins), which is what the stencil tables hold (the float32
+    grouping of the sum may differ from the lowered program's by rounding, inside the threshold band)."""
+    specs = lowered.specs
+    if lowered.n_free_blocks != 2 or len(specs) != 2 or any(s.family != Family.SPIN for s in specs):
+        return None
+    half = specs[0].n_nodes
+    if specs[1].n_nodes != half or specs[0].block_global_start != 0 or specs[1].block_global_start != half:
+        return None
+    if sorted(tuple(int(i) for i in g) for g in lowered.sampling_order) != [(0,), (1,)]:
+        return None
+    n = 2 * half
+    biases, nbrs, weights = [], [], []
+    for s in specs:
+        bias = np.zeros(half, dtype=np.float32)
+        pairs = []
+        for it, rp, w, src in _ragged_tables(s):
+            if it.n_categorical or w.shape[1] != 1 or src.shape[0] > 1:
+                return None
+            if src.shape[0] == 0:
+                bias = (bias + _sequential_row_sum(rp, w)).astype(np.float32)
+            else:
+                pairs.append((rp, w[:, 0], src[0]))
+        if not pairs:
+            return None
+        rp, vals, cols = _merge_rows(pairs, half) if len(pairs) > 1 else pairs[0]
+        keep = vals != 0.0
+        row_of = np.repeat(np.arange(half, dtype=np.int64), np.diff(rp))[keep]
+        if not (np.bincount(row_of, minlength=half) == 4).all():
+            return None
+        v = vals[keep]
+        if not (v == v[0]).all():
+            return None
+        weights.append(v[0])
+        biases.append(bias)
+        nbrs.append(np.sort(cols[keep].astype(np.int64).reshape(half, 4), axis=1))
+    if weights[0] != weights[1] or not (biases[0] == biases[0][0]).all() or not (biases[1] == biases[0][0]).all():
+        return None
+    # block-0 row 0 is site (0, 0): its neighbours sit at block-1 rows {0, W/2 - 1, W/2, (H - 1) W / 2}
+    W = 2 * int(nbrs[0][0][2] - half)
+    if W < 4 or n % W or (n // W) < 4 or (n // W) % 2:
+        return None
+    H = n // W
+    for c in range(2):
+        r = np.arange(half, dtype=np.int64)
+        y = (2 * r) // W
+        x = (2 * r) % W + ((y + c) & 1)
+        L = np.stack([y * W + (x - 1) % W, y * W + (x + 1) % W, ((y - 1) % H) * W + x, ((y + 1) % H) * W + x], 1)
+        if not np.array_equal(np.sort((1 - c) * half + L // 2, axis=1), nbrs[c]):
+            return None
+    return {"kind": "ising2d", "dims": (H, W), "edge_weight": np.float32(weights[0]),
+            "site_bias": np.float32(biases[0][0]), "block_rows": (0, half)}
+
+
+class _DetectedStencil:
+    """A lowered program recognised as a lattice, seen through the stencil planner's interface."""
+
+    def __init__(self, lowered, stencil: dict):
+        from types import SimpleNamespace
+
+        self.gibbs_spec = SimpleNamespace(sampling_order=[list(g) for g in lowered.sampling_order])
+        self._stencil = stencil
+
+    def tt_stencil(self) -> dict:
+        return self._stencil
+
+
 def _stencil_specs(program):
     """Light block specs (no tables) of a stencil program: family, size, flat start."""
     st = program.tt_stencil()
@@ -1019,6 +1099,126 @@ def _stencil_specs(program):
     )
 
 
+# ---------------------------------------------------------------------------
+# Plan cache (the counterpart of the reference's artifact cache,
+# tt_thrml/compiler.py:398-433, 457-463): compiled plans -- the lowered
+# program, the state layout and the group plans with their device tables --
+# keyed by a SHA-256 signature of the program's contents plus the device, the
+# chain count and the configuration fields that shape the plans.  A second
+# executor (or a second `sample_states` call) over the same program reuses the
+# tables instead of lowering and uploading them again.  Programs are taken as
+# immutable once compiled, as thrml's are.  The cache holds device memory, so
+# it keeps the most recent PLAN_CACHE_SIZE entries; `clear_plan_cache()` drops
+# them.  Thread-safe.
+# ---------------------------------------------------------------------------
+
+PLAN_CACHE_SIZE = 8
+_PLAN_CACHE_LOCK = threading.Lock()
+_PLAN_CACHE: "OrderedDict[tuple, tuple]" = OrderedDict()  # key -> (lowered, state_dtype, plans)
+_PROGRAM_SIGNATURES: dict = {}  # id(program) -> (weakref to program, signature, lowered or None)
+
+
+def clear_plan_cache() -> None:
+    with _PLAN_CACHE_LOCK:
+        _PLAN_CACHE.clear()
+        _PROGRAM_SIGNATURES.clear()
+
+
+def plan_cache_size() -> int:
+    with _PLAN_CACHE_LOCK:
+        return len(_PLAN_CACHE)
+
+
+def _hash_into(h, obj) -> None:
+    torch = _torch()
+    if isinstance(obj, torch.Tensor):
+        obj = obj.detach().cpu().numpy()
+    if isinstance(obj, np.ndarray) or isinstance(obj, np.generic):
+        a = np.ascontiguousarray(obj)
+        h.update(f"nd{a.dtype.str}{a.shape}".encode())
+        h.update(a.tobytes())
+    elif isinstance(obj, dict):
+        h.update(b"{")
+        for k in sorted(obj, key=str):
+            h.update(str(k).encode())
+            _hash_into(h, obj[k])
+        h.update(b"}")
+    elif isinstance(obj, (list, tuple)):
+        h.update(b"[")
+        for x in obj:
+            _hash_into(h, x)
+        h.update(b"]")
+    elif isinstance(obj, Enum):
+        h.update(repr(obj.value).encode())
+    elif dataclasses.is_dataclass(obj) and not isinstance(obj, type):
+        h.update(type(obj).__name__.encode())
+        for f in dataclasses.fields(obj):
+            h.update(f.name.encode())
+            _hash_into(h, getattr(obj, f.name))
+    else:
+        h.update(repr(obj).encode())
+
+
+def _structure(program) -> list:
+    gs = program.gibbs_spec
+    return [[len(b.nodes) for b in gs.free_blocks], [len(b.nodes) for b in gs.clamped_blocks],
+            [[int(i) for i in g] for g in gs.sampling_order]]
+
+
+def program_signature(program) -> tuple[str, Any]:
+    """(SHA-256 signature of the program's contents, its lowering when one was needed to compute it).
+
+    Lattice programs are signed by their stencil description, dense bipartite programs by their
+    coupling matrices, table programs by their tables and any other program (a thrml program) by its
+    lowering, like the reference's kernel signature keys (tt_thrml/compiler.py:398-433)."""
+    h = hashlib.sha256()
+    lowered = None
+    _hash_into(h, _structure(program))
+    if callable(getattr(program, "tt_stencil", None)):
+        h.update(b"stencil")
+        _hash_into(h, program.tt_stencil())
+    if callable(getattr(program, "tt_dense_couplings", None)):
+        h.update(b"dense")
+        _hash_into(h, program.tt_dense_couplings())
+    elif callable(getattr(program, "tt_lower_blocks", None)) and not callable(getattr(program, "tt_stencil", None)):
+        h.update(b"tables")
+        _hash_into(h, list(program.tt_lower_blocks()))
+    elif not callable(getattr(program, "tt_stencil", None)):
+        lowered = lower_program(program)
+        h.update(b"lowered")
+        _hash_into(h, list(lowered.specs))
+    return h.hexdigest(), lowered
+
+
+def _signature_of(program) -> tuple[str, Any]:
+    """program_signature, remembered per live program object (a repeated call does not lower again)."""
+    with _PLAN_CACHE_LOCK:
+        hit = _PROGRAM_SIGNATURES.get(id(program))
+        if hit is not None and hit[0]() is program:
+            return hit[1], hit[2]
+    sig, lowered = program_signature(program)
+    try:
+        ref = weakref.ref(program)
+    except TypeError:
+        return sig, lowered
+    with _PLAN_CACHE_LOCK:
+        for k in [k for k, v in _PROGRAM_SIGNATURES.items() if v[0]() is None]:
+            del _PROGRAM_SIGNATURES[k]
+        _PROGRAM_SIGNATURES[id(program)] = (ref, sig, lowered)
+    return sig, lowered
+
+
+def _copy_plans(plans) -> list:
+    """Per-executor plan objects sharing the cached device tables (descriptor caches stay private)."""
+    out = []
+    for p in plans:
+        q = dataclasses.replace(p)
+        if isinstance(q, GenericGroupPlan):
+            q._desc, q._desc_variates = None, ()
+        out.append(q)
+    return out
+
+
 def compile_program(
     ttnn,
     device,
@@ -1028,11 +1228,38 @@ def compile_program(
     n_sweeps: int = 100,
     n_chains: int | None = None,
     force_generic: bool = False,
+    cache: bool = True,
 ) -> CompiledProgram:
-    """Compile a thrml program for the CUDA executor (tt_thrml/compiler.py:524-592)."""
+    """Compile a thrml program for the CUDA executor (tt_thrml/compiler.py:524-592).
+
+    cache: reuse the plans (device tables) of an earlier compilation of a program with the same
+    signature for the same device, chain count and configuration."""
     del ttnn
     n_chains = int(n_chains if n_chains is not None else config.n_chains)
     tdev = resolve_torch_device(device)
+    key, pre_lowered = None, None
+    if cache:
+        sig, pre_lowered = _signature_of(program)
+        key = (sig, tdev.type, tdev.index, n_chains, config.plan_key(), bool(force_generic))
+        with _PLAN_CACHE_LOCK:
+            hit = _PLAN_CACHE.get(key)
+            if hit is not None:
+                _PLAN_CACHE.move_to_end(key)
+        if hit is not None:
+            lowered, state_dtype, plans = hit
+            return _assemble(lowered, state_dtype, _copy_plans(plans), n_sweeps, n_chains, tdev)
+    lowered, state_dtype, plans = _build_plans(program, config, n_chains, tdev, force_generic, pre_lowered)
+    if key is not None:
+        with _PLAN_CACHE_LOCK:
+            _PLAN_CACHE[key] = (lowered, state_dtype, plans)
+            _PLAN_CACHE.move_to_end(key)
+            while len(_PLAN_CACHE) > PLAN_CACHE_SIZE:
+                _PLAN_CACHE.popitem(last=False)
+        plans = _copy_plans(plans)
+    return _assemble(lowered, state_dtype, plans, n_sweeps, n_chains, tdev)
+
+
+def _build_plans(program, config: CUDAConfig, n_chains: int, tdev, force_generic: bool, pre_lowered=None):
     if not force_generic and config.stencil and stencil_eligible(program, n_chains, config.rng_mode):
         specs = _stencil_specs(program)
         order = tuple(tuple(int(i) for i in g) for g in program.gibbs_spec.sampling_order)
@@ -1047,7 +1274,14 @@ def compile_program(
                                  tuple(s.block_global_start for s in specs))
         state_dtype, plans = "dense_bf16", _plan_dense(program, tdev, config.resolved_dense_precision)
     else:
-        lowered = lower_program(program)
+        lowered = pre_lowered if pre_lowered is not None else lower_program(program)
+        if not force_generic and config.stencil:
+            st = detect_ising_lattice(lowered)
+            view = _DetectedStencil(lowered, st) if st is not None else None
+            if view is not None and stencil_eligible(view, n_chains, config.rng_mode):
+                plans = _plan_stencil(view, tdev, n_chains)
+                _torch().cuda.synchronize(tdev)
+                return lowered, ("bits" if plans[0].kind == "ising2d_resident" else "int8"), plans
         couplings = None
         if not force_generic and config.dense_detect and not callable(getattr(program, "tt_stencil", None)):
             couplings = detect_dense_couplings(lowered, n_chains, round_weights=config.dense_round_weights)
@@ -1059,6 +1293,10 @@ def compile_program(
                 lowered, n_chains, tdev, force_generic=force_generic, spin_layout=config.spin_layout
             )
     _torch().cuda.synchronize(tdev)  # tables uploaded before any stream uses them
+    return lowered, state_dtype, plans
+
+
+def _assemble(lowered, state_dtype, plans, n_sweeps: int, n_chains: int, tdev) -> CompiledProgram:
     blocks = tuple(CompiledFusedBlock(spec=s, kernel_artifact=None) for s in lowered.specs)
     groups = tuple(
         CompiledSamplingGroup(block_indices=tuple(g), kernel_artifact=p) for g, p in zip(lowered.sampling_order, plans)
@@ -1082,6 +1320,10 @@ def compile_program(
 
 __all__ = [
     "compile_program",
+    "clear_plan_cache",
+    "plan_cache_size",
+    "program_signature",
+    "PLAN_CACHE_SIZE",
     "lower_program",
     "plan_program",
     "LoweredProgram",
@@ -1092,5 +1334,6 @@ __all__ = [
     "IsingStencilGroupPlan",
     "IsingResidentGroupPlan",
     "detect_dense_couplings",
+    "detect_ising_lattice",
     "ising_pattern_tables",
 ]

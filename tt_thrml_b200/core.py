@@ -93,6 +93,11 @@ class CUDAConfig:
         payload = {"arch": self.arch, "rng_mode": self.rng_mode}
         return hashlib.sha256(json.dumps(payload, sort_keys=True).encode()).hexdigest()[:16]
 
+    def plan_key(self) -> tuple:
+        """The fields that decide a program's kernels and device tables (the plan cache's part of the key)."""
+        return (self.arch, self.rng_mode, self.spin_layout, self.resolved_dense_precision, bool(self.stencil),
+                bool(self.dense_detect), bool(self.dense_round_weights))
+
 
 # Drop-in name for callers written against the reference.
 TTMLIRConfig = CUDAConfig
