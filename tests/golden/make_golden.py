@@ -107,7 +107,11 @@ def probe_kats(ref: Path) -> dict:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    ref = Path(sys.argv[1])
+    if not (ref / "tests" / "test_compiler_lowering.py").exists():
+        sys.exit(f"{ref} does not look like the reference checkout (tests/test_compiler_lowering.py missing)")
     out = {"source": "reference tests/test_compiler_lowering.py and scripts/probe_gather_pipeline.py"}
     out.update(lowering_kats(ref))
     out.update(probe_kats(ref))
