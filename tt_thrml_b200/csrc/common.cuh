@@ -277,6 +277,30 @@ __device__ __forceinline__ int categorical_icdf(const float (&theta)[QMAX], int 
   }
 }
 
+// The same inverse-CDF draw from unnormalised weights e_k (e_k = 0 for k >= q):
+// the count of boundaries u reaches, decided on head sums for u < 1/2 and on
+// tail sums against (1 - u) * S otherwise.  Returns -1 when the total S is not
+// a normal float32 number (the weights underflowed), so the caller can decide
+// from theta instead.
+template <int QMAX>
+__device__ __forceinline__ int categorical_icdf_weights(const float (&e)[QMAX], float u) {
+  const bool low = u < 0.5f;
+  float h[QMAX];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < QMAX; ++j) {
+    const float x = low ? e[j] : e[QMAX - 1 - j];
+    s = j == 0 ? x : __fadd_rn(s, x);
+    h[j] = s;
+  }
+  if (!(s >= 1.17549435e-38f)) return -1;
+  const float t = __fmul_rn(low ? u : 1.0f - u, s);
+  int cnt = 0;
+#pragma unroll
+  for (int j = 0; j < QMAX - 1; ++j) cnt += h[j] <= t ? 1 : 0;
+  return low ? cnt : QMAX - 1 - cnt;
+}
+
 // Heat-bath spin decision in Philox mode: +1 with probability sigmoid(2*gamma)
 // (thrml's SpinGibbsConditional; tt_thrml/compiler.py:321-324), written as
 // u * (1 + exp(-2 gamma)) < 1 so a single exponential decides it.

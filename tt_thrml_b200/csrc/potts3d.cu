@@ -42,6 +42,15 @@ constexpr int kRowFloats = TTHRML_POTTS_ROW_FLOATS;
 #ifndef TTHRML_POTTS_WPT
 #define TTHRML_POTTS_WPT 2  // chain words per thread when n_chains allows
 #endif
+#ifndef TTHRML_POTTS_EXP
+#define TTHRML_POTTS_EXP 1  // Philox mode, q = 8: the exponential-table kernel
+#endif
+#ifndef TTHRML_POTTS_EXP_MINB
+#define TTHRML_POTTS_EXP_MINB 2  // resident blocks per SM the exponential-table kernel is compiled for
+#endif
+#ifndef TTHRML_POTTS_V_UNROLL
+#define TTHRML_POTTS_V_UNROLL 4  // chains of a word unrolled in the exponential-table kernel
+#endif
 
 // QC: the category count as a compile-time constant (8, the common case: no
 // per-category predicates) or 0 (any q <= 8, read from the argument).
@@ -183,6 +192,219 @@ __global__ void __launch_bounds__(kPottsThreads) k_potts3d(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Philox-mode kernel on exponential tables.
+//
+// The inverse-CDF draw needs the unnormalised weights e^(theta_k) only up to
+// a common factor per site and chain, and
+//   e^(theta_k) = e^(b_k) * e^(Px_k) * e^(Py_k) * e^(Pz_k)
+// with P_a = J_a[k][s-] + J_a[k][s+] the pair sum of axis a.  Each CTA
+// tabulates E_a[s0][s1][k] = e^(P_a[s0][s1][k] - max_k P_a[s0][s1][.]) (every
+// row's largest entry is 1, so products cannot overflow), and a thread turns
+// its site's bias row into e^(b_k - max b) once for its 8 chains.  A chain's
+// weights are then three 8-wide products of table rows and no exponential at
+// all (the theta kernel above evaluates 8 per chain).  The weights are those
+// of the reference's theta up to float32 rounding (a few 1e-7 relative, i.e.
+// decisions move by ~1e-6 in logit units, inside the threshold band).  When
+// the normalised product underflows (couplings spanning more than ~80 in
+// theta), the chain falls back to theta from the matrices and the ex2 draw.
+//
+// Shared-memory layout: a row of 8 floats is two 16-byte chunks, each stored
+// 8 times, [axis][s0][s1][chunk][copy][4 floats]; lane l reads copy l % 8, and
+// a quarter-warp (the 8 lanes one 16-byte load serves at a time) then always
+// touches 8 different bank groups: the lookups are free of bank conflicts.
+// The fallback draw: theta of one chain from the matrices and the bias row (global memory), then the
+// inverse-CDF draw with exponentials (categorical_icdf).
+template <int WPT>
+__device__ __forceinline__ int potts_theta_draw(const uint32_t (&nw)[6][WPT], int ww, int v,
+                                                const float* __restrict__ J, const float* __restrict__ bias,
+                                                uint32_t r, int q, float u) {
+  float theta[kPottsQ];
+#pragma unroll
+  for (int k = 0; k < kPottsQ; ++k) {
+    float acc = k < q ? __ldg(bias + (size_t)r * kPottsQ + k) : 0.0f;
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      const uint32_t s0 = __byte_perm(nw[2 * a][ww], 0u, 0x4440u + v);
+      const uint32_t s1 = __byte_perm(nw[2 * a + 1][ww], 0u, 0x4440u + v);
+      const float j0 = (s0 < (uint32_t)q && k < q) ? __ldg(J + (a * q + k) * q + s0) : 0.0f;
+      const float j1 = (s1 < (uint32_t)q && k < q) ? __ldg(J + (a * q + k) * q + s1) : 0.0f;
+      acc = __fadd_rn(acc, __fadd_rn(j0, j1));
+    }
+    theta[k] = acc;
+  }
+  return categorical_icdf(theta, q, u);
+}
+
+constexpr int kPottsVUnroll = TTHRML_POTTS_V_UNROLL;
+#ifndef TTHRML_POTTS_EXP_COPIES
+#define TTHRML_POTTS_EXP_COPIES 8
+#endif
+constexpr int kExpCopies = TTHRML_POTTS_EXP_COPIES;
+// one table row: 2 chunks x copies x 4 floats; a single copy is padded to 3 chunks (rows 48 bytes apart)
+constexpr int kExpRowFloats = kExpCopies == 1 ? 12 : 2 * kExpCopies * 4;
+constexpr int kExpSmemBytes = 3 * kRows * kRows * kExpRowFloats * 4;
+
+template <int WPT>
+__global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3d_exp(
+    int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
+    int32_t colour, int64_t target_row0, int64_t source_row0, const float* __restrict__ J,
+    const float* __restrict__ bias, int32_t q, int64_t chain_offset, uint64_t seed, uint32_t sweep_base,
+    const tthrml_run_ctl* __restrict__ ctl) {
+  extern __shared__ __align__(16) float E[];  // [3][kRows][kRows][2][kExpCopies][4]
+  for (int row = threadIdx.x; row < 3 * kRows * kRows; row += blockDim.x) {
+    const int s1 = row % kRows, s0 = (row / kRows) % kRows, a = row / (kRows * kRows);
+    float p[kPottsQ];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kPottsQ; ++k) {
+      const float j0 = (s0 < q && k < q) ? J[((int64_t)a * q + k) * q + s0] : 0.0f;
+      const float j1 = (s1 < q && k < q) ? J[((int64_t)a * q + k) * q + s1] : 0.0f;
+      p[k] = __fadd_rn(j0, j1);
+      if (k < q) m = fmaxf(m, p[k]);
+    }
+    float e[kPottsQ];
+#pragma unroll
+    for (int k = 0; k < kPottsQ; ++k) e[k] = k < q ? expf(p[k] - m) : 0.0f;
+    float4* dst = reinterpret_cast<float4*>(E + (size_t)row * kExpRowFloats);
+#pragma unroll
+    for (int c = 0; c < kExpCopies; ++c) {
+      dst[c] = make_float4(e[0], e[1], e[2], e[3]);
+      dst[kExpCopies + c] = make_float4(e[4], e[5], e[6], e[7]);
+    }
+  }
+  __syncthreads();
+
+  const int copy = threadIdx.x & (kExpCopies - 1);
+  const uint32_t sweep = sweep_base + (ctl ? ctl->sweep : 0u);
+  const uint64_t sd = ctl ? ctl->seed : seed;
+  const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
+  const uint32_t words = div_words.d;
+  const int64_t half = (int64_t)X * Y * Z / 2;
+  const uint32_t items = (uint32_t)(half * words);
+  const uint32_t XY = (uint32_t)X * (uint32_t)Y;
+
+  for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+    const uint32_t r = fdiv(it, div_words);
+    const uint32_t w = (it - r * words) * WPT;
+    const uint32_t even = 2 * r;
+    const uint32_t yz = fdiv(even, div_x);
+    const int32_t z = (int32_t)fdiv(yz, div_y);
+    const int32_t y = (int32_t)yz - z * Y;
+    const int32_t x = (int32_t)(even - yz * (uint32_t)X) + ((y + z + colour) & 1);
+    const int32_t xm = x == 0 ? X - 1 : x - 1, xp = x == X - 1 ? 0 : x + 1;
+    const int32_t ym = y == 0 ? Y - 1 : y - 1, yp = y == Y - 1 ? 0 : y + 1;
+    const int32_t zm = z == 0 ? Z - 1 : z - 1, zp = z == Z - 1 ? 0 : z + 1;
+    const uint32_t zXY = (uint32_t)z * XY, yX = (uint32_t)y * (uint32_t)X;
+    uint32_t nb[6];
+    nb[0] = (zXY + yX + (uint32_t)xm) >> 1;
+    nb[1] = (zXY + yX + (uint32_t)xp) >> 1;
+    nb[2] = (zXY + (uint32_t)ym * (uint32_t)X + (uint32_t)x) >> 1;
+    nb[3] = (zXY + (uint32_t)yp * (uint32_t)X + (uint32_t)x) >> 1;
+    nb[4] = ((uint32_t)zm * XY + yX + (uint32_t)x) >> 1;
+    nb[5] = ((uint32_t)zp * XY + yX + (uint32_t)x) >> 1;
+    uint32_t nw[6][WPT];
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(state + (uint64_t)((uint32_t)source_row0 + nb[j]) *
+                                                                          (uint32_t)C) + w;
+      if (WPT == 2) {
+        const uint2 v2 = __ldg(reinterpret_cast<const uint2*>(src));
+        nw[j][0] = v2.x;
+        nw[j][WPT - 1] = v2.y;
+      } else {
+        nw[j][0] = __ldg(src);
+      }
+    }
+    // the site's bias row (16-byte loads; the host checks the alignment) as e^(b_k - max b)
+    float eb[kPottsQ];
+    {
+      float b[kPottsQ];
+      const float4* bp = reinterpret_cast<const float4*>(bias + (size_t)r * kPottsQ);
+      const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+      b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+      float mb = b[0];
+#pragma unroll
+      for (int k = 1; k < kPottsQ; ++k)
+        if (k < q) mb = fmaxf(mb, b[k]);
+      const float ml = mb * 1.44269502162933349609375f;
+#pragma unroll
+      for (int k = 0; k < kPottsQ; ++k) {
+        float v = 0.0f;
+        if (k < q) asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(__fmaf_rn(b[k], 1.44269502162933349609375f, -ml)));
+        eb[k] = v;
+      }
+    }
+
+    const int64_t row = target_row0 + r;
+    uint32_t out[WPT];
+#pragma unroll
+    for (int ww = 0; ww < WPT; ++ww) {
+      out[ww] = 0u;
+      const u32x4 rr =
+          philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w + ww), (uint32_t)row, sweep, kSaltCat}, keys);
+#pragma unroll kPottsVUnroll
+      for (int v = 0; v < 4; ++v) {
+        float e[kPottsQ];
+#pragma unroll
+        for (int k = 0; k < kPottsQ; ++k) e[k] = eb[k];
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+          const uint32_t s0 = min(__byte_perm(nw[2 * a][ww], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+          const uint32_t s1 = min(__byte_perm(nw[2 * a + 1][ww], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+          const float4* pp = reinterpret_cast<const float4*>(
+              E + (size_t)((a * kRows + (int)s0) * kRows + (int)s1) * kExpRowFloats) + copy;
+          const float4 p0 = pp[0], p1 = pp[kExpCopies];
+          e[0] = __fmul_rn(e[0], p0.x);
+          e[1] = __fmul_rn(e[1], p0.y);
+          e[2] = __fmul_rn(e[2], p0.z);
+          e[3] = __fmul_rn(e[3], p0.w);
+          e[4] = __fmul_rn(e[4], p1.x);
+          e[5] = __fmul_rn(e[5], p1.y);
+          e[6] = __fmul_rn(e[6], p1.z);
+          e[7] = __fmul_rn(e[7], p1.w);
+        }
+        const float u = uniform_open(word_of(rr, v));
+        int cat = categorical_icdf_weights<kPottsQ>(e, u);
+        if (cat < 0) cat = potts_theta_draw(nw, ww, v, J, bias, r, q, u);  // the weights underflowed
+        out[ww] |= (uint32_t)cat << (8 * v);
+      }
+    }
+    uint32_t* dst = reinterpret_cast<uint32_t*>(state + row * C) + w;
+    if (WPT == 2)
+      *reinterpret_cast<uint2*>(dst) = make_uint2(out[0], out[WPT - 1]);
+    else
+      *dst = out[0];
+  }
+}
+
+template <int WPT>
+int launch_potts_exp(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int32_t colour, int64_t target_row0,
+                     int64_t source_row0, const float* J, const float* bias, int32_t q, int64_t chain_offset,
+                     uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, cudaStream_t s) {
+  static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
+  if (!per_sm) {
+    int dev = 0, n = 0, b = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_potts3d_exp<WPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kExpSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_potts3d_exp<WPT>, kPottsThreads, kExpSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "k_potts3d_exp set-up");
+    sms = n;
+    per_sm = b > 0 ? b : 1;
+  }
+  const int64_t items = (int64_t)X * Y * Z / 2 * (C / (4 * WPT));
+  const int64_t need = (items + kPottsThreads - 1) / kPottsThreads;
+  const int64_t full = (int64_t)sms * per_sm;
+  const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
+  k_potts3d_exp<WPT><<<grid, kPottsThreads, kExpSmemBytes, s>>>(
+      state, C, X, Y, Z, make_fastdiv((uint32_t)(C / (4 * WPT))), make_fastdiv((uint32_t)X),
+      make_fastdiv((uint32_t)Y), colour, target_row0, source_row0, J, bias, q, chain_offset, seed, sweep, ctl);
+  return launch_status("k_potts3d_exp launch");
+}
+
 template <bool VARIATES, int QC, int WPT>
 int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int32_t colour, int64_t target_row0,
                  int64_t source_row0, const float* J, const float* bias, int32_t q, int64_t chain_offset,
@@ -253,6 +475,11 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
                                                                   variates_sweeps, seed, sweep, ctl, s)
   const bool q8 = q == kPottsQ && (uintptr_t)bias % 16 == 0;  // the q = 8 kernel reads 16-byte bias vectors
   const bool wide = TTHRML_POTTS_WIDE && n_chains % (4 * TTHRML_POTTS_WPT) == 0;  // several chain words per thread
+  if (!variates && q8 && TTHRML_POTTS_EXP) {
+    return (wide ? launch_potts_exp<TTHRML_POTTS_WPT> : launch_potts_exp<1>)(state, n_chains, X, Y, Z, colour,
+                                                                             target_row0, source_row0, J, bias, q,
+                                                                             chain_offset, seed, sweep, ctl, s);
+  }
   if (variates) {
     if (q8) TTHRML_POTTS_LAUNCH(true, kPottsQ);
     TTHRML_POTTS_LAUNCH(true, 0);
