@@ -143,7 +143,7 @@ struct DenseArgs {
 // Tile t of a persistent CTA -> (m block, n block): groups of kGroupM row
 // blocks are walked n-fastest, so the tiles in flight at one time share a few
 // A row panels and a band of B panels in L2.
-constexpr int kGroupM = 8;
+constexpr int kGroupM = 16;
 __device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int& mb, int& nb) {
   const int per_group = kGroupM * n_blocks;
   const int g = t / per_group, w = t - g * per_group;
