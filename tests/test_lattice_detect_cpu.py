@@ -38,3 +38,36 @@ def test_other_programs_are_not_lattices(kind):
 def test_small_non_lattice_cases_are_not_detected():
     assert detect_ising_lattice(lower_program(th.make_spin_case().program)) is None
     assert detect_ising_lattice(lower_program(th.make_mixed_case().program)) is None
+
+
+def _sym(q, seed):
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal((3, q, q)).astype(np.float32)
+    return ((A + A.transpose(0, 2, 1)) * np.float32(0.5)).astype(np.float32)
+
+
+@pytest.mark.parametrize("dims,q", [((4, 4, 4), 8), ((6, 4, 8), 3), ((4, 6, 4), 5)])
+def test_potts_grid_is_detected(dims, q):
+    from tt_thrml_b200.compiler import detect_potts_lattice
+    from tt_thrml_b200 import workloads
+
+    J = _sym(q, 1)
+    bias = np.random.default_rng(2).standard_normal((int(np.prod(dims)), q)).astype(np.float32)
+    prog, _ = th.potts_grid_program(dims, J, bias)
+    st = detect_potts_lattice(lower_program(prog))
+    assert st is not None and st["dims"] == dims and st["q"] == q
+    np.testing.assert_array_equal(st["J"], J)
+    native = workloads.PottsLattice3D(dims, J, bias).tt_stencil()
+    for c in range(2):
+        np.testing.assert_array_equal(st["bias"][c], native["bias"][c])
+
+
+def test_potts_grid_with_asymmetric_or_varying_couplings_is_not_detected():
+    from tt_thrml_b200.compiler import detect_potts_lattice
+
+    q = 3
+    J = _sym(q, 3)
+    J[1, 0, 2] += 0.5  # axis-y matrix no longer symmetric: the two directions differ
+    prog, _ = th.potts_grid_program((4, 4, 4), J, np.zeros((64, q), np.float32))
+    assert detect_potts_lattice(lower_program(prog)) is None
+    assert detect_potts_lattice(lower_program(th.make_categorical_case().program)) is None

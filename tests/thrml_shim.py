@@ -415,3 +415,28 @@ def ising_grid_program(height: int, width: int, *, J: float = 1.0, h: float = 0.
     else:  # rows split in halves: not a checkerboard
         free = [Block(nodes[: len(nodes) // 2]), Block(nodes[len(nodes) // 2 :])]
     return IsingSamplingProgram(model, free, []), nodes
+
+
+def potts_grid_program(dims, J, bias):
+    """A q-state Potts model over a periodic X x Y x Z grid written with thrml factors: one
+    CategoricalEBMFactor per axis over the (site, site + unit step) edges with that axis's q x q matrix,
+    one for the site biases; free blocks = the two checkerboard colours with sites in row-major order."""
+    X, Y, Z = (int(d) for d in dims)
+    J = np.asarray(J, np.float32)
+    q = J.shape[-1]
+    nodes = [CategoricalNode() for _ in range(X * Y * Z)]
+    idx = lambda x, y, z: ((z % Z) * Y + (y % Y)) * X + (x % X)  # noqa: E731
+    factors = [CategoricalEBMFactor([Block(nodes)], np.asarray(bias, np.float32).reshape(len(nodes), q))]
+    for a, (dx, dy, dz) in enumerate(((1, 0, 0), (0, 1, 0), (0, 0, 1))):
+        us, vs = [], []
+        for z in range(Z):
+            for y in range(Y):
+                for x in range(X):
+                    us.append(nodes[idx(x, y, z)])
+                    vs.append(nodes[idx(x + dx, y + dy, z + dz)])
+        factors.append(CategoricalEBMFactor([Block(us), Block(vs)], np.broadcast_to(J[a], (len(us), q, q)).copy()))
+    colour = [((i % X) + (i // X) % Y + i // (X * Y)) % 2 for i in range(len(nodes))]
+    free = [Block([nd for nd, c in zip(nodes, colour) if c == k]) for k in range(2)]
+    spec = BlockGibbsSpec(free, [], {CategoricalNode: sd(np.uint8)})
+    sampler = CategoricalGibbsConditional(q)
+    return FactorSamplingProgram(spec, [sampler, sampler], factors, []), nodes

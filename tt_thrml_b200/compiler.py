@@ -1072,6 +1072,100 @@ def detect_ising_lattice(lowered) -> dict | None:
             "site_bias": np.float32(biases[0][0]), "block_rows": (0, half)}
 
 
+def _potts_geometry(dims, half: int):
+    """Per colour c: (n/2, 6) flat rows of the neighbours (x-, x+, y-, y+, z-, z+) of block c's sites."""
+    X, Y, Z = dims
+    out = []
+    for c in range(2):
+        even = 2 * np.arange(half, dtype=np.int64)
+        yy = (even // X) % Y
+        zz = even // (X * Y)
+        L = even + ((yy + zz + c) & 1)
+        x, y, z = L % X, (L // X) % Y, L // (X * Y)
+        nb = [(((z + dz) % Z) * Y + (y + dy) % Y) * X + (x + dx) % X
+              for dx, dy, dz in ((-1, 0, 0), (1, 0, 0), (0, -1, 0), (0, 1, 0), (0, 0, -1), (0, 0, 1))]
+        out.append((1 - c) * half + np.stack(nb, axis=1) // 2)
+    return out
+
+
+def detect_potts_lattice(lowered) -> dict | None:
+    """The stencil description of a lowered program that is a periodic 3-D Potts lattice, else None.
+
+    The counterpart of `detect_ising_lattice` for categorical programs (e.g. CategoricalEBMFactors over
+    the x, y and z edges of a periodic grid): two free categorical blocks of n/2 nodes with q <= 8, block
+    c the colour-c sites (x + y + z = c mod 2) in row-major order, one sampling group each; per node a
+    bias q-vector (any values) and exactly six pair terms with one categorical source each, whose
+    sources are its six lattice neighbours and whose q x q matrices are one matrix per axis, the same for
+    both directions and for every node."""
+    specs = lowered.specs
+    if lowered.n_free_blocks != 2 or len(specs) != 2 or any(s.family != Family.CATEGORICAL for s in specs):
+        return None
+    q = int(specs[0].n_categories or 2)
+    half = specs[0].n_nodes
+    if int(specs[1].n_categories or 2) != q or not 1 <= q <= POTTS_MAX_Q or specs[1].n_nodes != half:
+        return None
+    if specs[0].block_global_start != 0 or specs[1].block_global_start != half:
+        return None
+    if sorted(tuple(int(i) for i in g) for g in lowered.sampling_order) != [(0,), (1,)]:
+        return None
+    n = 2 * half
+    biases, srcs, mats = [], [], []
+    for s in specs:
+        bias = np.zeros((half, q), dtype=np.float32)
+        parts = []
+        for it in s.interactions:
+            rp, w, src = it.ragged(s.n_nodes)
+            if src.shape[0] == 0 and it.n_categorical == 0 and w.shape[1] == q:
+                for t in range(int(np.diff(rp).max()) if half else 0):
+                    has = np.diff(rp) > t
+                    bias[has] = (bias[has] + w[rp[:-1][has] + t]).astype(np.float32)
+            elif src.shape[0] == 1 and it.n_categorical == 1 and w.shape[1] == q * q:
+                parts.append((rp, w, src[0]))
+            else:
+                return None
+        if not parts:
+            return None
+        counts = sum(np.diff(rp) for rp, _, _ in parts)
+        rows = np.concatenate([np.repeat(np.arange(half), np.diff(rp)) for rp, _, _ in parts])
+        ws = np.concatenate([w for _, w, _ in parts])
+        cs = np.concatenate([c for _, _, c in parts]).astype(np.int64)
+        live = np.any(ws != 0.0, axis=1)
+        if not (np.bincount(rows[live], minlength=half) == 6).all():
+            return None
+        order = np.argsort(rows[live], kind="stable")
+        biases.append(bias)
+        srcs.append(cs[live][order].reshape(half, 6))
+        mats.append(ws[live][order].reshape(half, 6, q, q))
+    # dims from site (0, 0, 0) = block-0 row 0: its neighbour rows in block 1 hold X/2 - 1 and X/2
+    r0 = set((srcs[0][0] - half).tolist())
+    for X in sorted(2 * (r + 1) for r in r0 if r + 1 in r0):
+        for r in sorted(r0):
+            if r <= 0 or X < 4 or 2 * r % X or n % (2 * r) or 2 * r // X < 4:
+                continue
+            Y = 2 * r // X
+            if n % (X * Y) or (n // (X * Y)) < 4 or (n // (X * Y)) % 2 or Y % 2:
+                continue
+            dims = (X, Y, n // (X * Y))
+            geo = _potts_geometry(dims, half)
+            if not all(np.array_equal(np.sort(geo[c], 1), np.sort(srcs[c], 1)) for c in range(2)):
+                continue
+            J = np.zeros((3, q, q), dtype=np.float32)
+            for c in range(2):
+                # which lattice direction each term points to
+                d = np.argmax(srcs[c][:, :, None] == geo[c][:, None, :], axis=2)  # [half][term] -> direction
+                for a in range(3):
+                    for sgn in range(2):
+                        sel = mats[c][d == 2 * a + sgn]
+                        if not (sel == sel[0]).all():
+                            return None
+                        if c == 0 and sgn == 0:
+                            J[a] = sel[0]
+                        elif not np.array_equal(sel[0], J[a]):
+                            return None
+            return {"kind": "potts3d", "dims": dims, "q": q, "J": J, "bias": biases, "block_rows": (0, half)}
+    return None
+
+
 class _DetectedStencil:
     """A lowered program recognised as a lattice, seen through the stencil planner's interface."""
 
@@ -1276,7 +1370,7 @@ def _build_plans(program, config: CUDAConfig, n_chains: int, tdev, force_generic
     else:
         lowered = pre_lowered if pre_lowered is not None else lower_program(program)
         if not force_generic and config.stencil:
-            st = detect_ising_lattice(lowered)
+            st = detect_ising_lattice(lowered) or detect_potts_lattice(lowered)
             view = _DetectedStencil(lowered, st) if st is not None else None
             if view is not None and stencil_eligible(view, n_chains, config.rng_mode):
                 plans = _plan_stencil(view, tdev, n_chains)
@@ -1335,5 +1429,6 @@ __all__ = [
     "IsingResidentGroupPlan",
     "detect_dense_couplings",
     "detect_ising_lattice",
+    "detect_potts_lattice",
     "ising_pattern_tables",
 ]
