@@ -428,6 +428,29 @@ int tthrml_dense_field_sample(const void* source_state, const void* weights_nk, 
                               void* stream);
 
 /*
+ * tthrml_dense_field_sample with the spin decisions settled from the exact
+ * field (the same group call, tt_thrml/compiler.py:173-176, 303-365).  The
+ * tensor cores' float32 sum of a K-term field can be off by ~1e-5 at K =
+ * 4096; a spin decided within 1e-5 of its threshold (u * (1 + e^(-2 field))
+ * against 1, or 2 field - logit in variates mode) is recorded in `ties` and
+ * decided again by a second kernel on the same stream from bias[n] +
+ * sum_k source_state[m][k] * weights_nk[n][k] summed in double, with the
+ * same Philox word or uploaded logit.  ties: uint32 [4 + 2 * ties_capacity],
+ * 16-byte aligned, zero before its first use and owned by one stream; words
+ * 0-1 are zero again after each call, word 2 counts the near decisions that
+ * did not fit (they keep their float32 decision), then (chain, unit) pairs.
+ * 1 <= ties_capacity < 2^31.  Gaussian blocks ignore the list.  Other
+ * arguments and requirements as tthrml_dense_field_sample.
+ */
+int tthrml_dense_field_sample_ties(const void* source_state, const void* weights_nk, int64_t n_chains,
+                                   int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
+                                   float precision, void* out_state, float* out_state_f32, int32_t out_pieces,
+                                   int64_t row0, int64_t chain_offset, const float* variates,
+                                   int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                                   const tthrml_run_ctl* ctl, int32_t* error, uint32_t* ties,
+                                   int64_t ties_capacity, void* stream);
+
+/*
  * Adds `delta` to ctl->sweep on `stream` (the last node of a captured
  * multi-sweep CUDA graph, so each replay continues the run).
  */

@@ -121,7 +121,10 @@ def compare_group(report: ParityReport, ex: Executor, o: orc.OracleSampler, gi: 
         tie = np.abs(m) < BAND
         report.band += int(tie.sum())
         diff = gg != oo
-        report.hard_mismatches += int((diff & ~tie).sum())
+        hard = diff & ~tie
+        report.hard_mismatches += int(hard.sum())
+        if hard.any():  # the decision margins (oracle, logit units) of the sites that disagree
+            report.notes.append(("hard mismatch margins", sorted(float(x) for x in np.abs(m[hard]))[:8]))
     if follow_gpu:
         o.state[...] = g
     elif not np.array_equal(g, o.state):

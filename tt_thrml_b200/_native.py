@@ -108,6 +108,11 @@ _SIGNATURES = {
         [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, ctypes.c_float, c_vp, c_vp, c_i32, c_i64, c_i64, c_vp,
          c_i64, c_u64, c_u32, c_vp, c_vp, c_vp],
     ),
+    "tthrml_dense_field_sample_ties": (
+        c_i32,
+        [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, ctypes.c_float, c_vp, c_vp, c_i32, c_i64, c_i64, c_vp,
+         c_i64, c_u64, c_u32, c_vp, c_vp, c_vp, c_i64, c_vp],
+    ),
     "tthrml_potts3d_step": (
         c_i32,
         [c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i64, c_vp, c_i64, c_u64, c_u32,

@@ -138,7 +138,49 @@ struct DenseArgs {
   float precision;         // gaussian: sum of precision contributions (1 for unit variance)
   const tthrml_run_ctl* ctl;
   int* error;              // device word, set on a wait timeout
+  uint32_t* ties;          // near-threshold spin decisions: [count, blocks done, dropped, 0, (m, n) x ties_cap]
+  int64_t ties_cap;        // or NULL: decisions from the float32 field alone
 };
+
+// A spin decision whose float32 margin is this close to the threshold (in units of u * (1 + e^(-2 gamma))
+// around 1, or of 2 gamma - logit in variates mode; |t - 1| ~ (1 - u) |2 gamma - logit u|) is decided
+// again from the exact field.  The tensor cores' float32 accumulation of a K-term field can be off by
+// ~1e-5 at K = 4096 with terms of size 0.01; a decision the float32 field gets wrong at a true margin
+// beyond the 1e-5 band therefore shows a float32 margin below (error - 1e-5), which this bound catches
+// for errors up to 2e-5.  The exact field is bias + sum_k A[m][k] B[n][k] in double (bf16 products are
+// exact there).  The epilogue only records such decisions (a few in 10^5); k_dense_settle, launched
+// next on the same stream, decides them again and overwrites their outputs.
+constexpr float kNearTie = 1e-5f;
+#ifndef TTHRML_DENSE_SETTLE
+#define TTHRML_DENSE_SETTLE 2  // 0: no near-threshold check, 1: check only, 2: check and record
+#endif
+constexpr int kTieHeaderWords = 4;  // count, blocks of k_dense_settle done, entries dropped (cumulative), 0
+
+// Appends the (chain m, unit n_first + j) of every bit j of each lane's `near` to the tie list: one
+// atomic per warp, then each lane's entries at its prefix offset.  Entries past the capacity are
+// dropped (their float32 decisions stand) and counted by k_dense_settle.  All 32 lanes call it.
+__device__ __forceinline__ void record_ties(uint32_t* ties, int64_t cap, uint32_t near, int64_t m,
+                                            int64_t n_first) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t cnt = (uint32_t)__popc(near);
+  uint32_t incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  uint32_t base = 0u;
+  if (lane == 31) base = atomicAdd(ties, incl);
+  base = __shfl_sync(0xffffffffu, base, 31);
+  uint32_t idx = base + incl - cnt;
+  uint2* entries = reinterpret_cast<uint2*>(ties + kTieHeaderWords);
+  while (near) {
+    const int j = __ffs(near) - 1;
+    near &= near - 1u;
+    if ((int64_t)idx < cap) entries[idx] = make_uint2((uint32_t)m, (uint32_t)(n_first + j));
+    ++idx;
+  }
+}
 
 // Tile t of a persistent CTA -> (m block, n block): groups of kGroupM row
 // blocks are walked n-fastest, so the tiles in flight at one time share a few
@@ -160,6 +202,7 @@ __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc
   const int64_t gchain = a.chain_offset + m;
   float outf[32];
   u32x4 r{0u, 0u, 0u, 0u};
+  uint32_t near = 0u;  // bit j: the spin of column n_first + j was decided within kNearTie of its threshold
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const int64_t n = n_first + j;
@@ -169,11 +212,15 @@ __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc
     if (FAMILY == TTHRML_SPIN) {
       bool up;
       if (VARIATES) {
-        up = __fmul_rn(2.0f, field) > __ldg(a.variates + (vs * a.N + n) * a.M + m);
+        const float d = __fsub_rn(__fmul_rn(2.0f, field), __ldg(a.variates + (vs * a.N + n) * a.M + m));
+        up = d > 0.0f;
+        if (TTHRML_DENSE_SETTLE) near |= (fabsf(d) < kNearTie ? 1u : 0u) << j;
       } else {
         if (j == 0 || (row & 3) == 0)
           r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseSpin}, k0, k1);
-        up = spin_up_philox(field, word_of(r, (int)(row & 3)));
+        const float t = uniform_open(word_of(r, (int)(row & 3))) * (1.0f + __expf(-2.0f * field));
+        up = t < 1.0f;
+        if (TTHRML_DENSE_SETTLE) near |= (fabsf(t - 1.0f) < kNearTie ? 1u : 0u) << j;
       }
       v = up ? 1.0f : -1.0f;
     } else {
@@ -190,6 +237,9 @@ __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc
     }
     outf[j] = v;
   }
+  if (FAMILY == TTHRML_SPIN && TTHRML_DENSE_SETTLE == 2 && a.ties != nullptr &&
+      __any_sync(0xffffffffu, near != 0u))  // rare: k_dense_settle decides these again from the exact field
+    record_ties(a.ties, a.ties_cap, near, m, n_first);
   if (a.out_f32) {
     float4* df = reinterpret_cast<float4*>(a.out_f32 + m * a.N + n_first);
 #pragma unroll
@@ -369,6 +419,239 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair kernel (tcgen05 cta_group::2), for chain counts that are multiples
+// of 256.  A cluster of two CTAs on two SMs computes 256 x 256 output tiles:
+// CTA r holds rows 128r..128r+127 of the tile's A slice and units
+// 128r..128r+127 of its B slice in its own shared memory, so a stage is 32 KiB
+// per CTA (half the B bytes of the single-CTA kernel) and 6 stages fit.  The
+// even CTA (the leader) issues every MMA (M = 256, N = 256, K = 16) over both
+// CTAs' operands; the accumulator rows of CTA r land in CTA r's TMEM, which
+// its own 8 epilogue warps drain exactly as in the single-CTA kernel.
+// Synchronisation (the protocol of the sm100 2-SM pipelines):
+//   full[s]   (leader only)  the leader's producer arrives with the stage's
+//             bytes of both CTAs; both CTAs' TMA loads complete on it (their
+//             mbarrier address with the CTA-rank bit cleared);
+//   empty[s]  (each CTA)     the leader's tcgen05.commit multicasts to both;
+//   acc_full  (each CTA)     likewise, once a tile's MMAs are done;
+//   acc_empty (leader only)  every epilogue warp of both CTAs arrives (16).
+// TMEM is allocated and freed pairwise (cta_group::2 by warp 1 of each CTA);
+// a cluster barrier after barrier set-up and another before the free keep
+// either CTA from signalling the other's uninitialised or exited memory.
+// Every mbarrier wait is bounded as in the single-CTA kernel.
+// ---------------------------------------------------------------------------
+#ifndef TTHRML_DENSE_2SM
+#define TTHRML_DENSE_2SM 1
+#endif
+constexpr int BM2 = 128, BN2H = 128, STAGES2 = 6;
+constexpr int A2_BYTES = BM2 * BK * 2;   // 16 KiB
+constexpr int B2_BYTES = BN2H * BK * 2;  // 16 KiB
+constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int SMEM2_BYTES = 1024 + STAGES2 * STAGE2_BYTES + 256;
+constexpr uint32_t kPeerMask = 0xFEFFFFFFu;  // clears the CTA-rank bit of a shared::cluster address
+// Instruction descriptor of the pair MMA: D fp32, A and B bf16, K-major, N = 256, M = 256.
+constexpr uint32_t kIdesc2 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t n_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_leader, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_leader), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(kIdesc2), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u));
+}
+// arrives (once all earlier MMAs of this thread are done) on the barrier at this offset in both CTAs
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(smem_u32(bar) & kPeerMask) : "memory");
+}
+
+template <int FAMILY, bool VARIATES>
+__global__ void __launch_bounds__(kDenseThreads, 1)
+    k_dense_field_sample_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                              DenseArgs args) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* tiles = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint64_t* empty = full + STAGES2;
+  uint64_t* acc_full = empty + STAGES2;  // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int num_k = (int)(args.K / BK);
+  const int m_blocks = (int)(args.M / (2 * BM2)), n_blocks = (int)(args.N / BN);
+  const int n_tiles = m_blocks * n_blocks;
+  const int first = (int)cluster_id_x(), step = (int)n_clusters_x();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);  // every epilogue warp of both CTAs
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(2 * kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  int last_it[2] = {-1, -1};
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer (both CTAs): this CTA's halves of the A and B slices
+      int64_t issued = 0;
+      bool failed = false;
+      for (int t = first; t < n_tiles && !failed; t += step) {
+        int mb, nb;
+        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        for (int kb = 0; kb < num_k; ++kb) {
+          const int s = (int)(issued % STAGES2);
+          const uint32_t round = (uint32_t)(issued / STAGES2);
+          if (!mbar_wait(&empty[s], (round & 1u) ^ 1u)) {
+            atomicExch(args.error, kErrEmptyWait);
+            failed = true;
+            break;
+          }
+          if (leader) mbar_expect_tx(&full[s], 2 * STAGE2_BYTES);  // the stage's bytes of both CTAs
+          unsigned char* a = tiles + s * STAGE2_BYTES;
+          const int kc = (num_k - 1 - kb) * BK;  // K blocks last to first (see the single-CTA kernel)
+          const uint32_t bar = smem_u32(&full[s]) & kPeerMask;
+          tma_load_2d_pair(a, &map_a, bar, kc, mb * 2 * BM2 + (int)rank * BM2);
+          tma_load_2d_pair(a + A2_BYTES, &map_b, bar, kc, nb * BN + (int)rank * BN2H);
+          ++issued;
+        }
+      }
+      // every stage this CTA filled has been consumed (released by the leader's MMAs) before exit
+      for (int64_t j = issued > STAGES2 ? issued - STAGES2 : 0; j < issued; ++j)
+        if (!mbar_wait(&empty[j % STAGES2], (uint32_t)(j / STAGES2) & 1u)) atomicExch(args.error, kErrEmptyWait);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // MMA issue: the leader only
+      int64_t consumed = 0;
+      int it = 0;
+      bool failed = false;
+      for (int t = first; t < n_tiles && !failed; t += step, ++it) {
+        const int b = it & 1;
+        const uint32_t use = (uint32_t)(it >> 1);
+        if (!mbar_wait(&acc_empty[b], (use & 1u) ^ 1u)) {
+          atomicExch(args.error, kErrAccWait);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * kTmemCols);
+        for (int kb = 0; kb < num_k; ++kb) {
+          const int s = (int)(consumed % STAGES2);
+          if (!mbar_wait(&full[s], (uint32_t)(consumed / STAGES2) & 1u)) {
+            atomicExch(args.error, kErrFullWait);
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          const unsigned char* a = tiles + s * STAGE2_BYTES;
+          const uint64_t ad = umma_desc_sw128(a), bd = umma_desc_sw128(a + A2_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16_pair(d, ad + 2ull * kk, bd + 2ull * kk, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(&empty[s]);  // the stage is free again in both CTAs
+          ++consumed;
+        }
+        umma_commit_pair(&acc_full[b]);  // both CTAs' accumulator halves complete
+        last_it[b] = it;
+      }
+    }
+  } else {
+    // epilogue (both CTAs): this CTA's 128 rows of the tile, as in the single-CTA kernel
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    int it = 0;
+    for (int t = first; t < n_tiles; t += step, ++it) {
+      int mb, nb;
+      tile_coords(t, m_blocks, n_blocks, mb, nb);
+      const int b = it & 1;
+      if (!mbar_wait(&acc_full[b], (uint32_t)(it >> 1) & 1u)) {
+        atomicExch(args.error, kErrAccWait);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sweep = args.sweep + (args.ctl ? args.ctl->sweep : 0u);
+      const uint64_t sd = args.ctl ? args.ctl->seed : args.seed;
+      const float inv = 1.0f / __fadd_rn(args.precision, 1e-6f);
+      const float sd_g = sqrtf(inv);
+      const int64_t vs =
+          args.variates ? (int64_t)(sweep % (uint32_t)(args.variates_sweeps > 0 ? args.variates_sweeps : 1)) : 0;
+      const int64_t m = (int64_t)mb * 2 * BM2 + (int64_t)rank * BM2 + quad * 32 + lane;
+      for (int c = half; c < BN / 32; c += 2) {
+        float acc[32];
+        tmem_load32(tmem + (uint32_t)(b * kTmemCols) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32), acc);
+        draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, seed_lo(sd), seed_hi(sd), inv,
+                                     sd_g, vs);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&acc_empty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1 && leader) {
+    // every MMA the pair issued has completed (in both CTAs' TMEM) before TMEM is freed
+    if (lane == 0) {
+      for (int b = 0; b < 2; ++b)
+        if (last_it[b] >= 0) (void)mbar_wait(&acc_full[b], (uint32_t)(last_it[b] >> 1) & 1u);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA frees TMEM or exits while the other may still signal it
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTmemCols));
+}
+
 // --- host side --------------------------------------------------------------
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -413,19 +696,182 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, uin
   return TTHRML_OK;
 }
 
+// Launches the CTA-pair kernel: clusters of 2 CTAs, as many as can be resident at once (persistent).
+// ---------------------------------------------------------------------------
+// Near-threshold settling.  One warp per recorded (chain m, unit n): the exact
+// field bias[n] + sum_k A[m][k] B[n][k] in double (a bf16 product is exact in
+// double; 8 terms per lane per step from 16-byte loads, rows 128-byte aligned
+// because K % 64 == 0), the same variate as the epilogue (Philox word or
+// uploaded logit) in double, and the decision written over the epilogue's:
+// +-1 in piece 0, 0 in the remainder pieces, +-1 in the float32 copy.  The
+// last block to finish clears the count, so the list is empty for the next
+// launch on the stream (CUDA graph replays included).
+// ---------------------------------------------------------------------------
+struct SettleArgs {
+  const __nv_bfloat16* a_mat;  // [M][K] source state
+  const __nv_bfloat16* b_mat;  // [N][K] weights
+  const float* bias;
+  const float* variates;
+  int64_t variates_sweeps;
+  __nv_bfloat16* out;
+  float* out_f32;
+  int32_t pieces;
+  int64_t M, N, K, row0, chain_offset;
+  uint64_t seed;
+  uint32_t sweep;
+  const tthrml_run_ctl* ctl;
+  uint32_t* ties;
+  int64_t cap;
+};
+
+constexpr int kSettleThreads = 256;
+
+template <bool VARIATES>
+__global__ void __launch_bounds__(kSettleThreads) k_dense_settle(SettleArgs a) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t count = *reinterpret_cast<volatile const uint32_t*>(a.ties);
+  const int64_t n_entries = (int64_t)count < a.cap ? (int64_t)count : a.cap;
+  const uint32_t sweep = a.sweep + (a.ctl ? a.ctl->sweep : 0u);
+  const uint64_t sd = a.ctl ? a.ctl->seed : a.seed;
+  const int64_t vs =
+      a.variates ? (int64_t)(sweep % (uint32_t)(a.variates_sweeps > 0 ? a.variates_sweeps : 1)) : 0;
+  const uint2* entries = reinterpret_cast<const uint2*>(a.ties + kTieHeaderWords);
+  const int64_t warps = (int64_t)gridDim.x * (kSettleThreads / 32);
+  for (int64_t i = (int64_t)blockIdx.x * (kSettleThreads / 32) + (threadIdx.x >> 5); i < n_entries; i += warps) {
+    const uint2 e = entries[i];
+    const int64_t m = e.x, n = e.y;
+    if (m >= a.M || n >= a.N) continue;  // never recorded so; keeps every access below in bounds
+    const __nv_bfloat16* ar = a.a_mat + m * a.K;
+    const __nv_bfloat16* br = a.b_mat + n * a.K;
+    double acc = 0.0;
+#pragma unroll 4
+    for (int64_t k = 8 * lane; k < a.K; k += 256) {
+      const uint4 av = __ldg(reinterpret_cast<const uint4*>(ar + k));
+      const uint4 bv = __ldg(reinterpret_cast<const uint4*>(br + k));
+      const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc += (double)__uint_as_float(aw[q] << 16) * (double)__uint_as_float(bw[q] << 16);
+        acc += (double)__uint_as_float(aw[q] & 0xFFFF0000u) * (double)__uint_as_float(bw[q] & 0xFFFF0000u);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      const double field = acc + (a.bias ? (double)__ldg(a.bias + n) : 0.0);
+      double l;
+      if (VARIATES) {
+        l = (double)__ldg(a.variates + (vs * a.N + n) * a.M + m);
+      } else {
+        const int64_t row = a.row0 + n;
+        const u32x4 r = philox4x32_10(u32x4{(uint32_t)(a.chain_offset + m), (uint32_t)(row >> 2), sweep,
+                                            kSaltDenseSpin},
+                                      seed_lo(sd), seed_hi(sd));
+        const double u = (double)uniform_open(word_of(r, (int)(row & 3)));
+        l = log(u) - log1p(-u);
+      }
+      const float v = 2.0 * field > l ? 1.0f : -1.0f;
+      __nv_bfloat16* o = a.out + m * (a.N * a.pieces) + n;
+      o[0] = __float2bfloat16_rn(v);
+      for (int p = 1; p < a.pieces; ++p) o[p * a.N] = __float2bfloat16_rn(0.0f);
+      if (a.out_f32) a.out_f32[m * a.N + n] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0 && (int64_t)count > a.cap) atomicAdd(a.ties + 2, count - (uint32_t)a.cap);
+    __threadfence();
+    if (atomicAdd(a.ties + 1, 1u) == gridDim.x - 1) {  // every block has read the count
+      a.ties[0] = 0u;
+      a.ties[1] = 0u;
+    }
+  }
+}
+
+int launch_settle(const DenseArgs& d, const void* a_mat, const void* b_mat, int sms, cudaStream_t st) {
+  SettleArgs s;
+  s.a_mat = reinterpret_cast<const __nv_bfloat16*>(a_mat);
+  s.b_mat = reinterpret_cast<const __nv_bfloat16*>(b_mat);
+  s.bias = d.bias;
+  s.variates = d.variates;
+  s.variates_sweeps = d.variates_sweeps;
+  s.out = d.out;
+  s.out_f32 = d.out_f32;
+  s.pieces = d.pieces;
+  s.M = d.M;
+  s.N = d.N;
+  s.K = d.K;
+  s.row0 = d.row0;
+  s.chain_offset = d.chain_offset;
+  s.seed = d.seed;
+  s.sweep = d.sweep;
+  s.ctl = d.ctl;
+  s.ties = d.ties;
+  s.cap = d.ties_cap;
+  const int64_t per_block = kSettleThreads / 32;
+  const int64_t want = (d.ties_cap + per_block - 1) / per_block;
+  const int grid = (int)(want < 2 * sms ? want : 2 * sms);
+  if (d.variates)
+    k_dense_settle<true><<<grid, kSettleThreads, 0, st>>>(s);
+  else
+    k_dense_settle<false><<<grid, kSettleThreads, 0, st>>>(s);
+  return launch_status("k_dense_settle launch");
+}
+
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const DenseArgs& a, int32_t family, bool variates,
+                cudaStream_t st) {
+  const void* fn = family == TTHRML_SPIN
+                       ? (variates ? (const void*)k_dense_field_sample_pair<TTHRML_SPIN, true>
+                                   : (const void*)k_dense_field_sample_pair<TTHRML_SPIN, false>)
+                       : (variates ? (const void*)k_dense_field_sample_pair<TTHRML_GAUSSIAN, true>
+                                   : (const void*)k_dense_field_sample_pair<TTHRML_GAUSSIAN, false>);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kDenseThreads, 1, 1);
+  cfg.dynamicSmemBytes = SMEM2_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int64_t n_tiles = (a.M / (2 * BM2)) * (a.N / BN);
+  int clusters = 0;
+  cfg.gridDim = dim3(2, 1, 1);
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg);
+  if (e != cudaSuccess) return cuda_status(e, "k_dense_field_sample_pair: cudaOccupancyMaxActiveClusters");
+  if (clusters < 1) {
+    set_error("k_dense_field_sample_pair: no CTA pair fits on this device");
+    return TTHRML_ERR_UNSUPPORTED;
+  }
+  const int64_t want = n_tiles < clusters ? n_tiles : clusters;
+  cfg.gridDim = dim3((unsigned)(2 * want), 1, 1);
+  void* params[3] = {(void*)&ma, (void*)&mb, (void*)&a};
+  e = cudaLaunchKernelExC(&cfg, fn, params);
+  if (e != cudaSuccess) return cuda_status(e, "k_dense_field_sample_pair launch");
+  return launch_status("k_dense_field_sample_pair launch");
+}
+
 }  // namespace
 }  // namespace tthrml
 
-extern "C" int tthrml_dense_field_sample(const void* source_state, const void* weights_nk, int64_t n_chains,
-                                         int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
-                                         float precision, void* out_state, float* out_state_f32,
-                                         int32_t out_pieces, int64_t row0,
-                                         int64_t chain_offset, const float* variates, int64_t variates_sweeps,
-                                         uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int32_t* error,
-                                         void* stream) {
+namespace {
+
+int dense_field_sample(const void* source_state, const void* weights_nk, int64_t n_chains, int64_t n_units,
+                       int64_t n_sources, const float* bias, int32_t family, float precision, void* out_state,
+                       float* out_state_f32, int32_t out_pieces, int64_t row0, int64_t chain_offset,
+                       const float* variates, int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                       const tthrml_run_ctl* ctl, int32_t* error, uint32_t* ties, int64_t ties_capacity,
+                       void* stream) {
   using namespace tthrml;
   if (!source_state || !weights_nk || !out_state || !error) {
     set_error("tthrml_dense_field_sample: NULL argument");
+    return TTHRML_ERR_ARG;
+  }
+  if (ties && (ties_capacity < 1 || ties_capacity > 0x7fffffff || ((uintptr_t)ties % 16))) {
+    set_error("tthrml_dense_field_sample_ties: ties must be 16-byte aligned with 1 <= capacity < 2^31 (got %lld)",
+              (long long)ties_capacity);
     return TTHRML_ERR_ARG;
   }
   if (n_chains <= 0 || n_units <= 0 || n_sources <= 0 || n_chains % BM || n_units % BN || n_sources % BK) {
@@ -450,10 +896,11 @@ extern "C" int tthrml_dense_field_sample(const void* source_state, const void* w
     set_error("tthrml_dense_field_sample: buffers must be 16-byte aligned and chain_offset a multiple of 4");
     return TTHRML_ERR_ARG;
   }
+  const bool pair = TTHRML_DENSE_2SM && n_chains % (2 * BM2) == 0;  // CTA-pair kernel: 256-row tiles
   CUtensorMap ma, mb;
   int rc = make_map(&ma, source_state, n_chains, n_sources, BM);
   if (rc) return rc;
-  rc = make_map(&mb, weights_nk, n_units, n_sources, BN);
+  rc = make_map(&mb, weights_nk, n_units, n_sources, pair ? BN2H : BN);
   if (rc) return rc;
   {  // the shared-memory limit is a per-device function attribute
     static std::mutex mu;
@@ -474,6 +921,14 @@ extern "C" int tthrml_dense_field_sample(const void* source_state, const void* w
       for (const void* f : fns) {
         e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return cuda_status(e, "k_dense_field_sample shared memory attribute");
+      }
+      const void* fns2[4] = {(const void*)k_dense_field_sample_pair<TTHRML_SPIN, false>,
+                             (const void*)k_dense_field_sample_pair<TTHRML_SPIN, true>,
+                             (const void*)k_dense_field_sample_pair<TTHRML_GAUSSIAN, false>,
+                             (const void*)k_dense_field_sample_pair<TTHRML_GAUSSIAN, true>};
+      for (const void* f : fns2) {
+        e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+        if (e != cudaSuccess) return cuda_status(e, "k_dense_field_sample_pair shared memory attribute");
       }
       attr_set[dev] = true;
     }
@@ -496,13 +951,21 @@ extern "C" int tthrml_dense_field_sample(const void* source_state, const void* w
   a.precision = precision;
   a.ctl = ctl;
   a.error = error;
+  const bool settle = TTHRML_DENSE_SETTLE == 2 && ties != nullptr && family == TTHRML_SPIN;
+  a.ties = settle ? ties : nullptr;
+  a.ties_cap = settle ? ties_capacity : 0;
   int sms = 0, dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return cuda_status(e, "tthrml_dense_field_sample: device query");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (pair) {
+    rc = launch_pair(ma, mb, a, family, variates != nullptr, st);
+    if (rc == TTHRML_OK && settle) rc = launch_settle(a, source_state, weights_nk, sms, st);
+    return rc;
+  }
   const int64_t n_tiles = (n_chains / BM) * (n_units / BN);
   const int grid = (int)(n_tiles < sms ? n_tiles : sms);
-  cudaStream_t st = (cudaStream_t)stream;
   if (family == TTHRML_SPIN) {
     if (variates)
       k_dense_field_sample<TTHRML_SPIN, true><<<grid, kDenseThreads, SMEM_BYTES, st>>>(ma, mb, a);
@@ -514,5 +977,37 @@ extern "C" int tthrml_dense_field_sample(const void* source_state, const void* w
     else
       k_dense_field_sample<TTHRML_GAUSSIAN, false><<<grid, kDenseThreads, SMEM_BYTES, st>>>(ma, mb, a);
   }
-  return launch_status("k_dense_field_sample launch");
+  rc = launch_status("k_dense_field_sample launch");
+  if (rc == TTHRML_OK && settle) rc = launch_settle(a, source_state, weights_nk, sms, st);
+  return rc;
+}
+
+}  // namespace
+
+extern "C" int tthrml_dense_field_sample(const void* source_state, const void* weights_nk, int64_t n_chains,
+                                         int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
+                                         float precision, void* out_state, float* out_state_f32,
+                                         int32_t out_pieces, int64_t row0,
+                                         int64_t chain_offset, const float* variates, int64_t variates_sweeps,
+                                         uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, int32_t* error,
+                                         void* stream) {
+  return dense_field_sample(source_state, weights_nk, n_chains, n_units, n_sources, bias, family, precision,
+                            out_state, out_state_f32, out_pieces, row0, chain_offset, variates, variates_sweeps,
+                            seed, sweep, ctl, error, nullptr, 0, stream);
+}
+
+extern "C" int tthrml_dense_field_sample_ties(const void* source_state, const void* weights_nk, int64_t n_chains,
+                                              int64_t n_units, int64_t n_sources, const float* bias, int32_t family,
+                                              float precision, void* out_state, float* out_state_f32,
+                                              int32_t out_pieces, int64_t row0, int64_t chain_offset,
+                                              const float* variates, int64_t variates_sweeps, uint64_t seed,
+                                              uint32_t sweep, const tthrml_run_ctl* ctl, int32_t* error,
+                                              uint32_t* ties, int64_t ties_capacity, void* stream) {
+  if (!ties) {
+    tthrml::set_error("tthrml_dense_field_sample_ties: NULL tie list");
+    return TTHRML_ERR_ARG;
+  }
+  return dense_field_sample(source_state, weights_nk, n_chains, n_units, n_sources, bias, family, precision,
+                            out_state, out_state_f32, out_pieces, row0, chain_offset, variates, variates_sweeps,
+                            seed, sweep, ctl, error, ties, ties_capacity, stream);
 }

@@ -99,6 +99,7 @@ class Executor:
         self._dense = self.compiled.state_dtype == "dense_bf16"
         self._block_states: list | None = None
         self._error_word = None
+        self._ties = None
 
         self._global_state = None
         self._state_loaded = False
@@ -144,6 +145,12 @@ class Executor:
                     for p, cb in zip(self._dense_pieces, self.compiled.blocks)
                 ]
                 self._error_word = torch.zeros(1, dtype=torch.int32, device=self._tdev)
+                # near-threshold spin decisions of one dense launch, settled from the exact field
+                # (4 header words, then (chain, unit) pairs; a few in 10^5 decisions are near)
+                sizes = [self.n_chains * plan.n_units for plan in self._plans()
+                         if plan.kind == "dense" and plan.family == Family.SPIN]
+                self._ties_cap = min(2**31 - 1, max([min(n, max(4096, n // 256)) for n in sizes], default=1))
+                self._ties = torch.zeros(4 + 2 * self._ties_cap, dtype=torch.int32, device=self._tdev)
             return self._block_states
         if self._global_state is None:
             self._global_state = torch.empty(
@@ -491,7 +498,7 @@ class Executor:
             bi = plan.block_indices[0]
             v = self._variates(bi)
             nat.check(
-                self._lib.tthrml_dense_field_sample(
+                self._lib.tthrml_dense_field_sample_ties(
                     self._block_states[plan.source].data_ptr(),
                     plan.weights_nk.data_ptr(),
                     self.n_chains,
@@ -511,9 +518,11 @@ class Executor:
                     sweep_idx,
                     ctl,
                     self._error_word.data_ptr(),
+                    self._ties.data_ptr(),
+                    self._ties_cap,
                     stream,
                 ),
-                "tthrml_dense_field_sample",
+                "tthrml_dense_field_sample_ties",
             )
         elif plan.kind == "ising2d":
             bi = plan.block_indices[0]
@@ -695,6 +704,13 @@ class Executor:
             meta = ast.literal_eval(str(f["meta"]))
             meta["buffers"] = [f[f"buffer{i}"] for i in range(sum(1 for k in f.files if k.startswith("buffer")))]
         self.restore(meta, key=key)
+
+    def near_ties_dropped(self) -> int:
+        """Near-threshold dense spin decisions that did not fit the tie list (they kept their float32 decision)."""
+        if self._ties is None:
+            return 0
+        self._stream.synchronize()
+        return int(self._ties[2].item())
 
     def check_device_errors(self) -> None:
         """Raises if a kernel recorded an expired in-kernel wait (dense programs)."""
