@@ -669,7 +669,9 @@ def run_chain_sharded(ctx, args, W, steps, warmup, cpu):
     ex = mesh.shards[0]  # this process's chains
     assert ex.n_chains == C and ex.chain_offset == ctx.rank * C
     W.check(ex)
-    n_groups = len(ex.compiled.sampling_groups)
+    # a dense spin group launches the GEMM and the near-threshold settle kernel
+    n_group_launches = sum(2 if g.kernel_artifact.kind == "dense" and g.kernel_artifact.family == "spin" else 1
+                           for g in ex.compiled.sampling_groups)
     init = W.init(prog, C, 100 + ctx.rank)
     mesh.load_state(init, [])
     mesh.prepare_rng(SEED)
@@ -697,7 +699,7 @@ def run_chain_sharded(ctx, args, W, steps, warmup, cpu):
     value = updates / (dt_ms / 1000.0)
     resident = ex._resident_plans() is not None
     # group kernels + the run-control advance of each graph, or one launch per step (resident lattice)
-    gpu_launches = steps * (1 if resident else S * n_groups + 1)
+    gpu_launches = steps * (1 if resident else S * n_group_launches + 1)
 
     # ---- roofline: per-launch CUDA events on the launch stream (eager sweeps)
     ex.profile = True

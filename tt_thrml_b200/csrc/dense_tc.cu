@@ -140,6 +140,7 @@ struct DenseArgs {
   int* error;              // device word, set on a wait timeout
   uint32_t* ties;          // near-threshold spin decisions: [count, blocks done, dropped, 0, (m, n) x ties_cap]
   int64_t ties_cap;        // or NULL: decisions from the float32 field alone
+  int32_t group;           // CTA-pair kernel: row blocks per raster group
 };
 
 // A spin decision whose float32 margin is this close to the threshold (in units of u * (1 + e^(-2 gamma))
@@ -182,15 +183,21 @@ __device__ __forceinline__ void record_ties(uint32_t* ties, int64_t cap, uint32_
   }
 }
 
-// Tile t of a persistent CTA -> (m block, n block): groups of kGroupM row
-// blocks are walked n-fastest, so the tiles in flight at one time share a few
-// A row panels and a band of B panels in L2.
+// Tile t of a persistent CTA -> (m block, n block): the row blocks are taken
+// `group` at a time and each group is walked row-fastest, so the tiles in
+// flight at one time share one or two B column panels while the group's A
+// row panels stay in L2 for the sweep over the group's columns.  The
+// single-CTA kernel takes 16 row blocks of 128 rows; the CTA-pair kernel
+// sizes its groups of 256-row blocks to about 32 MiB of A panels
+// (group x 256 x K x 2 bytes), which measured lowest in DRAM bytes for both
+// GEMMs of the 4096 x 8192 RBM (K = 4096: 16 blocks, K = 8192: 8 blocks;
+// 64 MiB groups or a plain row-major walk re-read more).
 constexpr int kGroupM = 16;
-__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int& mb, int& nb) {
-  const int per_group = kGroupM * n_blocks;
+__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int group, int& mb, int& nb) {
+  const int per_group = group * n_blocks;
   const int g = t / per_group, w = t - g * per_group;
-  const int rows = min(kGroupM, m_blocks - g * kGroupM);
-  mb = g * kGroupM + w % rows;
+  const int rows = min(group, m_blocks - g * group);
+  mb = g * group + w % rows;
   nb = w / rows;
 }
 
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       bool failed = false;
       for (int t = blockIdx.x; t < n_tiles && !failed; t += gridDim.x) {
         int mb, nb;
-        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        tile_coords(t, m_blocks, n_blocks, kGroupM, mb, nb);
         for (int kb = 0; kb < num_k; ++kb) {
           const int s = (int)(issued % STAGES);
           const uint32_t round = (uint32_t)(issued / STAGES);
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
     int it = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       int mb, nb;
-      tile_coords(t, m_blocks, n_blocks, mb, nb);
+      tile_coords(t, m_blocks, n_blocks, kGroupM, mb, nb);
       const int b = it & 1;
       const bool ok = mbar_wait(&acc_full[b], (uint32_t)(it >> 1) & 1u);
       if (!ok) {
@@ -547,7 +554,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       bool failed = false;
       for (int t = first; t < n_tiles && !failed; t += step) {
         int mb, nb;
-        tile_coords(t, m_blocks, n_blocks, mb, nb);
+        tile_coords(t, m_blocks, n_blocks, args.group, mb, nb);
         for (int kb = 0; kb < num_k; ++kb) {
           const int s = (int)(issued % STAGES2);
           const uint32_t round = (uint32_t)(issued / STAGES2);
@@ -610,7 +617,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
     int it = 0;
     for (int t = first; t < n_tiles; t += step, ++it) {
       int mb, nb;
-      tile_coords(t, m_blocks, n_blocks, mb, nb);
+      tile_coords(t, m_blocks, n_blocks, args.group, mb, nb);
       const int b = it & 1;
       if (!mbar_wait(&acc_full[b], (uint32_t)(it >> 1) & 1u)) {
         atomicExch(args.error, kErrAccWait);
@@ -743,18 +750,19 @@ __global__ void __launch_bounds__(kSettleThreads) k_dense_settle(SettleArgs a) {
     if (m >= a.M || n >= a.N) continue;  // never recorded so; keeps every access below in bounds
     const __nv_bfloat16* ar = a.a_mat + m * a.K;
     const __nv_bfloat16* br = a.b_mat + n * a.K;
-    double acc = 0.0;
-#pragma unroll 4
+    double part[4] = {0.0, 0.0, 0.0, 0.0};  // four independent chains of double adds
+#pragma unroll 8
     for (int64_t k = 8 * lane; k < a.K; k += 256) {
       const uint4 av = __ldg(reinterpret_cast<const uint4*>(ar + k));
       const uint4 bv = __ldg(reinterpret_cast<const uint4*>(br + k));
       const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        acc += (double)__uint_as_float(aw[q] << 16) * (double)__uint_as_float(bw[q] << 16);
-        acc += (double)__uint_as_float(aw[q] & 0xFFFF0000u) * (double)__uint_as_float(bw[q] & 0xFFFF0000u);
+        part[q] += (double)__uint_as_float(aw[q] << 16) * (double)__uint_as_float(bw[q] << 16);
+        part[q] += (double)__uint_as_float(aw[q] & 0xFFFF0000u) * (double)__uint_as_float(bw[q] & 0xFFFF0000u);
       }
     }
+    double acc = (part[0] + part[1]) + (part[2] + part[3]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) {
@@ -951,6 +959,11 @@ int dense_field_sample(const void* source_state, const void* weights_nk, int64_t
   a.precision = precision;
   a.ctl = ctl;
   a.error = error;
+  {  // raster groups of about 32 MiB of A panels (256-row blocks)
+    const int64_t g = ((int64_t)32 << 20) / (2 * BM2 * n_sources * 2);
+    const int64_t mblk = n_chains / (2 * BM2);
+    a.group = (int32_t)(g < 1 ? 1 : (g > mblk ? (mblk > 0 ? mblk : 1) : g));
+  }
   const bool settle = TTHRML_DENSE_SETTLE == 2 && ties != nullptr && family == TTHRML_SPIN;
   a.ties = settle ? ties : nullptr;
   a.ties_cap = settle ? ties_capacity : 0;
