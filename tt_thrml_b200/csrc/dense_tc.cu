@@ -28,7 +28,7 @@
 
 #include <mutex>
 
-#include "common.cuh"
+#include "spin_common.cuh"
 
 namespace tthrml {
 namespace {
@@ -37,7 +37,12 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each taking half of the columns
+#ifndef TTHRML_DENSE_EPI_WARPS
+#define TTHRML_DENSE_EPI_WARPS 8
+#endif
+// epilogue warps: kEpiGroups per TMEM lane quadrant, group g taking the 32-column chunks c = g mod kEpiGroups
+constexpr int kEpiWarps = TTHRML_DENSE_EPI_WARPS;
+constexpr int kEpiGroups = kEpiWarps / 4;
 constexpr int kDenseThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kTmemCols = 256;
 constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
@@ -201,66 +206,163 @@ __device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, i
   nb = w / rows;
 }
 
-// Epilogue of one 32-column chunk of one row (chain m): draw and store.
-template <int FAMILY, bool VARIATES>
-__device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m, int64_t n_first,
-                                           uint32_t sweep, uint32_t k0, uint32_t k1, float inv, float sd_g,
-                                           int64_t vs) {
+// The 32 biases of a chunk (n_first % 32 == 0, bias 16-byte aligned): eight 16-byte loads, the same
+// addresses in every lane; zeros without a bias.
+__device__ __forceinline__ void load_bias32(const float* bias, int64_t n_first, float (&b)[32]) {
+  if (!bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) b[j] = 0.0f;
+    return;
+  }
+  const float4* bq = reinterpret_cast<const float4*>(bias + n_first);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 v = __ldg(bq + q);
+    b[4 * q] = v.x;
+    b[4 * q + 1] = v.y;
+    b[4 * q + 2] = v.z;
+    b[4 * q + 3] = v.w;
+  }
+}
+
+// Spin epilogue of one 32-column chunk of row m: bit j of the result is set when unit n_first + j samples
+// -1.  +1 with probability sigmoid(2 field): u * (1 + e^(-2 field)) < 1 with u = uniform_open of the
+// unit's Philox word (u is built with ALU operations, bit for bit the same value), or 2 field > logit.
+// `near` receives the decisions within kNearTie of their threshold.
+template <bool VARIATES>
+__device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m,
+                                               int64_t n_first, uint32_t sweep, uint32_t k0, uint32_t k1,
+                                               int64_t vs, uint32_t& near) {
   const int64_t gchain = a.chain_offset + m;
-  float outf[32];
+  const int64_t r0 = a.row0 + n_first;
+  uint32_t down = 0u;
+  near = 0u;
+  if (VARIATES) {
+    float b[32];
+    load_bias32(a.bias, n_first, b);
+    const float* vrow = a.variates + (vs * a.N + n_first) * a.M + m;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float field = __fadd_rn(acc[j], b[j]);
+      const float d = __fsub_rn(__fmul_rn(2.0f, field), __ldg(vrow + (int64_t)j * a.M));
+      down |= (d > 0.0f ? 0u : 1u) << j;
+      if (TTHRML_DENSE_SETTLE) near |= (fabsf(d) < kNearTie ? 1u : 0u) << j;
+    }
+  } else if ((r0 & 3) == 0) {  // the chunk starts a Philox counter: word j % 4 of counter r0 / 4 + j / 4
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)((r0 >> 2) + q), sweep, kSaltDenseSpin}, k0, k1);
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+      const float4 bq = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + n_first) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float b[4] = {bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = 4 * q + i;
+        const float field = __fadd_rn(acc[j], b[i]);
+        const float t = uniform_open_alu(w[i]) * (1.0f + __expf(-2.0f * field));
+        down |= (t < 1.0f ? 0u : 1u) << j;
+        if (TTHRML_DENSE_SETTLE) near |= (fabsf(t - 1.0f) < kNearTie ? 1u : 0u) << j;
+      }
+    }
+  } else {
+    float b[32];
+    load_bias32(a.bias, n_first, b);
+    u32x4 r{0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int64_t row = r0 + j;
+      if (j == 0 || (row & 3) == 0)
+        r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseSpin}, k0, k1);
+      const float field = __fadd_rn(acc[j], b[j]);
+      const float t = uniform_open_alu(word_of(r, (int)(row & 3))) * (1.0f + __expf(-2.0f * field));
+      down |= (t < 1.0f ? 0u : 1u) << j;
+      if (TTHRML_DENSE_SETTLE) near |= (fabsf(t - 1.0f) < kNearTie ? 1u : 0u) << j;
+    }
+  }
+  return down;
+}
+
+// Gaussian epilogue of one 32-column chunk: field * var + sqrt(var) * xi, xi from Box-Muller on the two
+// words of the unit's Philox pair (or the uploaded normal).
+template <bool VARIATES>
+__device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m,
+                                            int64_t n_first, uint32_t sweep, uint32_t k0, uint32_t k1, float inv,
+                                            float sd_g, int64_t vs, float (&outf)[32]) {
+  float b[32];
+  load_bias32(a.bias, n_first, b);
+  const int64_t gchain = a.chain_offset + m;
   u32x4 r{0u, 0u, 0u, 0u};
-  uint32_t near = 0u;  // bit j: the spin of column n_first + j was decided within kNearTie of its threshold
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const int64_t n = n_first + j;
     const int64_t row = a.row0 + n;
-    const float field = a.bias ? __fadd_rn(acc[j], __ldg(a.bias + n)) : acc[j];
-    float v;
-    if (FAMILY == TTHRML_SPIN) {
-      bool up;
-      if (VARIATES) {
-        const float d = __fsub_rn(__fmul_rn(2.0f, field), __ldg(a.variates + (vs * a.N + n) * a.M + m));
-        up = d > 0.0f;
-        if (TTHRML_DENSE_SETTLE) near |= (fabsf(d) < kNearTie ? 1u : 0u) << j;
-      } else {
-        if (j == 0 || (row & 3) == 0)
-          r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseSpin}, k0, k1);
-        const float t = uniform_open(word_of(r, (int)(row & 3))) * (1.0f + __expf(-2.0f * field));
-        up = t < 1.0f;
-        if (TTHRML_DENSE_SETTLE) near |= (fabsf(t - 1.0f) < kNearTie ? 1u : 0u) << j;
-      }
-      v = up ? 1.0f : -1.0f;
+    const float field = a.bias ? __fadd_rn(acc[j], b[j]) : acc[j];
+    float xi;
+    if (VARIATES) {
+      xi = __ldg(a.variates + (vs * a.N + n) * a.M + m);
     } else {
-      float xi;
-      if (VARIATES) {
-        xi = __ldg(a.variates + (vs * a.N + n) * a.M + m);
-      } else {
-        if (j == 0 || (row & 1) == 0)
-          r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 1), sweep, kSaltDenseGauss}, k0, k1);
-        const int w = (int)(row & 1) * 2;
-        xi = sqrtf(-2.0f * logf(uniform_open(word_of(r, w)))) * cospif(2.0f * uniform_open(word_of(r, w + 1)));
-      }
-      v = __fadd_rn(__fmul_rn(field, inv), __fmul_rn(sd_g, xi));
+      if (j == 0 || (row & 1) == 0)
+        r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 1), sweep, kSaltDenseGauss}, k0, k1);
+      const int w = (int)(row & 1) * 2;
+      xi = sqrtf(-2.0f * logf(uniform_open(word_of(r, w)))) * cospif(2.0f * uniform_open(word_of(r, w + 1)));
     }
-    outf[j] = v;
+    outf[j] = __fadd_rn(__fmul_rn(field, inv), __fmul_rn(sd_g, xi));
   }
-  if (FAMILY == TTHRML_SPIN && TTHRML_DENSE_SETTLE == 2 && a.ties != nullptr &&
-      __any_sync(0xffffffffu, near != 0u))  // rare: k_dense_settle decides these again from the exact field
-    record_ties(a.ties, a.ties_cap, near, m, n_first);
+}
+
+// Epilogue of one 32-column chunk of one row (chain m): draw and store.  The new value goes to the
+// float32 copy (if any) and as `pieces` bf16 pieces: piece p = bf16(v - pieces 0..p-1), each remainder
+// exact in float32, so three pieces carry all 24 significand bits.  A spin's +-1 is one bf16 piece
+// (0x3F80 / 0xBF80) and zero remainders.
+template <int FAMILY, bool VARIATES>
+__device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m, int64_t n_first,
+                                           uint32_t sweep, uint32_t k0, uint32_t k1, float inv, float sd_g,
+                                           int64_t vs) {
+  __nv_bfloat16* row = a.out + m * (a.N * a.pieces) + n_first;
+  if (FAMILY == TTHRML_SPIN) {
+    uint32_t near;
+    const uint32_t down = spin_chunk<VARIATES>(a, acc, m, n_first, sweep, k0, k1, vs, near);
+    if (TTHRML_DENSE_SETTLE == 2 && a.ties != nullptr &&
+        __any_sync(0xffffffffu, near != 0u))  // rare: k_dense_settle decides these again from the exact field
+      record_ties(a.ties, a.ties_cap, near, m, n_first);
+    if (a.out_f32) {
+      float4* df = reinterpret_cast<float4*>(a.out_f32 + m * a.N + n_first);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(0x3F800000u | (((down >> (4 * q + i)) & 1u) << 31));
+        df[q] = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+    uint32_t w[16];  // bf16 pairs (unit 2k in the low half)
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      w[k] = 0x3F803F80u | (((down >> (2 * k)) & 1u) << 15) | (((down >> (2 * k + 1)) & 1u) << 31);
+    uint4* dst = reinterpret_cast<uint4*>(row);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    for (int p = 1; p < a.pieces; ++p) {
+      uint4* z = reinterpret_cast<uint4*>(row + p * a.N);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) z[q] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
+  float outf[32];
+  gauss_chunk<VARIATES>(a, acc, m, n_first, sweep, k0, k1, inv, sd_g, vs, outf);
   if (a.out_f32) {
     float4* df = reinterpret_cast<float4*>(a.out_f32 + m * a.N + n_first);
 #pragma unroll
     for (int q = 0; q < 8; ++q) df[q] = make_float4(outf[4 * q], outf[4 * q + 1], outf[4 * q + 2], outf[4 * q + 3]);
   }
-  // piece p = bf16(v - pieces 0..p-1); each remainder is exact in float32, so
-  // three pieces carry all 24 significand bits
-  __nv_bfloat16* row = a.out + m * (a.N * a.pieces) + n_first;
   for (int p = 0; p < a.pieces; ++p) {
     __align__(16) __nv_bfloat16 outv[32];
+    const bool last = p + 1 == a.pieces;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       outv[j] = __float2bfloat16_rn(outf[j]);
-      outf[j] = __fsub_rn(outf[j], __bfloat162float(outv[j]));
+      if (!last) outf[j] = __fsub_rn(outf[j], __bfloat162float(outv[j]));
     }
     uint4* dst = reinterpret_cast<uint4*>(row + p * a.N);
     const uint4* srcv = reinterpret_cast<const uint4*>(outv);
@@ -380,7 +482,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
     // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 of the finished
     // accumulator; warps 2-5 take the even 32-column chunks, warps 6-9 the odd
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int grp = (warp - 2) >> 2;
     int it = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       int mb, nb;
@@ -399,7 +501,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       const int64_t vs =
           args.variates ? (int64_t)(sweep % (uint32_t)(args.variates_sweeps > 0 ? args.variates_sweeps : 1)) : 0;
       const int64_t m = (int64_t)mb * BM + quad * 32 + lane;
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = grp; c < BN / 32; c += kEpiGroups) {
         float acc[32];
         tmem_load32(tmem + (uint32_t)(b * kTmemCols) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32), acc);
         draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, seed_lo(sd), seed_hi(sd), inv,
@@ -450,7 +552,10 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
 #ifndef TTHRML_DENSE_2SM
 #define TTHRML_DENSE_2SM 1
 #endif
-constexpr int BM2 = 128, BN2H = 128, STAGES2 = 6;
+#ifndef TTHRML_DENSE_STAGES2
+#define TTHRML_DENSE_STAGES2 6
+#endif
+constexpr int BM2 = 128, BN2H = 128, STAGES2 = TTHRML_DENSE_STAGES2;
 constexpr int A2_BYTES = BM2 * BK * 2;   // 16 KiB
 constexpr int B2_BYTES = BN2H * BK * 2;  // 16 KiB
 constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
@@ -613,7 +718,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
   } else {
     // epilogue (both CTAs): this CTA's 128 rows of the tile, as in the single-CTA kernel
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int grp = (warp - 2) >> 2;
     int it = 0;
     for (int t = first; t < n_tiles; t += step, ++it) {
       int mb, nb;
@@ -631,7 +736,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       const int64_t vs =
           args.variates ? (int64_t)(sweep % (uint32_t)(args.variates_sweeps > 0 ? args.variates_sweeps : 1)) : 0;
       const int64_t m = (int64_t)mb * 2 * BM2 + (int64_t)rank * BM2 + quad * 32 + lane;
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = grp; c < BN / 32; c += kEpiGroups) {
         float acc[32];
         tmem_load32(tmem + (uint32_t)(b * kTmemCols) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32), acc);
         draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, seed_lo(sd), seed_hi(sd), inv,
@@ -900,7 +1005,7 @@ int dense_field_sample(const void* source_state, const void* weights_nk, int64_t
     return TTHRML_ERR_ARG;
   }
   if (chain_offset % 4 || ((uintptr_t)source_state % 16) || ((uintptr_t)weights_nk % 16) || ((uintptr_t)out_state % 16) ||
-      (out_state_f32 && ((uintptr_t)out_state_f32 % 16))) {
+      (out_state_f32 && ((uintptr_t)out_state_f32 % 16)) || (bias && ((uintptr_t)bias % 16))) {
     set_error("tthrml_dense_field_sample: buffers must be 16-byte aligned and chain_offset a multiple of 4");
     return TTHRML_ERR_ARG;
   }
