@@ -412,8 +412,10 @@ int tthrml_halo_import(int8_t* colour0_dev, int8_t* colour1_dev, int64_t width, 
  * var = 1/(precision + 1e-6).  Philox counters run along the unit axis of a
  * chain: spins of units 4j..4j+3 take the four words of
  * (chain_offset + chain, (row0 + unit) / 4, sweep, "DSPI"); gaussian units
- * 2j, 2j+1 the word pairs of (chain_offset + chain, (row0 + unit) / 2, sweep,
- * "DGAU") through Box-Muller.  variates: [variates_sweeps][n_units][n_chains]
+ * of flat rows 4j..4j+3 (row = row0 + unit) the counter (chain_offset +
+ * chain, j, sweep, "DGAU") through Box-Muller: words 2p, 2p+1 give
+ * r = sqrt(-2 ln u0), theta = 2 pi u1, row 4j+2p takes r cos theta and row
+ * 4j+2p+1 r sin theta.  variates: [variates_sweeps][n_units][n_chains]
  * or NULL.
  * Requires n_chains % 128 == 0, n_units % 256 == 0, n_sources % 64 == 0 and
  * 16-byte aligned buffers.  Waits inside the kernel are bounded: a device

@@ -186,13 +186,19 @@ static double or_spin_uniform(int layout, int64_t gc, int64_t row, uint32_t swee
   return or_uniform(or_philox((uint32_t)(gc >> 2), (uint32_t)row, sweep, SALT_SPIN, k0, k1).v[gc & 3]);
 }
 
-/* Philox-mode standard normal of a gaussian draw (Box-Muller on two uniforms of one counter). */
+/* Philox-mode standard normal of a gaussian draw: Box-Muller on two uniforms of one counter.  Generic
+ * kernels: counter (chain, row, sweep, "GAUS"), words 0 and 1, the cosine output.  Dense kernel (layout 1):
+ * counter (chain, row/4, sweep, "DGAU") serves four rows, words 2p and 2p+1 for rows 4j+2p and 4j+2p+1,
+ * the cosine output for the even row and the sine output for the odd one. */
 static double or_gauss_normal(int layout, int64_t gc, int64_t row, uint32_t sweep, uint32_t k0, uint32_t k1) {
-  const int dense = layout == 1;
-  const or_u32x4 r = dense ? or_philox((uint32_t)gc, (uint32_t)(row >> 1), sweep, SALT_DENSE_GAUSS, k0, k1)
-                           : or_philox((uint32_t)gc, (uint32_t)row, sweep, SALT_GAUSS, k0, k1);
-  const int w = dense ? (int)(row & 1) * 2 : 0;
-  return sqrt(-2.0 * log(or_uniform(r.v[w]))) * cos(2.0 * M_PI * or_uniform(r.v[w + 1]));
+  if (layout == 1) {
+    const or_u32x4 r = or_philox((uint32_t)gc, (uint32_t)(row >> 2), sweep, SALT_DENSE_GAUSS, k0, k1);
+    const int w = (int)((row >> 1) & 1) * 2;
+    const double rad = sqrt(-2.0 * log(or_uniform(r.v[w]))), th = 2.0 * M_PI * or_uniform(r.v[w + 1]);
+    return (row & 1) ? rad * sin(th) : rad * cos(th);
+  }
+  const or_u32x4 r = or_philox((uint32_t)gc, (uint32_t)row, sweep, SALT_GAUSS, k0, k1);
+  return sqrt(-2.0 * log(or_uniform(r.v[0]))) * cos(2.0 * M_PI * or_uniform(r.v[1]));
 }
 
 /* Philox-mode uniform of a categorical draw: counter (chain/4, row, sweep), word chain % 4. */

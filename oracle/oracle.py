@@ -358,7 +358,8 @@ class OracleSampler:
         every block or a dict block index -> name.  "chain4": counter (chain/4,
         row, sweep), word chain % 4 (the sparse, generic and Potts kernels);
         "row4": counter (chain, row/4, sweep), word row % 4 (the tensor-core
-        dense kernel); "row8s" / "chain8s": the lattice kernels' split uniforms
+        dense kernel; its gaussians take Box-Muller on words 2p, 2p+1 for rows
+        4j+2p (cosine) and 4j+2p+1 (sine)); "row8s" / "chain8s": the lattice kernels' split uniforms
         (spin blocks: 16 bits of counter (chain, row/8, sweep) resp.
         (chain/8, row, sweep), "LSPI", and 7 refill bits of (chain, row, sweep),
         "LREF"; the single-chain stencil and the resident lattice kernel);

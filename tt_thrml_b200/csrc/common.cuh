@@ -31,8 +31,9 @@ constexpr uint32_t kSaltSpin = 0x5350494eu;      // "SPIN"
 constexpr uint32_t kSaltGauss = 0x47415553u;     // "GAUS"
 constexpr uint32_t kSaltCat = 0x43415400u;       // "CAT\0"
 // Dense (tensor-core) blocks draw along the unit axis of one chain: counter
-// (chain, row/4, sweep, salt) gives the spins of four consecutive rows,
-// (chain, row/2, sweep, salt) the two uniforms of two gaussian rows.
+// (chain, row/4, sweep, salt) gives the spins of four consecutive rows, or
+// the normals of four gaussian rows: Box-Muller on words 2p, 2p+1 gives rows
+// 4j+2p (r cos theta) and 4j+2p+1 (r sin theta).
 constexpr uint32_t kSaltDenseSpin = 0x44535049u;   // "DSPI"
 constexpr uint32_t kSaltDenseGauss = 0x44474155u;  // "DGAU"
 // Lattice (threshold-table) spin draws use split uniforms: the 23-bit draw

@@ -282,8 +282,17 @@ __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (
   return down;
 }
 
-// Gaussian epilogue of one 32-column chunk: field * var + sqrt(var) * xi, xi from Box-Muller on the two
-// words of the unit's Philox pair (or the uploaded normal).
+// Box-Muller on words 2p, 2p+1 of a counter: the normals of rows 4j+2p (cosine) and 4j+2p+1 (sine).
+__device__ __forceinline__ void box_muller_pair(uint32_t w0, uint32_t w1, float& xc, float& xs) {
+  const float rad = sqrtf(-2.0f * logf(uniform_open(w0)));
+  float sn, cs;
+  sincospif(2.0f * uniform_open(w1), &sn, &cs);
+  xc = rad * cs;
+  xs = rad * sn;
+}
+
+// Gaussian epilogue of one 32-column chunk: field * var + sqrt(var) * xi, xi the unit's normal from the
+// counter (chain, row / 4, sweep, "DGAU") (or the uploaded normal).
 template <bool VARIATES>
 __device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m,
                                             int64_t n_first, uint32_t sweep, uint32_t k0, uint32_t k1, float inv,
@@ -291,22 +300,34 @@ __device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&ac
   float b[32];
   load_bias32(a.bias, n_first, b);
   const int64_t gchain = a.chain_offset + m;
-  u32x4 r{0u, 0u, 0u, 0u};
+  const int64_t r0 = a.row0 + n_first;
+  float xi[32];
+  if (VARIATES) {
+    const float* vrow = a.variates + (vs * a.N + n_first) * a.M + m;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) xi[j] = __ldg(vrow + (int64_t)j * a.M);
+  } else if ((r0 & 3) == 0) {  // the chunk starts a counter: rows 4q..4q+3 of the chunk share counter q
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)((r0 >> 2) + q), sweep, kSaltDenseGauss}, k0, k1);
+      box_muller_pair(r.x, r.y, xi[4 * q], xi[4 * q + 1]);
+      box_muller_pair(r.z, r.w, xi[4 * q + 2], xi[4 * q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int64_t row = r0 + j;
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseGauss}, k0, k1);
+      const int w = (int)((row >> 1) & 1) * 2;
+      float xc, xs;
+      box_muller_pair(word_of(r, w), word_of(r, w + 1), xc, xs);
+      xi[j] = (row & 1) ? xs : xc;
+    }
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const int64_t n = n_first + j;
-    const int64_t row = a.row0 + n;
     const float field = a.bias ? __fadd_rn(acc[j], b[j]) : acc[j];
-    float xi;
-    if (VARIATES) {
-      xi = __ldg(a.variates + (vs * a.N + n) * a.M + m);
-    } else {
-      if (j == 0 || (row & 1) == 0)
-        r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 1), sweep, kSaltDenseGauss}, k0, k1);
-      const int w = (int)(row & 1) * 2;
-      xi = sqrtf(-2.0f * logf(uniform_open(word_of(r, w)))) * cospif(2.0f * uniform_open(word_of(r, w + 1)));
-    }
-    outf[j] = __fadd_rn(__fmul_rn(field, inv), __fmul_rn(sd_g, xi));
+    outf[j] = __fadd_rn(__fmul_rn(field, inv), __fmul_rn(sd_g, xi[j]));
   }
 }
 
