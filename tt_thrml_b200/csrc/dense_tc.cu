@@ -231,7 +231,7 @@ __device__ __forceinline__ void load_bias32(const float* bias, int64_t n_first, 
 // `near` receives the decisions within kNearTie of their threshold.
 template <bool VARIATES>
 __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m,
-                                               int64_t n_first, uint32_t sweep, uint32_t k0, uint32_t k1,
+                                               int64_t n_first, uint32_t sweep, const PhiloxKeys& keys,
                                                int64_t vs, uint32_t& near) {
   const int64_t gchain = a.chain_offset + m;
   const int64_t r0 = a.row0 + n_first;
@@ -251,7 +251,7 @@ __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (
   } else if ((r0 & 3) == 0) {  // the chunk starts a Philox counter: word j % 4 of counter r0 / 4 + j / 4
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)((r0 >> 2) + q), sweep, kSaltDenseSpin}, k0, k1);
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)((r0 >> 2) + q), sweep, kSaltDenseSpin}, keys);
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
       const float4 bq = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + n_first) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       const float b[4] = {bq.x, bq.y, bq.z, bq.w};
@@ -272,7 +272,7 @@ __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (
     for (int j = 0; j < 32; ++j) {
       const int64_t row = r0 + j;
       if (j == 0 || (row & 3) == 0)
-        r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseSpin}, k0, k1);
+        r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseSpin}, keys);
       const float field = __fadd_rn(acc[j], b[j]);
       const float t = uniform_open_alu(word_of(r, (int)(row & 3))) * (1.0f + __expf(-2.0f * field));
       down |= (t < 1.0f ? 0u : 1u) << j;
@@ -295,7 +295,7 @@ __device__ __forceinline__ void box_muller_pair(uint32_t w0, uint32_t w1, float&
 // counter (chain, row / 4, sweep, "DGAU") (or the uploaded normal).
 template <bool VARIATES>
 __device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m,
-                                            int64_t n_first, uint32_t sweep, uint32_t k0, uint32_t k1, float inv,
+                                            int64_t n_first, uint32_t sweep, const PhiloxKeys& keys, float inv,
                                             float sd_g, int64_t vs, float (&outf)[32]) {
   float b[32];
   load_bias32(a.bias, n_first, b);
@@ -309,7 +309,7 @@ __device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&ac
   } else if ((r0 & 3) == 0) {  // the chunk starts a counter: rows 4q..4q+3 of the chunk share counter q
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)((r0 >> 2) + q), sweep, kSaltDenseGauss}, k0, k1);
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)((r0 >> 2) + q), sweep, kSaltDenseGauss}, keys);
       box_muller_pair(r.x, r.y, xi[4 * q], xi[4 * q + 1]);
       box_muller_pair(r.z, r.w, xi[4 * q + 2], xi[4 * q + 3]);
     }
@@ -317,7 +317,7 @@ __device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&ac
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int64_t row = r0 + j;
-      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseGauss}, k0, k1);
+      const u32x4 r = philox4x32_10(u32x4{(uint32_t)gchain, (uint32_t)(row >> 2), sweep, kSaltDenseGauss}, keys);
       const int w = (int)((row >> 1) & 1) * 2;
       float xc, xs;
       box_muller_pair(word_of(r, w), word_of(r, w + 1), xc, xs);
@@ -337,12 +337,12 @@ __device__ __forceinline__ void gauss_chunk(const DenseArgs& a, const float (&ac
 // (0x3F80 / 0xBF80) and zero remainders.
 template <int FAMILY, bool VARIATES>
 __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc)[32], int64_t m, int64_t n_first,
-                                           uint32_t sweep, uint32_t k0, uint32_t k1, float inv, float sd_g,
+                                           uint32_t sweep, const PhiloxKeys& keys, float inv, float sd_g,
                                            int64_t vs) {
   __nv_bfloat16* row = a.out + m * (a.N * a.pieces) + n_first;
   if (FAMILY == TTHRML_SPIN) {
     uint32_t near;
-    const uint32_t down = spin_chunk<VARIATES>(a, acc, m, n_first, sweep, k0, k1, vs, near);
+    const uint32_t down = spin_chunk<VARIATES>(a, acc, m, n_first, sweep, keys, vs, near);
     if (TTHRML_DENSE_SETTLE == 2 && a.ties != nullptr &&
         __any_sync(0xffffffffu, near != 0u))  // rare: k_dense_settle decides these again from the exact field
       record_ties(a.ties, a.ties_cap, near, m, n_first);
@@ -371,7 +371,7 @@ __device__ __forceinline__ void draw_chunk(const DenseArgs& a, const float (&acc
     return;
   }
   float outf[32];
-  gauss_chunk<VARIATES>(a, acc, m, n_first, sweep, k0, k1, inv, sd_g, vs, outf);
+  gauss_chunk<VARIATES>(a, acc, m, n_first, sweep, keys, inv, sd_g, vs, outf);
   if (a.out_f32) {
     float4* df = reinterpret_cast<float4*>(a.out_f32 + m * a.N + n_first);
 #pragma unroll
@@ -517,6 +517,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       tc_fence_after();
       const uint32_t sweep = args.sweep + (args.ctl ? args.ctl->sweep : 0u);
       const uint64_t sd = args.ctl ? args.ctl->seed : args.seed;
+      const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));  // round keys, once per tile
       const float inv = 1.0f / __fadd_rn(args.precision, 1e-6f);
       const float sd_g = sqrtf(inv);
       const int64_t vs =
@@ -525,7 +526,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       for (int c = grp; c < BN / 32; c += kEpiGroups) {
         float acc[32];
         tmem_load32(tmem + (uint32_t)(b * kTmemCols) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32), acc);
-        draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, seed_lo(sd), seed_hi(sd), inv,
+        draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, keys, inv,
                                      sd_g, vs);
       }
       tc_fence_before();
@@ -752,6 +753,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       tc_fence_after();
       const uint32_t sweep = args.sweep + (args.ctl ? args.ctl->sweep : 0u);
       const uint64_t sd = args.ctl ? args.ctl->seed : args.seed;
+      const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));  // round keys, once per tile
       const float inv = 1.0f / __fadd_rn(args.precision, 1e-6f);
       const float sd_g = sqrtf(inv);
       const int64_t vs =
@@ -760,7 +762,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1)
       for (int c = grp; c < BN / 32; c += kEpiGroups) {
         float acc[32];
         tmem_load32(tmem + (uint32_t)(b * kTmemCols) + ((uint32_t)(quad * 32) << 16) + (uint32_t)(c * 32), acc);
-        draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, seed_lo(sd), seed_hi(sd), inv,
+        draw_chunk<FAMILY, VARIATES>(args, acc, m, (int64_t)nb * BN + c * 32, sweep, keys, inv,
                                      sd_g, vs);
       }
       tc_fence_before();
