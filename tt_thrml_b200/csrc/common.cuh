@@ -140,6 +140,15 @@ __host__ __device__ __forceinline__ float uniform_open(uint32_t bits) {
   return (float)(((bits >> 9) << 1) | 1u) * 5.9604644775390625e-08f;  // 2^-24
 }
 
+#ifdef __CUDACC__
+// Open uniform (2m+1)/2^24, m = bits >> 9, built without an int->float
+// conversion: 1 + m/2^23 from the mantissa, minus (1 - 2^-24); both steps exact,
+// so the value equals uniform_open(bits) bit for bit.
+__device__ __forceinline__ float uniform_open_alu(uint32_t bits) {
+  return __uint_as_float(0x3F800000u | (bits >> 9)) - 0.99999994039535522461f;
+}
+#endif
+
 __host__ __device__ __forceinline__ uint32_t seed_lo(uint64_t s) { return (uint32_t)s; }
 __host__ __device__ __forceinline__ uint32_t seed_hi(uint64_t s) { return (uint32_t)(s >> 32); }
 
@@ -297,8 +306,17 @@ __device__ __forceinline__ int categorical_icdf_weights(const float (&e)[QMAX], 
   if (!(s >= 1.17549435e-38f)) return -1;
   const float t = __fmul_rn(low ? u : 1.0f - u, s);
   int cnt = 0;
+  if constexpr (QMAX == 8) {
+    // h is non-decreasing, so the count of h[0..6] <= t is found by a three-step binary search
+    // (the same count as the linear one): h[3], then h[1] or h[5], then one of h[0], h[2], h[4], h[6]
+    const bool c2 = h[3] <= t;
+    const bool c1 = (c2 ? h[5] : h[1]) <= t;
+    const bool c0 = (c2 ? (c1 ? h[6] : h[4]) : (c1 ? h[2] : h[0])) <= t;
+    cnt = (c2 ? 4 : 0) + (c1 ? 2 : 0) + (c0 ? 1 : 0);
+  } else {
 #pragma unroll
-  for (int j = 0; j < QMAX - 1; ++j) cnt += h[j] <= t ? 1 : 0;
+    for (int j = 0; j < QMAX - 1; ++j) cnt += h[j] <= t ? 1 : 0;
+  }
   return low ? cnt : QMAX - 1 - cnt;
 }
 

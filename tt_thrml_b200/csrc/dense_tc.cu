@@ -28,7 +28,7 @@
 
 #include <mutex>
 
-#include "spin_common.cuh"
+#include "common.cuh"
 
 namespace tthrml {
 namespace {

@@ -245,6 +245,14 @@ constexpr int kExpCopies = TTHRML_POTTS_EXP_COPIES;
 constexpr int kExpRowFloats = kExpCopies == 1 ? 12 : 2 * kExpCopies * 4;
 constexpr int kExpSmemBytes = 3 * kRows * kRows * kExpRowFloats * 4;
 
+// Bytes of x clamped to at most c (each byte unsigned).
+__device__ __forceinline__ uint32_t clamp_bytes(uint32_t x, uint32_t c) {
+  uint32_t y = 0u;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) y |= min((x >> (8 * k)) & 0xFFu, c) << (8 * k);
+  return y;
+}
+
 template <int WPT>
 __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3d_exp(
     int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
@@ -343,6 +351,22 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
       out[ww] = 0u;
       const u32x4 rr =
           philox4x32_10(u32x4{(uint32_t)((chain_offset >> 2) + w + ww), (uint32_t)row, sweep, kSaltCat}, keys);
+      // table rows of the 4 chains of this word, one byte each: 9 * s0 + s1 per axis (<= 80, so the
+      // byte-wise sums never carry), neighbour categories above kPottsQ taken as the zero row kPottsQ
+      uint32_t chk = 0u;
+#pragma unroll
+      for (int j = 0; j < 6; ++j) chk |= nw[j][ww] | (nw[j][ww] + 0x77777777u);  // bit 7 of a byte: >= 9
+      const bool clean = !(chk & 0x80808080u);
+      uint32_t I[3];
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        uint32_t s0w = nw[2 * a][ww], s1w = nw[2 * a + 1][ww];
+        if (!clean) {  // only with neighbour categories outside [0, kPottsQ]
+          s0w = clamp_bytes(s0w, kPottsQ);
+          s1w = clamp_bytes(s1w, kPottsQ);
+        }
+        I[a] = (s0w << 3) + s0w + s1w;
+      }
 #pragma unroll kPottsVUnroll
       for (int v = 0; v < 4; ++v) {
         float e[kPottsQ];
@@ -350,10 +374,9 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
         for (int k = 0; k < kPottsQ; ++k) e[k] = eb[k];
 #pragma unroll
         for (int a = 0; a < 3; ++a) {
-          const uint32_t s0 = min(__byte_perm(nw[2 * a][ww], 0u, 0x4440u + v), (uint32_t)kPottsQ);
-          const uint32_t s1 = min(__byte_perm(nw[2 * a + 1][ww], 0u, 0x4440u + v), (uint32_t)kPottsQ);
+          const uint32_t idx = __byte_perm(I[a], 0u, 0x4440u + v);
           const float4* pp = reinterpret_cast<const float4*>(
-              E + (size_t)((a * kRows + (int)s0) * kRows + (int)s1) * kExpRowFloats) + copy;
+              E + (size_t)(a * kRows * kRows + (int)idx) * kExpRowFloats) + copy;
           const float4 p0 = pp[0], p1 = pp[kExpCopies];
           e[0] = __fmul_rn(e[0], p0.x);
           e[1] = __fmul_rn(e[1], p0.y);
@@ -364,7 +387,7 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
           e[6] = __fmul_rn(e[6], p1.z);
           e[7] = __fmul_rn(e[7], p1.w);
         }
-        const float u = uniform_open(word_of(rr, v));
+        const float u = uniform_open_alu(word_of(rr, v));
         int cat = categorical_icdf_weights<kPottsQ>(e, u);
         if (cat < 0) cat = potts_theta_draw(nw, ww, v, J, bias, r, q, u);  // the weights underflowed
         out[ww] |= (uint32_t)cat << (8 * v);

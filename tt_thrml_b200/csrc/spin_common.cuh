@@ -8,13 +8,6 @@ namespace {
 
 constexpr int kTableBits = 8;  // neighbours folded into one partial-sum table
 
-// Open uniform (2m+1)/2^24, m = bits >> 9, built without an int->float
-// conversion: 1 + m/2^23 from the mantissa, minus (1 - 2^-24); both steps exact,
-// so the value equals uniform_open(bits) bit for bit.
-__device__ __forceinline__ float uniform_open_alu(uint32_t bits) {
-  return __uint_as_float(0x3F800000u | (bits >> 9)) - 0.99999994039535522461f;
-}
-
 // +1 with probability sigmoid(2*gamma): u * (1 + 2^(-2*gamma*log2(e))) < 1.
 __device__ __forceinline__ bool spin_up_fast(float gamma, uint32_t bits) {
   const float u = uniform_open_alu(bits);
