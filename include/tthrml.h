@@ -272,14 +272,17 @@ int tthrml_ising2d_halfsweep(int8_t* colour_state, const int8_t* other_state, in
  * sample i = per-chain sum of the spins of the colours in obs_colours (bit
  * mask) after half-sweep obs_first + i * obs_every.  A thrml schedule with
  * its magnetisation observable is one launch.  Requires n_chains % 32 == 0,
- * chain_offset % 8 == 0, even dimensions.
+ * chain_offset % 8 == 0, even dimensions.  Half-sweeps are separated by a
+ * bounded split-phase barrier in shared memory: on expiry *error_dev, when
+ * not NULL, receives a non-zero code and the remaining half-sweeps are
+ * skipped.
  */
 int tthrml_ising2d_resident(uint32_t* state_dev, int64_t n_chains, int32_t height, int32_t width,
                             int64_t row0_colour0, int64_t row0_colour1, const uint32_t* thresholds_dev,
                             uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
                             double* obs_dev, int64_t obs_first, int64_t obs_every, int64_t n_obs,
                             int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl_dev,
-                            void* stream);
+                            int32_t* error_dev, void* stream);
 
 /*
  * tthrml_ising2d_resident for count-symmetric threshold tables (the kernel
@@ -294,7 +297,7 @@ int tthrml_ising2d_resident_planes(uint32_t* state_dev, int64_t n_chains, int32_
                                    uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
                                    double* obs_dev, int64_t obs_first, int64_t obs_every, int64_t n_obs,
                                    int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl_dev,
-                                   void* stream);
+                                   int32_t* error_dev, void* stream);
 
 /*
  * Halo export of a strip-decomposed lattice (tthrml_ising2d_halfsweep_x):

@@ -149,12 +149,12 @@ _SIGNATURES = {
     "tthrml_ising2d_resident": (
         c_i32,
         [c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_u64, c_u32, c_i32, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32,
-         c_i64, c_vp, c_vp],
+         c_i64, c_vp, c_vp, c_vp],
     ),
     "tthrml_ising2d_resident_planes": (
         c_i32,
         [c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_u64, c_u32, c_i32, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32,
-         c_i64, c_vp, c_vp],
+         c_i64, c_vp, c_vp, c_vp],
     ),
     "tthrml_ctl_advance": (c_i32, [c_vp, c_u32, c_vp]),
     "tthrml_decode_rows": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp]),

@@ -170,9 +170,19 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t s
 // with T(n) from the top bit down; the result has a bit set where m >= T(n),
 // i.e. where the spin goes to -1.  The first TTHRML_PLANES_EAGER chunks of four
 // planes are drawn unconditionally, the rest only while some spin is tied.
-__device__ __forceinline__ uint32_t planes_decide(uint32_t L, uint32_t R, uint32_t U, uint32_t D,
-                                                  const uint32_t (*MS)[8], uint32_t c0, uint32_t c1, uint32_t sweep,
-                                                  const PhiloxKeys& keys) {
+// The eager chunks' Philox words of one word's draws (they depend on the counter only, so a kernel may
+// compute them before the state they decide is ready).
+__device__ __forceinline__ void planes_eager(u32x4 (&pre)[TTHRML_PLANES_EAGER], uint32_t c0, uint32_t c1,
+                                             uint32_t sweep, const PhiloxKeys& keys) {
+#pragma unroll
+  for (int ch = 0; ch < TTHRML_PLANES_EAGER; ++ch)
+    pre[ch] = philox4x32_10(u32x4{c0, c1, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
+}
+
+template <bool PRE>
+__device__ __forceinline__ uint32_t planes_decide_impl(uint32_t L, uint32_t R, uint32_t U, uint32_t D,
+                                                       const uint32_t (*MS)[8], const u32x4* pre, uint32_t c0,
+                                                       uint32_t c1, uint32_t sweep, const PhiloxKeys& keys) {
   // n = L + R + U + D in bit-planes n0, n1, n2 (n2 set only for n = 4)
   const uint32_t s1 = L ^ R, k1 = L & R, s2 = U ^ D, k2 = U & D;
   const uint32_t n0 = s1 ^ s2, t = s1 & s2;
@@ -187,7 +197,9 @@ __device__ __forceinline__ uint32_t planes_decide(uint32_t L, uint32_t R, uint32
   uint32_t lt = tbit(0);  // decided "m < T" (only T = 2^23 so far)
   uint32_t eq = ~lt;      // still tied with T
   auto planes4 = [&](int ch) {
-    const u32x4 r = philox4x32_10(u32x4{c0, c1, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
+    const u32x4 r = (PRE && ch < TTHRML_PLANES_EAGER)
+                        ? pre[ch]
+                        : philox4x32_10(u32x4{c0, c1, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int b = 4 * ch + q;
@@ -203,6 +215,20 @@ __device__ __forceinline__ uint32_t planes_decide(uint32_t L, uint32_t R, uint32
 #pragma unroll 1
   for (int ch = TTHRML_PLANES_EAGER; ch < 6 && eq; ++ch) planes4(ch);
   return ~lt;
+}
+
+__device__ __forceinline__ uint32_t planes_decide(uint32_t L, uint32_t R, uint32_t U, uint32_t D,
+                                                  const uint32_t (*MS)[8], uint32_t c0, uint32_t c1, uint32_t sweep,
+                                                  const PhiloxKeys& keys) {
+  return planes_decide_impl<false>(L, R, U, D, MS, nullptr, c0, c1, sweep, keys);
+}
+
+// planes_decide with the eager chunks' words given (planes_eager of the same counter).
+__device__ __forceinline__ uint32_t planes_decide_pre(uint32_t L, uint32_t R, uint32_t U, uint32_t D,
+                                                      const uint32_t (*MS)[8], const u32x4 (&pre)[TTHRML_PLANES_EAGER],
+                                                      uint32_t c0, uint32_t c1, uint32_t sweep,
+                                                      const PhiloxKeys& keys) {
+  return planes_decide_impl<true>(L, R, U, D, MS, pre, c0, c1, sweep, keys);
 }
 
 // Fills MS[24][8] (see planes_decide) from a 16-entry threshold table whose

@@ -27,6 +27,25 @@ namespace tthrml {
 namespace {
 
 constexpr int kResThreads = 512;
+constexpr uint32_t kResWaitLimit = 1u << 20;  // try_wait polls of the half-sweep barrier before giving up
+constexpr int32_t kErrHalfSweepWait = 5;       // error code: the half-sweep barrier never completed
+
+__device__ __forceinline__ uint32_t res_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Bounded wait for the completion of the phase of `bar` with the given parity.
+__device__ __forceinline__ bool res_bar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = res_smem_u32(bar);
+  for (uint32_t i = 0; i < kResWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
 
 __device__ __forceinline__ int wrapi(int i, int n) { return i < 0 ? i + n : (i >= n ? i - n : i); }
 
@@ -44,13 +63,14 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     uint32_t* state, int64_t C, int32_t H, int32_t W, int64_t row0_c0, int64_t row0_c1,
     const uint32_t* __restrict__ thresholds, uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half,
     double* __restrict__ obs, int64_t obs_first, int64_t obs_every, int64_t n_obs, int32_t obs_colours,
-    int64_t chain_offset, const tthrml_run_ctl* __restrict__ ctl, FastDiv div_hw) {
+    int64_t chain_offset, const tthrml_run_ctl* __restrict__ ctl, int32_t* __restrict__ error, FastDiv div_hw) {
   extern __shared__ __align__(16) unsigned char lat[];  // [2][H][W/2]
   __shared__ int32_t TH[16];   // threshold >> 7: compared with a draw's top 16 bits
   __shared__ uint32_t TL[16];  // threshold & 127: compared with the refill bits on a tie
   // PLANES: MS[i][n] = bit 23 - i of the count-n threshold as a 0 / ~0 mask
   __shared__ __align__(16) uint32_t MS[PLANES ? 24 : 1][8];
   __shared__ int counts[8];
+  __shared__ uint64_t half_bar;  // split-phase barrier between half-sweeps, one phase per half-sweep
   const int hw = W >> 1;
   const int half_sites = H * hw;
   const int g = blockIdx.x;  // chain group
@@ -61,6 +81,9 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
     TL[threadIdx.x] = thresholds[threadIdx.x] & 127u;
   }
   if (PLANES) planes_masks(MS, thresholds);
+  if (threadIdx.x == 0)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(res_smem_u32(&half_bar)), "r"((uint32_t)blockDim.x)
+                 : "memory");
   for (int i = threadIdx.x; i < 2 * half_sites; i += blockDim.x) {
     const int c = i / half_sites, r = i - c * half_sites;
     const int64_t row = (c ? row0_c1 : row0_c0) + r;
@@ -72,6 +95,17 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
   sweep0 += ctl ? ctl->sweep : 0u;
   const uint32_t gc0 = (uint32_t)(chain_offset + 8 * g);  // global index of the group's first chain
 
+  // Eager Philox words of this thread's first word of a half-sweep: they depend on the counter only, so
+  // the words of half-sweep t + 1 are drawn between arriving at and waiting on half-sweep t's barrier.
+  auto eager_for = [&](int64_t tt, u32x4 (&pre)[TTHRML_PLANES_EAGER]) {
+    const int cc = (int)((colour0 + tt) & 1);
+    const int64_t r0 = cc ? row0_c1 : row0_c0;
+    planes_eager(pre, gc0 >> 3, (uint32_t)((r0 + 4 * (int64_t)threadIdx.x) >> 2),
+                 sweep0 + (uint32_t)((colour0 + tt) >> 1), keys);
+  };
+  u32x4 pre[TTHRML_PLANES_EAGER];
+  if (PLANES && n_half > 0) eager_for(0, pre);
+  bool failed = false;
   int64_t next_obs = obs ? obs_first : -1, taken = 0;
   for (int64_t t = 0; t < n_half; ++t) {
     const int c = (int)((colour0 + t) & 1);
@@ -100,7 +134,9 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
           R = M;
         }
         const uint32_t quad = (uint32_t)((row0 + r) >> 2);
-        mw[q] = planes_decide(L, R, U, D, MS, gc0 >> 3, quad, sweep, keys);  // bit set: the chain's site samples -1
+        // bit set: the chain's site samples -1
+        mw[q] = q == (int)threadIdx.x ? planes_decide_pre(L, R, U, D, MS, pre, gc0 >> 3, quad, sweep, keys)
+                                      : planes_decide(L, R, U, D, MS, gc0 >> 3, quad, sweep, keys);
       }
     }
     for (int r = threadIdx.x; !PLANES && r < half_sites; r += blockDim.x) {
@@ -144,7 +180,12 @@ __global__ void __launch_bounds__(kResThreads) k_ising2d_resident(
       }
       mine[r] = (unsigned char)down;
     }
-    __syncthreads();
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(res_smem_u32(&half_bar)) : "memory");
+    if (PLANES && t + 1 < n_half) eager_for(t + 1, pre);
+    if (!failed && !res_bar_wait(&half_bar, (uint32_t)(t & 1))) {  // never expected: every thread arrives
+      failed = true;  // later phases are not waited for; every thread still arrives and meets every barrier
+      if (error) atomicExch(error, kErrHalfSweepWait);
+    }
     if (t + 1 == next_obs) {  // per-chain magnetisation after this half-sweep
       if (threadIdx.x < 8) counts[threadIdx.x] = 0;
       __syncthreads();
@@ -187,7 +228,8 @@ namespace {
 int resident_impl(uint32_t* state, int64_t n_chains, int32_t height, int32_t width, int64_t row0_colour0,
                   int64_t row0_colour1, const uint32_t* thresholds, uint64_t seed, uint32_t sweep0, int32_t colour0,
                   int64_t n_half_sweeps, double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
-                  int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl, void* stream, bool planes) {
+                  int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl, int32_t* error, void* stream,
+                  bool planes) {
   using namespace tthrml;
   if (!state || !thresholds || height <= 0 || width <= 0 || height % 2 || width % 2 || n_chains <= 0 ||
       n_chains % 32 || chain_offset % 8 || (colour0 != 0 && colour0 != 1) || n_half_sweeps < 0) {
@@ -220,7 +262,7 @@ int resident_impl(uint32_t* state, int64_t n_chains, int32_t height, int32_t wid
   if (n_half_sweeps == 0 && !obs) return TTHRML_OK;
   kernel<<<(unsigned)(n_chains / 8), kResThreads, (size_t)smem, (cudaStream_t)stream>>>(
       state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0, n_half_sweeps,
-      obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, make_fastdiv((uint32_t)(width / 2)));
+      obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, error, make_fastdiv((uint32_t)(width / 2)));
   return launch_status("k_ising2d_resident launch");
 }
 
@@ -231,9 +273,10 @@ extern "C" int tthrml_ising2d_resident(uint32_t* state, int64_t n_chains, int32_
                                        uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
                                        double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
                                        int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl,
-                                       void* stream) {
+                                       int32_t* error, void* stream) {
   return resident_impl(state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0,
-                       n_half_sweeps, obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, stream, false);
+                       n_half_sweeps, obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, error, stream,
+                       false);
 }
 
 extern "C" int tthrml_ising2d_resident_planes(uint32_t* state, int64_t n_chains, int32_t height, int32_t width,
@@ -241,7 +284,8 @@ extern "C" int tthrml_ising2d_resident_planes(uint32_t* state, int64_t n_chains,
                                               uint64_t seed, uint32_t sweep0, int32_t colour0, int64_t n_half_sweeps,
                                               double* obs, int64_t obs_first, int64_t obs_every, int64_t n_obs,
                                               int32_t obs_colours, int64_t chain_offset, const tthrml_run_ctl* ctl,
-                                              void* stream) {
+                                              int32_t* error, void* stream) {
   return resident_impl(state, n_chains, height, width, row0_colour0, row0_colour1, thresholds, seed, sweep0, colour0,
-                       n_half_sweeps, obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, stream, true);
+                       n_half_sweeps, obs, obs_first, obs_every, n_obs, obs_colours, chain_offset, ctl, error, stream,
+                       true);
 }

@@ -156,6 +156,9 @@ class Executor:
             self._global_state = torch.empty(
                 (self.compiled.total_nodes, self._row_len), dtype=self._torch_state_dtype, device=self._tdev
             )
+            if any(plan.kind == "ising2d_resident" for plan in self._plans()):
+                # set by the resident lattice kernel if its half-sweep barrier wait expired
+                self._error_word = torch.zeros(1, dtype=torch.int32, device=self._tdev)
         return self._global_state
 
     def _plans(self):
@@ -326,7 +329,7 @@ class Executor:
                 self._global_state.data_ptr(), self.n_chains, H, W, plan.block_rows[0], plan.block_rows[1],
                 plan.thresholds.data_ptr(), self._rng_buffers.seed, self._sweep_counter, 0, 2 * n_sweeps,
                 None if obs is None else obs.data_ptr(), obs_first, obs_every, n_obs, obs_colours,
-                self.chain_offset, None, nat.stream_handle(self._stream),
+                self.chain_offset, None, self._error_word.data_ptr(), nat.stream_handle(self._stream),
             ),
             fn,
         )
@@ -555,7 +558,7 @@ class Executor:
                 getattr(self._lib, fn)(
                     self._global_state.data_ptr(), self.n_chains, H, W, plan.block_rows[0], plan.block_rows[1],
                     plan.thresholds.data_ptr(), seed, sweep_idx, plan.colour, 1, None, 0, 0, 0, 0, self.chain_offset,
-                    ctl, stream,
+                    ctl, self._error_word.data_ptr(), stream,
                 ),
                 fn,
             )
@@ -713,12 +716,12 @@ class Executor:
         return int(self._ties[2].item())
 
     def check_device_errors(self) -> None:
-        """Raises if a kernel recorded an expired in-kernel wait (dense programs)."""
+        """Raises if a kernel recorded an expired in-kernel wait (dense and resident lattice programs)."""
         if self._error_word is not None:
             self._stream.synchronize()
             code = int(self._error_word.item())
             if code:
-                raise RuntimeError(f"tensor-core kernel reported an expired wait (code {code})")
+                raise RuntimeError(f"a device kernel reported an expired wait (code {code})")
 
     def raw_state(self) -> np.ndarray:
         """The whole state as host float32 [total_nodes, n_chains] values (spins +-1)."""
@@ -820,6 +823,8 @@ class Executor:
     def _block_states_host(self, block_indices) -> list[np.ndarray]:
         hosts = [self._decode_block(bi) for bi in block_indices]
         self._stream.synchronize()
+        if not self._dense:
+            self.check_device_errors()
         out = []
         for bi, h in zip(block_indices, hosts):
             spec = self.compiled.blocks[bi].spec
@@ -966,6 +971,7 @@ class Executor:
                                colours)
             with torch.cuda.stream(self._stream):
                 host = obs.cpu().numpy()
+            self.check_device_errors()
             return carry, (tree_expand(host[0]) if n_s <= 1 else host)
         if (device_side and self.config.cuda_graphs and not self.profile and schedule.n_samples >= 1
                 and callable(getattr(f_observe, "observe_capture", None))):
