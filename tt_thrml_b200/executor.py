@@ -820,6 +820,16 @@ class Executor:
         dev.record_stream(self._stream)
         return host
 
+    def _to_host(self, dev) -> np.ndarray:
+        """A device tensor as a numpy array, copied on the executor's stream into a pinned buffer from torch's
+        caching host allocator (the array keeps the buffer alive)."""
+        torch = _torch()
+        host = torch.empty(dev.shape, dtype=dev.dtype, pin_memory=True)
+        with torch.cuda.stream(self._stream):
+            host.copy_(dev, non_blocking=True)
+        self._stream.synchronize()
+        return host.numpy()
+
     def _block_states_host(self, block_indices) -> list[np.ndarray]:
         hosts = [self._decode_block(bi) for bi in block_indices]
         self._stream.synchronize()
@@ -969,8 +979,7 @@ class Executor:
                 obs = torch.empty((n_s, self.n_chains), dtype=torch.float64, device=self._tdev)
             self._run_resident(n_total, obs, 2 * int(schedule.n_warmup), 2 * int(schedule.steps_per_sample), n_s,
                                colours)
-            with torch.cuda.stream(self._stream):
-                host = obs.cpu().numpy()
+            host = self._to_host(obs)
             self.check_device_errors()
             return carry, (tree_expand(host[0]) if n_s <= 1 else host)
         if (device_side and self.config.cuda_graphs and not self.profile and schedule.n_samples >= 1
@@ -978,8 +987,7 @@ class Executor:
             # the whole schedule is one graph replay; observations stay on the device until the end
             carry = f_observe.prepare(self, carry)
             obs = self._run_schedule_graph(schedule, f_observe, carry)
-            with torch_stream(self._stream):
-                host = obs.cpu().numpy() if obs is not None else None
+            host = self._to_host(obs) if obs is not None else None
             finalize = getattr(f_observe, "finalize", None)
             if callable(finalize):
                 self._stream.synchronize()
