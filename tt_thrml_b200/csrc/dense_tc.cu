@@ -157,6 +157,9 @@ struct DenseArgs {
 // exact there).  The epilogue only records such decisions (a few in 10^5); k_dense_settle, launched
 // next on the same stream, decides them again and overwrites their outputs.
 constexpr float kNearTie = 1e-5f;
+#ifndef TTHRML_DENSE_F32X2
+#define TTHRML_DENSE_F32X2 1  // spin draws with packed f32x2 arithmetic (0: scalar)
+#endif
 #ifndef TTHRML_DENSE_SETTLE
 #define TTHRML_DENSE_SETTLE 2  // 0: no near-threshold check, 1: check only, 2: check and record
 #endif
@@ -255,6 +258,27 @@ __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (
       const uint32_t w[4] = {r.x, r.y, r.z, r.w};
       const float4 bq = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + n_first) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       const float b[4] = {bq.x, bq.y, bq.z, bq.w};
+#if TTHRML_DENSE_F32X2
+      // two units per packed instruction: t = u * (1 + 2^(-2 log2(e) field)), decided against 1
+#pragma unroll
+      for (int i = 0; i < 4; i += 2) {
+        const int j = 4 * q + i;
+        const float2 field = __fadd2_rn(make_float2(acc[j], acc[j + 1]), make_float2(b[i], b[i + 1]));
+        const float2 x = __fmul2_rn(field, make_float2(-2.8853900817779268f, -2.8853900817779268f));
+        float e0, e1;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(x.x));
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(x.y));
+        const float2 u = __fadd2_rn(make_float2(__uint_as_float(0x3F800000u | (w[i] >> 9)),
+                                                __uint_as_float(0x3F800000u | (w[i + 1] >> 9))),
+                                    make_float2(-0.99999994039535522461f, -0.99999994039535522461f));
+        const float2 t = __fmul2_rn(u, __fadd2_rn(make_float2(e0, e1), make_float2(1.0f, 1.0f)));
+        down |= ((t.x < 1.0f ? 0u : 1u) | (t.y < 1.0f ? 0u : 2u)) << j;
+        if (TTHRML_DENSE_SETTLE) {
+          const float2 d = __fadd2_rn(t, make_float2(-1.0f, -1.0f));
+          near |= ((fabsf(d.x) < kNearTie ? 1u : 0u) | (fabsf(d.y) < kNearTie ? 2u : 0u)) << j;
+        }
+      }
+#else
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int j = 4 * q + i;
@@ -263,6 +287,7 @@ __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (
         down |= (t < 1.0f ? 0u : 1u) << j;
         if (TTHRML_DENSE_SETTLE) near |= (fabsf(t - 1.0f) < kNearTie ? 1u : 0u) << j;
       }
+#endif
     }
   } else {
     float b[32];
