@@ -157,6 +157,9 @@ struct DenseArgs {
 // exact there).  The epilogue only records such decisions (a few in 10^5); k_dense_settle, launched
 // next on the same stream, decides them again and overwrites their outputs.
 constexpr float kNearTie = 1e-5f;
+#ifndef TTHRML_DENSE_FAST_TRIG
+#define TTHRML_DENSE_FAST_TRIG 1  // Box-Muller angle through the hardware sine / cosine (0: sincospif)
+#endif
 #ifndef TTHRML_DENSE_F32X2
 #define TTHRML_DENSE_F32X2 1  // spin draws with packed f32x2 arithmetic (0: scalar)
 #endif
@@ -311,9 +314,17 @@ __device__ __forceinline__ uint32_t spin_chunk(const DenseArgs& a, const float (
 __device__ __forceinline__ void box_muller_pair(uint32_t w0, uint32_t w1, float& xc, float& xs) {
   const float rad = sqrtf(-2.0f * logf(uniform_open(w0)));
   float sn, cs;
+#if TTHRML_DENSE_FAST_TRIG
+  // theta = 2 pi u1 = phi + pi with phi = 2 pi (u1 - 1/2) in (-pi, pi), where the hardware sine and cosine
+  // are accurate to ~5e-7 absolute: cos theta = -cos phi, sin theta = -sin phi
+  __sincosf(6.2831853071795865f * (uniform_open_alu(w1) - 0.5f), &sn, &cs);
+  xc = -rad * cs;
+  xs = -rad * sn;
+#else
   sincospif(2.0f * uniform_open(w1), &sn, &cs);
   xc = rad * cs;
   xs = rad * sn;
+#endif
 }
 
 // Gaussian epilogue of one 32-column chunk: field * var + sqrt(var) * xi, xi the unit's normal from the
