@@ -245,6 +245,10 @@ constexpr int kExpCopies = TTHRML_POTTS_EXP_COPIES;
 constexpr int kExpRowFloats = kExpCopies == 1 ? 12 : 2 * kExpCopies * 4;
 constexpr int kExpSmemBytes = 3 * kRows * kRows * kExpRowFloats * 4;
 
+#ifndef TTHRML_POTTS_F32X2
+#define TTHRML_POTTS_F32X2 1  // packed f32x2 category products (0: scalar)
+#endif
+
 // Bytes of x clamped to at most c (each byte unsigned).
 __device__ __forceinline__ uint32_t clamp_bytes(uint32_t x, uint32_t c) {
   uint32_t y = 0u;
@@ -378,6 +382,14 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
           const float4* pp = reinterpret_cast<const float4*>(
               E + (size_t)(a * kRows * kRows + (int)idx) * kExpRowFloats) + copy;
           const float4 p0 = pp[0], p1 = pp[kExpCopies];
+#if TTHRML_POTTS_F32X2  // two categories per packed multiply (each product rounded as alone)
+          const float2 q01 = __fmul2_rn(make_float2(e[0], e[1]), make_float2(p0.x, p0.y));
+          const float2 q23 = __fmul2_rn(make_float2(e[2], e[3]), make_float2(p0.z, p0.w));
+          const float2 q45 = __fmul2_rn(make_float2(e[4], e[5]), make_float2(p1.x, p1.y));
+          const float2 q67 = __fmul2_rn(make_float2(e[6], e[7]), make_float2(p1.z, p1.w));
+          e[0] = q01.x, e[1] = q01.y, e[2] = q23.x, e[3] = q23.y;
+          e[4] = q45.x, e[5] = q45.y, e[6] = q67.x, e[7] = q67.y;
+#else
           e[0] = __fmul_rn(e[0], p0.x);
           e[1] = __fmul_rn(e[1], p0.y);
           e[2] = __fmul_rn(e[2], p0.z);
@@ -386,6 +398,7 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
           e[5] = __fmul_rn(e[5], p1.y);
           e[6] = __fmul_rn(e[6], p1.z);
           e[7] = __fmul_rn(e[7], p1.w);
+#endif
         }
         const float u = uniform_open_alu(word_of(rr, v));
         int cat = categorical_icdf_weights<kPottsQ>(e, u);
