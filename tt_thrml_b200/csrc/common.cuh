@@ -170,6 +170,44 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t b, uint32_t s
 // with T(n) from the top bit down; the result has a bit set where m >= T(n),
 // i.e. where the spin goes to -1.  The first TTHRML_PLANES_EAGER chunks of four
 // planes are drawn unconditionally, the rest only while some spin is tied.
+// The bit-sliced decision of planes_decide in steps, for kernels that finish the rare undecided words
+// later (same planes in the same order, so the same result): PlaneState holds the neighbour-count
+// planes and the decided / tied masks; planes_chunk applies the four planes of Philox chunk ch.
+struct PlaneState {
+  uint32_t n0, n1, n2, lt, eq;
+};
+__device__ __forceinline__ uint32_t plane_tbit(const uint32_t (*MS)[8], const PlaneState& s, int i) {
+  const uint4 a = *reinterpret_cast<const uint4*>(&MS[i][0]);
+  const uint32_t m4 = MS[i][4];
+  const uint32_t lo = (s.n0 & a.y) | (~s.n0 & a.x), hi = (s.n0 & a.w) | (~s.n0 & a.z);
+  const uint32_t g = (s.n1 & hi) | (~s.n1 & lo);
+  return (s.n2 & m4) | (~s.n2 & g);
+}
+__device__ __forceinline__ void plane_counts(PlaneState& s, uint32_t L, uint32_t R, uint32_t U, uint32_t D) {
+  const uint32_t s1 = L ^ R, k1 = L & R, s2 = U ^ D, k2 = U & D;
+  const uint32_t t = s1 & s2;
+  s.n0 = s1 ^ s2;
+  s.n1 = k1 ^ k2 ^ t;
+  s.n2 = (k1 & k2) | (t & (k1 | k2));
+}
+__device__ __forceinline__ void planes_begin(PlaneState& s, uint32_t L, uint32_t R, uint32_t U, uint32_t D,
+                                             const uint32_t (*MS)[8]) {
+  plane_counts(s, L, R, U, D);
+  s.lt = plane_tbit(MS, s, 0);
+  s.eq = ~s.lt;
+}
+__device__ __forceinline__ void planes_chunk(PlaneState& s, const uint32_t (*MS)[8], const u32x4& r, int ch) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int b = 4 * ch + q;
+    if (b < 23) {
+      const uint32_t tb = plane_tbit(MS, s, b + 1), ub = word_of(r, q);
+      s.lt |= s.eq & tb & ~ub;
+      s.eq &= ~(tb ^ ub);
+    }
+  }
+}
+
 // The eager chunks' Philox words of one word's draws (they depend on the counter only, so a kernel may
 // compute them before the state they decide is ready).
 __device__ __forceinline__ void planes_eager(u32x4 (&pre)[TTHRML_PLANES_EAGER], uint32_t c0, uint32_t c1,

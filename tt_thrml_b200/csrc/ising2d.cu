@@ -39,6 +39,10 @@ namespace tthrml {
 namespace {
 
 constexpr int kIsingThreads = 256;
+#ifndef TTHRML_ISING_BITS_QUEUE
+#define TTHRML_ISING_BITS_QUEUE 1  // k_ising2d_bits: finish undecided words from a per-warp queue
+#endif
+constexpr int kBitsQueue = 64;  // queue slots per warp: fewer than 32 wait between drains, plus one word per lane
 #ifndef TTHRML_ISING_MIN_BLOCKS
 #define TTHRML_ISING_MIN_BLOCKS 3
 #endif
@@ -333,6 +337,9 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
     int64_t trace_len, tthrml_halo_export ex) {
   __shared__ __align__(16) uint32_t MS[24][8];
   __shared__ long long red[2];
+#if TTHRML_ISING_BITS_QUEUE
+  __shared__ uint32_t bits_queue[kIsingThreads / 32][7][kBitsQueue];
+#endif
   planes_masks(MS, thresholds);
   if (TRACE && threadIdx.x < 2) red[threadIdx.x] = 0;
   __syncthreads();
@@ -344,6 +351,123 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
   const uint32_t items = (uint32_t)(row_hi - row_lo) * (uint32_t)words;  // < 2^31, checked by the host
   long long mag = 0, bonds = 0;
 
+#if TTHRML_ISING_BITS_QUEUE
+  // Words whose 32 draws are not all decided after the first two Philox chunks (8 bit planes; about 12 %
+  // of words) are queued per warp and finished 32 at a time, so the rare third chunk runs with every
+  // lane busy instead of stalling whole warps; the planes and their order are those of planes_decide.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t (*q)[kBitsQueue] = bits_queue[warp];  // [L, R, U, D, lt, eq, item][slot]
+  int qn = 0;                                    // queued words of this warp (the same in every lane)
+  auto locate = [&](uint32_t it, int64_t& i, int64_t& w, int64_t& Y) {
+    const uint32_t ri = fdiv(it, div_words);
+    i = row_lo + ri;
+    w = (int64_t)(it - ri * (uint32_t)words);
+    Y = global_row0 + i;
+    if (Y >= height) Y -= height;
+    if (Y >= height) Y -= height;
+  };
+  auto finish = [&](uint32_t it, uint32_t L, uint32_t R, uint32_t U, uint32_t D, uint32_t dn) {
+    int64_t i, w, Y;
+    locate(it, i, w, Y);
+    if (TRACE && i >= count_lo && i < count_hi) {
+      const int nd = __popc(dn);
+      mag += 32 - 2 * nd;
+      if (colour == 1) {
+        const int ksum = __popc(L) + __popc(R) + __popc(U) + __popc(D);
+        const int mk = __popc(dn & L) + __popc(dn & R) + __popc(dn & U) + __popc(dn & D);
+        bonds += 4 * (32 - 2 * nd) - 2 * ksum + 4 * mk;
+      }
+    }
+    cc[i * words + w] = dn;
+    if (ex.rows) {  // boundary rows also go straight to the neighbours' mailboxes (peer memory)
+      const int64_t slot = (int64_t)(((sweep / ex.sweeps_per_period) + 1u) & 1u) * ex.slot_bytes;
+      bool sent = false;
+      if (ex.up && i >= ex.up_row0 && i < ex.up_row0 + ex.rows) {
+        reinterpret_cast<uint32_t*>(ex.up + slot)[(i - ex.up_row0) * words + w] = dn;
+        sent = true;
+      }
+      if (ex.down && i >= ex.down_row0 && i < ex.down_row0 + ex.rows) {
+        reinterpret_cast<uint32_t*>(ex.down + slot)[(i - ex.down_row0) * words + w] = dn;
+        sent = true;
+      }
+      if (sent) __threadfence_system();
+    }
+  };
+  auto drain = [&](int first, int n) {  // finish queue slots [first, first + n), one per lane
+    __syncwarp();
+    if (lane < n) {
+      const int k = first + lane;
+      const uint32_t L = q[0][k], R = q[1][k], U = q[2][k], D = q[3][k], it = q[6][k];
+      PlaneState st;
+      plane_counts(st, L, R, U, D);
+      st.lt = q[4][k];
+      st.eq = q[5][k];
+      int64_t i, w, Y;
+      locate(it, i, w, Y);
+      const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + 32 * w) >> 5);
+#pragma unroll 1
+      for (int ch = 2; ch < 6 && st.eq; ++ch)
+        planes_chunk(st, MS, philox4x32_10(u32x4{(uint32_t)chain, g32, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys),
+                     ch);
+      finish(it, L, R, U, D, ~st.lt);
+    }
+    __syncwarp();
+  };
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t it0 = blockIdx.x * blockDim.x + threadIdx.x - lane; it0 < items; it0 += stride) {
+    const uint32_t it = it0 + lane;
+    bool pend = false;
+    uint32_t L = 0u, R = 0u, U = 0u, D = 0u;
+    PlaneState st;
+    st.lt = 0u;
+    st.eq = 0u;
+    if (it < items) {
+      int64_t i, w, Y;
+      locate(it, i, w, Y);
+      const int p = (int)((Y + colour) & 1);
+      const int64_t iu = i == 0 ? (wrap ? rows_local - 1 : 0) : i - 1;
+      const int64_t id = i == rows_local - 1 ? (wrap ? 0 : i) : i + 1;
+      const uint32_t* rowc = co + i * words;
+      const uint32_t M = __ldg(rowc + w);
+      U = __ldg(co + iu * words + w);
+      D = __ldg(co + id * words + w);
+      if (p) {  // right neighbours: site 0 of the next word (bit 0) is the edge
+        L = M;
+        R = sites_plus1(M, __ldg(rowc + (w + 1 == words ? 0 : w + 1)) & 1u);
+      } else {  // left neighbours: site 31 of the previous word (bit 31) is the edge
+        L = sites_minus1(M, __ldg(rowc + (w == 0 ? words - 1 : w - 1)) >> 31);
+        R = M;
+      }
+      const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + 32 * w) >> 5);
+      planes_begin(st, L, R, U, D, MS);
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch)
+        planes_chunk(st, MS, philox4x32_10(u32x4{(uint32_t)chain, g32, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys),
+                     ch);
+      pend = st.eq != 0u;
+      if (!pend) finish(it, L, R, U, D, ~st.lt);  // bit set: -1
+    }
+    const uint32_t pm = __ballot_sync(0xffffffffu, pend);
+    if (pm) {
+      if (pend) {
+        const int k = qn + __popc(pm & ((1u << lane) - 1u));
+        q[0][k] = L;
+        q[1][k] = R;
+        q[2][k] = U;
+        q[3][k] = D;
+        q[4][k] = st.lt;
+        q[5][k] = st.eq;
+        q[6][k] = it;
+      }
+      qn += __popc(pm);
+      if (qn >= 32) {
+        drain(qn - 32, 32);
+        qn -= 32;
+      }
+    }
+  }
+  if (qn > 0) drain(0, qn);
+#else
   for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
     const uint32_t ri = fdiv(it, div_words);
     const int64_t i = row_lo + ri;
@@ -391,6 +515,7 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
       if (sent) __threadfence_system();
     }
   }
+#endif
   if (TRACE) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
