@@ -719,9 +719,22 @@ class Executor:
         """Raises if a kernel recorded an expired in-kernel wait (dense and resident lattice programs)."""
         if self._error_word is not None:
             self._stream.synchronize()
-            code = int(self._error_word.item())
-            if code:
-                raise RuntimeError(f"a device kernel reported an expired wait (code {code})")
+            self._raise_error_code(int(self._error_word.item()))
+
+    @staticmethod
+    def _raise_error_code(code: int) -> None:
+        if code:
+            raise RuntimeError(f"a device kernel reported an expired wait (code {code})")
+
+    def _error_copy(self):
+        """A pinned host copy of the device error word, queued on the executor's stream (None without one)."""
+        if self._error_word is None:
+            return None
+        torch = _torch()
+        host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        with torch.cuda.stream(self._stream):
+            host.copy_(self._error_word, non_blocking=True)
+        return host
 
     def raw_state(self) -> np.ndarray:
         """The whole state as host float32 [total_nodes, n_chains] values (spins +-1)."""
@@ -822,19 +835,24 @@ class Executor:
 
     def _to_host(self, dev) -> np.ndarray:
         """A device tensor as a numpy array, copied on the executor's stream into a pinned buffer from torch's
-        caching host allocator (the array keeps the buffer alive)."""
+        caching host allocator (the array keeps the buffer alive); raises if a kernel recorded an expired
+        wait (the error word travels with the same synchronisation)."""
         torch = _torch()
         host = torch.empty(dev.shape, dtype=dev.dtype, pin_memory=True)
         with torch.cuda.stream(self._stream):
             host.copy_(dev, non_blocking=True)
+        err = self._error_copy()
         self._stream.synchronize()
+        if err is not None:
+            self._raise_error_code(int(err[0]))
         return host.numpy()
 
     def _block_states_host(self, block_indices) -> list[np.ndarray]:
         hosts = [self._decode_block(bi) for bi in block_indices]
+        err = None if self._dense else self._error_copy()
         self._stream.synchronize()
-        if not self._dense:
-            self.check_device_errors()
+        if err is not None:
+            self._raise_error_code(int(err[0]))
         out = []
         for bi, h in zip(block_indices, hosts):
             spec = self.compiled.blocks[bi].spec
@@ -980,7 +998,6 @@ class Executor:
             self._run_resident(n_total, obs, 2 * int(schedule.n_warmup), 2 * int(schedule.steps_per_sample), n_s,
                                colours)
             host = self._to_host(obs)
-            self.check_device_errors()
             return carry, (tree_expand(host[0]) if n_s <= 1 else host)
         if (device_side and self.config.cuda_graphs and not self.profile and schedule.n_samples >= 1
                 and callable(getattr(f_observe, "observe_capture", None))):
