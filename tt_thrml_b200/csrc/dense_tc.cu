@@ -1041,7 +1041,8 @@ int dense_field_sample(const void* source_state, const void* weights_nk, int64_t
     set_error("tthrml_dense_field_sample: NULL argument");
     return TTHRML_ERR_ARG;
   }
-  if (ties && (ties_capacity < 1 || ties_capacity > 0x7fffffff || ((uintptr_t)ties % 16))) {
+  if (ties && (ties_capacity < 1 || ties_capacity > 0x7fffffff || ((uintptr_t)ties % 16) ||
+               n_units > 0xffffffffLL)) {  // entries hold 32-bit unit indices
     set_error("tthrml_dense_field_sample_ties: ties must be 16-byte aligned with 1 <= capacity < 2^31 (got %lld)",
               (long long)ties_capacity);
     return TTHRML_ERR_ARG;
