@@ -1043,8 +1043,8 @@ int dense_field_sample(const void* source_state, const void* weights_nk, int64_t
   }
   if (ties && (ties_capacity < 1 || ties_capacity > 0x7fffffff || ((uintptr_t)ties % 16) ||
                n_units > 0xffffffffLL)) {  // entries hold 32-bit unit indices
-    set_error("tthrml_dense_field_sample_ties: ties must be 16-byte aligned with 1 <= capacity < 2^31 (got %lld)",
-              (long long)ties_capacity);
+    set_error("tthrml_dense_field_sample_ties: ties must be 16-byte aligned with 1 <= capacity < 2^31 and "
+              "n_units < 2^32 (got capacity %lld, n_units %lld)", (long long)ties_capacity, (long long)n_units);
     return TTHRML_ERR_ARG;
   }
   if (n_chains <= 0 || n_units <= 0 || n_sources <= 0 || n_chains % BM || n_units % BN || n_sources % BK) {
