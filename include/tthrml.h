@@ -206,6 +206,19 @@ int tthrml_spin_bits_step(const int64_t* row_ptr_dev, const int32_t* cols_dev, c
                           void* stream);
 
 /*
+ * tthrml_spin_bits_step with the block's rows processed in the order given
+ * by row_order_dev (int32 [n_rows], a permutation of 0..n_rows-1, e.g. rows
+ * sorted by degree so that the rows handled side by side need equally many
+ * neighbour terms).  The order changes only which rows run together, not
+ * any sample: every row's field, draw and Philox counter are its own.
+ */
+int tthrml_spin_bits_step_ordered(const int64_t* row_ptr_dev, const int32_t* cols_dev, const float* vals_dev,
+                                  const float* bias_dev, int64_t row_start, int64_t n_rows, uint32_t* state_dev,
+                                  int64_t n_chains, int64_t chain_offset, const float* variates_dev,
+                                  int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                                  const tthrml_run_ctl* ctl_dev, const int32_t* row_order_dev, void* stream);
+
+/*
  * Checkerboard colour block of a q-state Potts model on a periodic X x Y x Z
  * lattice (q <= 8; one q x q matrix per axis).  Replaces the group kernel of
  * the categorical block (tt_thrml/compiler.py:289-344) for lattice programs:

@@ -103,6 +103,10 @@ _SIGNATURES = {
         c_i32,
         [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp, c_vp],
     ),
+    "tthrml_spin_bits_step_ordered": (
+        c_i32,
+        [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_u64, c_u32, c_vp, c_vp, c_vp],
+    ),
     "tthrml_dense_field_sample": (
         c_i32,
         [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, ctypes.c_float, c_vp, c_vp, c_i32, c_i64, c_i64, c_vp,

@@ -410,6 +410,9 @@ class SpinCSRBlock:
     vals: Any
     bias: Any
     nnz: int
+    # rows in processing order for the bit-packed kernel: sorted by degree, so the two rows a warp
+    # handles together need equally many neighbour terms (the order does not change any sample)
+    row_order: Any = None
 
 
 @dataclass
@@ -563,6 +566,7 @@ def _plan_spin_csr(group, specs, tables_by_block, device) -> SpinCSRGroupPlan:
                 vals=_to_dev(vals.astype(np.float32), device),
                 bias=None if bias is None else _to_dev(bias, device),
                 nnz=int(rp[-1]),
+                row_order=_to_dev(np.argsort(np.diff(rp), kind="stable").astype(np.int32), device),
             )
         )
     return SpinCSRGroupPlan(

@@ -221,7 +221,8 @@ int launch_bits(const int64_t* rp, const int32_t* cols, const float* vals, const
 template <bool VARIATES>
 int launch_bits16(const int64_t* rp, const int32_t* cols, const float* vals, const float* bias, int64_t row_start,
                   int64_t n_rows, uint32_t* state, int64_t W, int64_t chain_offset, const float* variates,
-                  int64_t variates_sweeps, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, cudaStream_t s);
+                  int64_t variates_sweeps, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl,
+                  const int32_t* row_order, cudaStream_t s);
 
 }  // namespace tthrml
 
@@ -229,11 +230,11 @@ int launch_bits16(const int64_t* rp, const int32_t* cols, const float* vals, con
 #define TTHRML_BITS16 1
 #endif
 
-extern "C" int tthrml_spin_bits_step(const int64_t* row_ptr, const int32_t* cols, const float* vals,
-                                     const float* bias, int64_t row_start, int64_t n_rows, uint32_t* state,
-                                     int64_t n_chains, int64_t chain_offset, const float* variates,
-                                     int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
-                                     const tthrml_run_ctl* ctl, void* stream) {
+namespace {
+int spin_bits_step(const int64_t* row_ptr, const int32_t* cols, const float* vals, const float* bias,
+                   int64_t row_start, int64_t n_rows, uint32_t* state, int64_t n_chains, int64_t chain_offset,
+                   const float* variates, int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                   const tthrml_run_ctl* ctl, const int32_t* row_order, void* stream) {
   using namespace tthrml;
   if (n_rows == 0) return TTHRML_OK;
   if (!row_ptr || !cols || !vals || !state || n_rows < 0 || row_start < 0) {
@@ -254,13 +255,36 @@ extern "C" int tthrml_spin_bits_step(const int64_t* row_ptr, const int32_t* cols
   if (TTHRML_BITS16) {
     if (variates)
       return launch_bits16<true>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
-                                 variates_sweeps, seed, sweep, ctl, s);
+                                 variates_sweeps, seed, sweep, ctl, row_order, s);
     return launch_bits16<false>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
-                                variates_sweeps, seed, sweep, ctl, s);
+                                variates_sweeps, seed, sweep, ctl, row_order, s);
   }
   if (variates)
     return launch_bits<true>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
                              variates_sweeps, seed, sweep, ctl, s);
   return launch_bits<false>(row_ptr, cols, vals, bias, row_start, n_rows, state, W, chain_offset, variates,
                             variates_sweeps, seed, sweep, ctl, s);
+}
+}  // namespace
+
+extern "C" int tthrml_spin_bits_step(const int64_t* row_ptr, const int32_t* cols, const float* vals,
+                                     const float* bias, int64_t row_start, int64_t n_rows, uint32_t* state,
+                                     int64_t n_chains, int64_t chain_offset, const float* variates,
+                                     int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                                     const tthrml_run_ctl* ctl, void* stream) {
+  return spin_bits_step(row_ptr, cols, vals, bias, row_start, n_rows, state, n_chains, chain_offset, variates,
+                        variates_sweeps, seed, sweep, ctl, nullptr, stream);
+}
+
+extern "C" int tthrml_spin_bits_step_ordered(const int64_t* row_ptr, const int32_t* cols, const float* vals,
+                                             const float* bias, int64_t row_start, int64_t n_rows, uint32_t* state,
+                                             int64_t n_chains, int64_t chain_offset, const float* variates,
+                                             int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                                             const tthrml_run_ctl* ctl, const int32_t* row_order, void* stream) {
+  if (!row_order) {
+    tthrml::set_error("tthrml_spin_bits_step_ordered: NULL row order");
+    return TTHRML_ERR_ARG;
+  }
+  return spin_bits_step(row_ptr, cols, vals, bias, row_start, n_rows, state, n_chains, chain_offset, variates,
+                        variates_sweeps, seed, sweep, ctl, row_order, stream);
 }

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kB16Threads, TTHRML_BITS16_MIN_BLOCKS) k_spin_
     const int64_t* __restrict__ row_ptr, const int32_t* __restrict__ cols, const float* __restrict__ vals,
     const float* __restrict__ bias, int64_t row_start, int64_t n_rows, uint32_t* state, int64_t W,
     int64_t chain_offset, const float* __restrict__ variates, int64_t variates_sweeps, uint64_t seed,
-    uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl) {
+    uint32_t sweep_base, const tthrml_run_ctl* __restrict__ ctl, const int32_t* __restrict__ row_order) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31, h = lane >> 4, lh = lane & 15;
   unsigned char* hbuf = smem + (size_t)((threadIdx.x >> 5) * 2 + h) * kB16HalfBytes;
@@ -132,25 +132,31 @@ __global__ void __launch_bounds__(kB16Threads, TTHRML_BITS16_MIN_BLOCKS) k_spin_
   const uint64_t sd = ctl ? ctl->seed : seed;
   const PhiloxKeys keys = philox_keys(seed_lo(sd), seed_hi(sd));
   const unsigned char* state_bytes = reinterpret_cast<const unsigned char*>(state);
-  auto row_of = [&](int64_t it) -> int64_t { return slices == 1 ? it : (int64_t)((uint64_t)it / (uint64_t)slices); };
+  // item -> (row, slice): items of one row are consecutive; row_order (if given) lists the block's rows
+  // in processing order (rows of equal degree side by side keep a warp's two half-warps in step)
+  auto row_of = [&](int64_t it) -> int64_t {
+    const int64_t ri = slices == 1 ? it : (int64_t)((uint64_t)it / (uint64_t)slices);
+    return row_order && it < items ? (int64_t)__ldg(row_order + ri) : ri;
+  };
+  auto slice_of = [&](int64_t it) -> int64_t { return slices == 1 ? 0 : (int64_t)((uint64_t)it % (uint64_t)slices); };
 
   Row16 cur, nxt;
   load_row16(row_of(item), item < items, row_ptr, cols, vals, bias, lh, cur);
   int stage = 0;
-  issue_rows16(cur, (item - cur.r * slices) * 8, item < items, state, W, hbuf, lh);
+  issue_rows16(cur, slice_of(item) * 8, item < items, state, W, hbuf, lh);
   cp_async_commit();
   int64_t next = item + stride;
   load_row16(row_of(next), next < items, row_ptr, cols, vals, bias, lh, nxt);
 
   while (__any_sync(kFull, item < items)) {
     const bool valid = item < items;
-    issue_rows16(nxt, (next - nxt.r * slices) * 8, next < items, state, W, hbuf + (stage ^ 1) * kB16StageBytes,
+    issue_rows16(nxt, slice_of(next) * 8, next < items, state, W, hbuf + (stage ^ 1) * kB16StageBytes,
                  lh);
     cp_async_commit();
     Row16 after;
     load_row16(row_of(next + stride), next + stride < items, row_ptr, cols, vals, bias, lh, after);
 
-    const int64_t slice = item - cur.r * slices;
+    const int64_t slice = slice_of(item);
     const int64_t c0 = slice * 256 + lh * 16;           // first chain of this lane
     const int64_t byte0 = slice * kB16Slice + lh * 2;   // this lane's two bytes within a row
     const int64_t row = row_start + cur.r;
@@ -248,7 +254,8 @@ __global__ void __launch_bounds__(kB16Threads, TTHRML_BITS16_MIN_BLOCKS) k_spin_
 template <bool VARIATES>
 int launch_bits16(const int64_t* rp, const int32_t* cols, const float* vals, const float* bias, int64_t row_start,
                   int64_t n_rows, uint32_t* state, int64_t W, int64_t chain_offset, const float* variates,
-                  int64_t variates_sweeps, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, cudaStream_t s) {
+                  int64_t variates_sweeps, uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl,
+                  const int32_t* row_order, cudaStream_t s) {
   constexpr int smem = (kB16Threads / 16) * kB16HalfBytes;
   static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
   if (!per_sm) {
@@ -266,15 +273,16 @@ int launch_bits16(const int64_t* rp, const int32_t* cols, const float* vals, con
   const int64_t full = (int64_t)sms * per_sm;
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
   k_spin_bits16<VARIATES><<<grid, kB16Threads, smem, s>>>(rp, cols, vals, bias, row_start, n_rows, state, W,
-                                                          chain_offset, variates, variates_sweeps, seed, sweep, ctl);
+                                                          chain_offset, variates, variates_sweeps, seed, sweep, ctl,
+                                                          row_order);
   return launch_status("k_spin_bits16 launch");
 }
 
 template int launch_bits16<true>(const int64_t*, const int32_t*, const float*, const float*, int64_t, int64_t,
                                  uint32_t*, int64_t, int64_t, const float*, int64_t, uint64_t, uint32_t,
-                                 const tthrml_run_ctl*, cudaStream_t);
+                                 const tthrml_run_ctl*, const int32_t*, cudaStream_t);
 template int launch_bits16<false>(const int64_t*, const int32_t*, const float*, const float*, int64_t, int64_t,
                                   uint32_t*, int64_t, int64_t, const float*, int64_t, uint64_t, uint32_t,
-                                  const tthrml_run_ctl*, cudaStream_t);
+                                  const tthrml_run_ctl*, const int32_t*, cudaStream_t);
 
 }  // namespace tthrml

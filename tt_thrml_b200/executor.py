@@ -576,26 +576,33 @@ class Executor:
                 "tthrml_potts3d_step",
             )
         elif plan.kind in ("spin_csr", "spin_bits"):
-            step = self._lib.tthrml_spin_bits_step if plan.kind == "spin_bits" else self._lib.tthrml_spin_csr_step
+            bits = plan.kind == "spin_bits"
             for blk in plan.blocks:
                 v = self._variates(blk.block_index)
                 vptr = None if v is None else v.data_ptr()
+                args = [
+                    blk.row_ptr.data_ptr(),
+                    blk.cols.data_ptr(),
+                    blk.vals.data_ptr(),
+                    None if blk.bias is None else blk.bias.data_ptr(),
+                    blk.row_start,
+                    blk.n_rows,
+                    self._global_state.data_ptr(),
+                    self.n_chains,
+                    self.chain_offset,
+                    vptr,
+                    self._rng_n_sweeps if v is not None else 0,
+                    seed,
+                    sweep_idx,
+                    ctl,
+                ]
+                if bits and blk.row_order is not None:
+                    step, args = self._lib.tthrml_spin_bits_step_ordered, args + [blk.row_order.data_ptr()]
+                else:
+                    step = self._lib.tthrml_spin_bits_step if bits else self._lib.tthrml_spin_csr_step
                 nat.check(
                     step(
-                        blk.row_ptr.data_ptr(),
-                        blk.cols.data_ptr(),
-                        blk.vals.data_ptr(),
-                        None if blk.bias is None else blk.bias.data_ptr(),
-                        blk.row_start,
-                        blk.n_rows,
-                        self._global_state.data_ptr(),
-                        self.n_chains,
-                        self.chain_offset,
-                        vptr,
-                        self._rng_n_sweeps if v is not None else 0,
-                        seed,
-                        sweep_idx,
-                        ctl,
+                        *args,
                         stream,
                     ),
                     plan.kind,
