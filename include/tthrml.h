@@ -240,6 +240,22 @@ int tthrml_potts3d_step(int8_t* state_dev, int64_t n_chains, int32_t X, int32_t 
                         uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl_dev, void* stream);
 
 /*
+ * The per-site bias weights e^(b_k - max b) of a q = 8 Potts block, computed
+ * once (they do not change between sweeps): bias and bias_weights are float32
+ * [n_sites][8], 16-byte aligned.  tthrml_potts3d_step_weights is
+ * tthrml_potts3d_step reading these weights instead of recomputing them per
+ * site and sweep (the same values, so the same samples; the raw bias is still
+ * read when a chain's weights underflow).
+ */
+int tthrml_potts3d_bias_weights(const float* bias_dev, int64_t n_sites, int32_t q, float* bias_weights_dev,
+                                void* stream);
+int tthrml_potts3d_step_weights(int8_t* state_dev, int64_t n_chains, int32_t X, int32_t Y, int32_t Z,
+                                int32_t colour, int64_t target_row0, int64_t source_row0, const float* J_dev,
+                                const float* bias_dev, int32_t q, int64_t chain_offset, const float* variates_dev,
+                                int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                                const tthrml_run_ctl* ctl_dev, const float* bias_weights_dev, void* stream);
+
+/*
  * One checkerboard half-sweep of a single-chain 2-D Ising lattice (uniform
  * couplings) on split-colour int8 state.  Replaces the spin group kernel
  * (tt_thrml/compiler.py:303-324) for lattice programs, where neighbours follow

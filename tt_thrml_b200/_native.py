@@ -122,6 +122,12 @@ _SIGNATURES = {
         [c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i64, c_vp, c_i64, c_u64, c_u32,
          c_vp, c_vp],
     ),
+    "tthrml_potts3d_step_weights": (
+        c_i32,
+        [c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i64, c_vp, c_i64, c_u64, c_u32,
+         c_vp, c_vp, c_vp],
+    ),
+    "tthrml_potts3d_bias_weights": (c_i32, [c_vp, c_i64, c_i32, c_vp, c_vp]),
     "tthrml_ising2d_halfsweep": (
         c_i32,
         [c_vp, c_vp, c_i64, c_i64, c_i32, c_i64, c_i64, c_i64, c_i64, c_i32, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,

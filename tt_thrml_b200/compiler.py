@@ -847,6 +847,7 @@ class PottsStencilGroupPlan:
     source_row0: int
     J: Any  # float32 [3][q][q] device tensor
     bias: Any  # float32 [n_rows][q] device tensor (target block rows)
+    bias_w: Any = None  # float32 [n_rows][8] e^(b - max b) per site (q = 8), made by the executor
     family: Family = Family.CATEGORICAL
     family_label: str = "categorical"
     kind: str = "potts3d"

@@ -249,6 +249,38 @@ constexpr int kExpSmemBytes = 3 * kRows * kRows * kExpRowFloats * 4;
 #define TTHRML_POTTS_F32X2 1  // packed f32x2 category products (0: scalar)
 #endif
 
+// e^(b_k - max b) of one site's bias row (16-byte loads; the host checks the alignment), k < q, else 0.
+__device__ __forceinline__ void site_bias_weights(const float* __restrict__ bias, int64_t r, int32_t q,
+                                                  float (&eb)[kPottsQ]) {
+  float b[kPottsQ];
+  const float4* bp = reinterpret_cast<const float4*>(bias + (size_t)r * kPottsQ);
+  const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
+  b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+  float mb = b[0];
+#pragma unroll
+  for (int k = 1; k < kPottsQ; ++k)
+    if (k < q) mb = fmaxf(mb, b[k]);
+  const float ml = mb * 1.44269502162933349609375f;
+#pragma unroll
+  for (int k = 0; k < kPottsQ; ++k) {
+    float v = 0.0f;
+    if (k < q) asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(__fmaf_rn(b[k], 1.44269502162933349609375f, -ml)));
+    eb[k] = v;
+  }
+}
+
+// The bias weights of every site once (they do not change between sweeps): the sweep kernel then reads
+// e^(b - max b) instead of computing it per site and launch, with the same values.
+__global__ void k_potts_bias_weights(const float* __restrict__ bias, int64_t n, int32_t q, float* __restrict__ w) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+    float eb[kPottsQ];
+    site_bias_weights(bias, r, q, eb);
+    float4* dst = reinterpret_cast<float4*>(w + (size_t)r * kPottsQ);
+    dst[0] = make_float4(eb[0], eb[1], eb[2], eb[3]);
+    dst[1] = make_float4(eb[4], eb[5], eb[6], eb[7]);
+  }
+}
+
 // Bytes of x clamped to at most c (each byte unsigned).
 __device__ __forceinline__ uint32_t clamp_bytes(uint32_t x, uint32_t c) {
   uint32_t y = 0u;
@@ -262,7 +294,7 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
     int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, FastDiv div_words, FastDiv div_x, FastDiv div_y,
     int32_t colour, int64_t target_row0, int64_t source_row0, const float* __restrict__ J,
     const float* __restrict__ bias, int32_t q, int64_t chain_offset, uint64_t seed, uint32_t sweep_base,
-    const tthrml_run_ctl* __restrict__ ctl) {
+    const tthrml_run_ctl* __restrict__ ctl, const float* __restrict__ bias_w) {
   extern __shared__ __align__(16) float E[];  // [3][kRows][kRows][2][kExpCopies][4]
   for (int row = threadIdx.x; row < 3 * kRows * kRows; row += blockDim.x) {
     const int s1 = row % kRows, s0 = (row / kRows) % kRows, a = row / (kRows * kRows);
@@ -328,24 +360,14 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
         nw[j][0] = __ldg(src);
       }
     }
-    // the site's bias row (16-byte loads; the host checks the alignment) as e^(b_k - max b)
+    // the site's bias row as e^(b_k - max b): from the precomputed table, or computed here
     float eb[kPottsQ];
-    {
-      float b[kPottsQ];
-      const float4* bp = reinterpret_cast<const float4*>(bias + (size_t)r * kPottsQ);
-      const float4 b0 = __ldg(bp), b1 = __ldg(bp + 1);
-      b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
-      float mb = b[0];
-#pragma unroll
-      for (int k = 1; k < kPottsQ; ++k)
-        if (k < q) mb = fmaxf(mb, b[k]);
-      const float ml = mb * 1.44269502162933349609375f;
-#pragma unroll
-      for (int k = 0; k < kPottsQ; ++k) {
-        float v = 0.0f;
-        if (k < q) asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(v) : "f"(__fmaf_rn(b[k], 1.44269502162933349609375f, -ml)));
-        eb[k] = v;
-      }
+    if (bias_w) {
+      const float4* wp = reinterpret_cast<const float4*>(bias_w + (size_t)r * kPottsQ);
+      const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+      eb[0] = w0.x, eb[1] = w0.y, eb[2] = w0.z, eb[3] = w0.w, eb[4] = w1.x, eb[5] = w1.y, eb[6] = w1.z, eb[7] = w1.w;
+    } else {
+      site_bias_weights(bias, r, q, eb);
     }
 
     const int64_t row = target_row0 + r;
@@ -417,7 +439,7 @@ __global__ void __launch_bounds__(kPottsThreads, TTHRML_POTTS_EXP_MINB) k_potts3
 template <int WPT>
 int launch_potts_exp(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int32_t colour, int64_t target_row0,
                      int64_t source_row0, const float* J, const float* bias, int32_t q, int64_t chain_offset,
-                     uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, cudaStream_t s) {
+                     uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, const float* bias_w, cudaStream_t s) {
   static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
   if (!per_sm) {
     int dev = 0, n = 0, b = 0;
@@ -437,7 +459,8 @@ int launch_potts_exp(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, 
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
   k_potts3d_exp<WPT><<<grid, kPottsThreads, kExpSmemBytes, s>>>(
       state, C, X, Y, Z, make_fastdiv((uint32_t)(C / (4 * WPT))), make_fastdiv((uint32_t)X),
-      make_fastdiv((uint32_t)Y), colour, target_row0, source_row0, J, bias, q, chain_offset, seed, sweep, ctl);
+      make_fastdiv((uint32_t)Y), colour, target_row0, source_row0, J, bias, q, chain_offset, seed, sweep, ctl,
+      bias_w);
   return launch_status("k_potts3d_exp launch");
 }
 
@@ -472,10 +495,11 @@ int launch_potts(int8_t* state, int64_t C, int32_t X, int32_t Y, int32_t Z, int3
 }  // namespace
 }  // namespace tthrml
 
-extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, int32_t Y, int32_t Z, int32_t colour,
-                                   int64_t target_row0, int64_t source_row0, const float* J, const float* bias,
-                                   int32_t q, int64_t chain_offset, const float* variates, int64_t variates_sweeps,
-                                   uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, void* stream) {
+namespace {
+int potts3d_step(int8_t* state, int64_t n_chains, int32_t X, int32_t Y, int32_t Z, int32_t colour,
+                 int64_t target_row0, int64_t source_row0, const float* J, const float* bias, int32_t q,
+                 int64_t chain_offset, const float* variates, int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                 const tthrml_run_ctl* ctl, const float* bias_w, void* stream) {
   using namespace tthrml;
   if (!state || !J || !bias || X <= 0 || Y <= 0 || Z <= 0 || (X | Y | Z) & 1 || (colour != 0 && colour != 1)) {
     set_error("tthrml_potts3d_step: invalid arguments (dimensions must be positive and even, colour 0 or 1)");
@@ -514,7 +538,7 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
   if (!variates && q8 && TTHRML_POTTS_EXP) {
     return (wide ? launch_potts_exp<TTHRML_POTTS_WPT> : launch_potts_exp<1>)(state, n_chains, X, Y, Z, colour,
                                                                              target_row0, source_row0, J, bias, q,
-                                                                             chain_offset, seed, sweep, ctl, s);
+                                                                             chain_offset, seed, sweep, ctl, bias_w, s);
   }
   if (variates) {
     if (q8) TTHRML_POTTS_LAUNCH(true, kPottsQ);
@@ -523,4 +547,42 @@ extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, i
   if (q8) TTHRML_POTTS_LAUNCH(false, kPottsQ);
   TTHRML_POTTS_LAUNCH(false, 0);
 #undef TTHRML_POTTS_LAUNCH
+}
+}  // namespace
+
+extern "C" int tthrml_potts3d_step(int8_t* state, int64_t n_chains, int32_t X, int32_t Y, int32_t Z, int32_t colour,
+                                   int64_t target_row0, int64_t source_row0, const float* J, const float* bias,
+                                   int32_t q, int64_t chain_offset, const float* variates, int64_t variates_sweeps,
+                                   uint64_t seed, uint32_t sweep, const tthrml_run_ctl* ctl, void* stream) {
+  return potts3d_step(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset, variates,
+                      variates_sweeps, seed, sweep, ctl, nullptr, stream);
+}
+
+extern "C" int tthrml_potts3d_step_weights(int8_t* state, int64_t n_chains, int32_t X, int32_t Y, int32_t Z,
+                                           int32_t colour, int64_t target_row0, int64_t source_row0, const float* J,
+                                           const float* bias, int32_t q, int64_t chain_offset, const float* variates,
+                                           int64_t variates_sweeps, uint64_t seed, uint32_t sweep,
+                                           const tthrml_run_ctl* ctl, const float* bias_weights, void* stream) {
+  if (!bias_weights || ((uintptr_t)bias_weights % 16)) {
+    tthrml::set_error("tthrml_potts3d_step_weights: bias_weights must be a 16-byte aligned device array");
+    return TTHRML_ERR_ARG;
+  }
+  return potts3d_step(state, n_chains, X, Y, Z, colour, target_row0, source_row0, J, bias, q, chain_offset, variates,
+                      variates_sweeps, seed, sweep, ctl, bias_weights, stream);
+}
+
+extern "C" int tthrml_potts3d_bias_weights(const float* bias, int64_t n_sites, int32_t q, float* bias_weights,
+                                           void* stream) {
+  using namespace tthrml;
+  if (!bias || !bias_weights || n_sites < 0 || q != kPottsQ || ((uintptr_t)bias % 16) ||
+      ((uintptr_t)bias_weights % 16)) {
+    set_error("tthrml_potts3d_bias_weights: q must be %d and both arrays 16-byte aligned [n_sites][%d]", kPottsQ,
+              kPottsQ);
+    return TTHRML_ERR_ARG;
+  }
+  if (n_sites == 0) return TTHRML_OK;
+  const int64_t blocks = (n_sites + 255) / 256;
+  k_potts_bias_weights<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, (cudaStream_t)stream>>>(bias, n_sites, q,
+                                                                                                   bias_weights);
+  return launch_status("k_potts_bias_weights launch");
 }

@@ -159,6 +159,19 @@ class Executor:
             if any(plan.kind == "ising2d_resident" for plan in self._plans()):
                 # set by the resident lattice kernel if its half-sweep barrier wait expired
                 self._error_word = torch.zeros(1, dtype=torch.int32, device=self._tdev)
+            for plan in self._plans():
+                if plan.kind == "potts3d" and plan.q == 8 and plan.bias_w is None:
+                    # e^(b - max b) per site, once: the q = 8 sweep kernel reads it instead of recomputing
+                    with torch.cuda.stream(self._stream):
+                        plan.bias_w = torch.empty_like(plan.bias)
+                    nat.bind_device(self._tdev.index)
+                    nat.check(
+                        self._lib.tthrml_potts3d_bias_weights(
+                            plan.bias.data_ptr(), plan.bias.shape[0], plan.q, plan.bias_w.data_ptr(),
+                            nat.stream_handle(self._stream),
+                        ),
+                        "tthrml_potts3d_bias_weights",
+                    )
         return self._global_state
 
     def _plans(self):
@@ -566,15 +579,17 @@ class Executor:
             bi = plan.block_indices[0]
             v = self._variates(bi)
             X, Y, Z = plan.dims
-            nat.check(
-                self._lib.tthrml_potts3d_step(
-                    self._global_state.data_ptr(), self.n_chains, X, Y, Z, plan.colour, plan.target_row0,
-                    plan.source_row0, plan.J.data_ptr(), plan.bias.data_ptr(), plan.q, self.chain_offset,
-                    None if v is None else v.data_ptr(), self._rng_n_sweeps if v is not None else 0, seed, sweep_idx,
-                    ctl, stream,
-                ),
-                "tthrml_potts3d_step",
-            )
+            args = [
+                self._global_state.data_ptr(), self.n_chains, X, Y, Z, plan.colour, plan.target_row0,
+                plan.source_row0, plan.J.data_ptr(), plan.bias.data_ptr(), plan.q, self.chain_offset,
+                None if v is None else v.data_ptr(), self._rng_n_sweeps if v is not None else 0, seed, sweep_idx,
+                ctl,
+            ]
+            if plan.bias_w is not None:
+                nat.check(self._lib.tthrml_potts3d_step_weights(*args, plan.bias_w.data_ptr(), stream),
+                          "tthrml_potts3d_step_weights")
+            else:
+                nat.check(self._lib.tthrml_potts3d_step(*args, stream), "tthrml_potts3d_step")
         elif plan.kind in ("spin_csr", "spin_bits"):
             bits = plan.kind == "spin_bits"
             for blk in plan.blocks:
