@@ -99,6 +99,33 @@ def test_generic_and_spin_csr_paths_agree_bit_for_bit(cuda_device):
     np.testing.assert_array_equal(outs[0], outs[1])
 
 
+def test_degree_ordered_rows_give_the_same_samples(cuda_device):
+    """The bit-packed kernel runs each colour block's rows sorted by degree; the order changes no sample."""
+    prog = workloads.erdos_renyi_ising(5000, 8.0, seed=4)
+    C = 256
+    outs = []
+    cfg = make_cuda_config(n_chains=C)
+    for ordered in (True, False):
+        # an uncached compile: the plan objects changed below are this executor's alone
+        comp = compile_program(None, 0, prog, cfg, n_sweeps=6, n_chains=C, cache=False)
+        ex = Executor(None, 0, prog, cfg, comp, n_sweeps=6, n_chains=C)
+        plans = [g.kernel_artifact for g in ex.compiled.sampling_groups]
+        assert {p.kind for p in plans} == {"spin_bits"}
+        for plan in plans:
+            for blk in plan.blocks:
+                order = blk.row_order.cpu().numpy()
+                deg = np.diff(blk.row_ptr.cpu().numpy())
+                assert sorted(order.tolist()) == list(range(blk.n_rows))
+                assert np.all(np.diff(deg[order]) >= 0)
+                if not ordered:
+                    blk.row_order = None  # natural order through tthrml_spin_bits_step
+        ex.load_state(gh.random_init(prog, C, 7), [])
+        ex.prepare_rng(13)
+        ex.run_sweeps(6)
+        outs.append(gh.gpu_state(ex))
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("C", [256, 512])
 def test_bit_packed_and_int8_layouts_agree_bit_for_bit(cuda_device, C):
     prog = workloads.erdos_renyi_ising(3000, 9.0, seed=8)
