@@ -196,3 +196,65 @@ def test_rbm_and_potts_generators_reproduce_the_configuration_inputs():
     np.testing.assert_array_equal(raw["J"], prog.J)
     np.testing.assert_array_equal(raw["bias"], prog.site_bias)
     assert raw["dims"] == prog.dims
+
+
+def test_dense_gaussian_draws_follow_the_paired_box_muller_layout():
+    """The dense path's Philox gaussians, restated independently: counter (chain, row / 4, sweep, "DGAU"), words
+    2p, 2p + 1 give rows 4j + 2p (r cos theta) and 4j + 2p + 1 (r sin theta); value = field / (1 + 1e-6) +
+    sqrt(1 / (1 + 1e-6)) * normal, field = b_v + W h in double."""
+    from ising_ref import philox4x32_10
+
+    V, H, C, seed, sweep = 12, 16, 5, 0x0123_4567_89AB_CDEF, 3
+    rng = np.random.default_rng(8)
+    W = (0.05 * rng.standard_normal((V, H))).astype(np.float32)
+    b_v = (0.2 * rng.standard_normal(V)).astype(np.float32)
+    prog = models.dense_bipartite(W, b_v, np.zeros(H, np.float32))
+    o = orc.OracleSampler(prog, n_chains=C, rng_layout="row4")
+    h = rng.integers(0, 2, (C, H)).astype(bool)
+    o.load_state([rng.standard_normal((C, V)).astype(np.float32), h])
+    o.group_step(1, sweep, seed=seed)  # the visible (gaussian) block; sampling order: hidden, visible
+    got = o.state[:V].astype(np.float64)  # [V][C]
+
+    field = b_v.astype(np.float64)[:, None] + W.astype(np.float64) @ np.where(h, 1.0, -1.0).T  # [V][C]
+    rows = np.arange(V)[:, None] + np.zeros((1, C), dtype=np.int64)  # the visible block starts at row 0
+    chains = np.zeros((V, 1), dtype=np.int64) + np.arange(C)[None, :]
+    words = np.stack(philox4x32_10(chains, rows >> 2, np.full_like(rows, sweep), np.full_like(rows, 0x44474155),
+                                   seed & 0xFFFFFFFF, seed >> 32), axis=0)  # [4][V][C]
+    p = (rows >> 1) & 1
+    w0 = np.take_along_axis(words, (2 * p)[None], 0)[0]
+    w1 = np.take_along_axis(words, (2 * p + 1)[None], 0)[0]
+    uniform = lambda w: ((w >> 9) * 2 + 1).astype(np.float64) * 2.0**-24  # noqa: E731
+    rad, theta = np.sqrt(-2.0 * np.log(uniform(w0))), 2.0 * np.pi * uniform(w1)
+    xi = np.where(rows & 1, rad * np.sin(theta), rad * np.cos(theta))
+    inv = 1.0 / (1.0 + 1e-6)
+    want = field * inv + np.sqrt(inv) * xi
+    np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-6)
+
+
+def test_dense_spin_draws_follow_the_row4_layout():
+    """The dense path's Philox spins, restated independently: word row % 4 of counter (chain, row / 4, sweep,
+    "DSPI"); +1 where 2 field > logit(u), field = b_h + W^T v in double (row = V + unit for the hidden block)."""
+    from ising_ref import philox4x32_10
+
+    V, H, C, seed, sweep = 8, 20, 6, 0x00FE_DCBA_9876_5432, 5
+    rng = np.random.default_rng(9)
+    W = (0.3 * rng.standard_normal((V, H))).astype(np.float32)
+    b_h = (0.2 * rng.standard_normal(H)).astype(np.float32)
+    prog = models.dense_bipartite(W, np.zeros(V, np.float32), b_h)
+    o = orc.OracleSampler(prog, n_chains=C, rng_layout="row4")
+    v = rng.standard_normal((C, V)).astype(np.float32)
+    o.load_state([v, rng.integers(0, 2, (C, H)).astype(bool)])
+    margins = o.group_step(0, sweep, seed=seed, return_margin=True)  # the hidden (spin) block
+    got = o.state[V:]  # [H][C], +-1
+
+    field = b_h.astype(np.float64)[:, None] + W.astype(np.float64).T @ v.astype(np.float64).T  # [H][C]
+    rows = V + np.arange(H)[:, None] + np.zeros((1, C), dtype=np.int64)
+    chains = np.zeros((H, 1), dtype=np.int64) + np.arange(C)[None, :]
+    words = np.stack(philox4x32_10(chains, rows >> 2, np.full_like(rows, sweep), np.full_like(rows, 0x44535049),
+                                   seed & 0xFFFFFFFF, seed >> 32), axis=0)
+    u = ((np.take_along_axis(words, (rows & 3)[None], 0)[0] >> 9) * 2 + 1).astype(np.float64) * 2.0**-24
+    margin = 2.0 * field - (np.log(u) - np.log1p(-u))
+    want = np.where(margin > 0, 1.0, -1.0)
+    tie = np.abs(margin) < 1e-5
+    assert np.all((got == want) | tie)
+    np.testing.assert_allclose(np.abs(np.asarray(margins)).reshape(H, C), np.abs(margin), rtol=1e-9, atol=1e-9)
