@@ -221,17 +221,18 @@ class GaussBernoulliRBM(Workload):
         flops = 2.0 * 2.0 * C * self.V * self.H * n_prof  # two GEMMs per sweep
         achieved = flops / (sum(kernel_ms) / 1000.0) / 1e12
         peaks = _peaks()
-        peak, kind = peaks["bf16"]
+        # the launches are timed inside long graph-replayed steps under the power cap: the sustained GEMM peak
+        peak, kind = peaks["bf16_sustained"]
         return {
-            # the timed group call covers the GEMM and, for spin blocks, the near-threshold settle kernel
+            # the group launches cover the GEMM and, for spin blocks, the near-threshold settle kernel
             "kernel": ("k_dense_field_sample_pair" if C % 256 == 0 else "k_dense_field_sample") + " + k_dense_settle",
             "bound": "tensor",
             "achieved": achieved,
             "peak": peak,
             "unit": "TFLOP/s",
             "frac": achieved / peak,
-            "peak_source": kind + " burst (kernels timed launch by launch)",
-            "frac_of_sustained": achieved / peaks["bf16_sustained"][0],
+            "peak_source": kind + " sustained (launches timed inside the long step)",
+            "frac_of_burst": achieved / peaks["bf16"][0],
             "traffic": _dense_traffic_per_launch(),
             "algorithmic_flops_per_update": 2.0 * 2.0 * self.V * self.H / (self.V + self.H),
         }
@@ -702,15 +703,23 @@ def run_chain_sharded(ctx, args, W, steps, warmup, cpu):
     # group kernels + the run-control advance of each graph, or one launch per step (resident lattice)
     gpu_launches = steps * (1 if resident else S * n_group_launches + 1)
 
-    # ---- roofline: per-launch CUDA events on the launch stream (eager sweeps)
+    # ---- roofline: the average launch duration over the timed region (graph-replayed steps, events on the
+    # launch stream): step time / group launches per step.  Per-launch events around eager sweeps are kept
+    # as a cross-check; they also count the GPU's wait for each eager launch.
+    n_prof = 5
+    n_sites = len(ex.compiled.sampling_groups)
+    timed_ms = [dt_ms / steps / (S * n_sites)] * (n_sites * n_prof)
+    roofline = W.roofline(ex, prog, C, timed_ms, n_prof, dt_ms / steps)
     ex.profile = True
     ex._timing_log.clear()
-    n_prof = 5
     for _ in range(n_prof):
         ex.run_sweep()
     ex.profile = False
     kernel_ms = [kms for _, _, kms in ex._timing_log]
-    roofline = W.roofline(ex, prog, C, kernel_ms, n_prof, dt_ms / steps)
+    eager = W.roofline(ex, prog, C, kernel_ms, n_prof, dt_ms / steps)
+    roofline["duration_source"] = ("timed region: step time / launches per step" if not resident
+                                   else "timed region: step time (one launch per step)")
+    roofline["eager_launch_frac"] = eager["frac"]
 
     # ---- end to end through the public API (pinned host state in, results out)
     host_init = W.host_inputs(init)
