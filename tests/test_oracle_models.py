@@ -258,3 +258,43 @@ def test_dense_spin_draws_follow_the_row4_layout():
     tie = np.abs(margin) < 1e-5
     assert np.all((got == want) | tie)
     np.testing.assert_allclose(np.abs(np.asarray(margins)).reshape(H, C), np.abs(margin), rtol=1e-9, atol=1e-9)
+
+
+def test_sparse_spin_draws_follow_the_chain4_layout():
+    """The sparse (table) path's Philox spins, restated independently: field = beta h + (sequential float32 sum of
+    beta J s over the node's CSR entries); word chain % 4 of counter (chain / 4, flat row, sweep, "SPIN");
+    +1 where 2 field > logit(u)."""
+    from ising_ref import philox4x32_10
+
+    raw = models.er_ising_raw(400, 6.0, seed=11)
+    prog = models.graph_ising(raw["row_ptr"], raw["cols"], raw["J"], raw["h"], raw["colours"], raw["beta"])
+    C, seed, sweep, chain_offset = 12, 0x0BAD_CAFE_1234_5678, 7, 8
+    o = orc.OracleSampler(prog, n_chains=C, rng_layout="chain4", chain_offset=chain_offset)
+    rng = np.random.default_rng(12)
+    o.load_state([rng.integers(0, 2, (C, b.n_nodes)).astype(bool) for b in prog.blocks])
+    before = o.state.copy()  # [flat rows][C], +-1
+    margins = np.asarray(o.group_step(0, sweep, seed=seed, return_margin=True))
+    after = o.state
+
+    colours, rp, cols = np.asarray(raw["colours"]), raw["row_ptr"], raw["cols"]
+    order = np.concatenate([np.flatnonzero(colours == k) for k in range(int(colours.max()) + 1)])
+    flat = np.empty_like(order)
+    flat[order] = np.arange(order.size)
+    b32 = np.float32(raw["beta"])
+    wJ = (b32 * raw["J"].astype(np.float32)).astype(np.float32)
+    wh = (b32 * raw["h"].astype(np.float32)).astype(np.float32)
+    members = np.flatnonzero(colours == 0)
+    for c in range(C):
+        gc = chain_offset + c
+        for idx, node in enumerate(members):
+            acc = None
+            for e in range(rp[node], rp[node + 1]):
+                term = np.float32(wJ[e] * np.float32(before[flat[cols[e]], c]))
+                acc = term if acc is None else np.float32(acc + term)
+            field = wh[node] if acc is None else np.float32(wh[node] + acc)
+            row = flat[node]
+            words = philox4x32_10(gc >> 2, row, sweep, 0x5350494E, seed & 0xFFFFFFFF, seed >> 32)
+            u = ((int(words[gc & 3]) >> 9) * 2 + 1) * 2.0**-24
+            margin = 2.0 * float(field) - (np.log(u) - np.log1p(-u))
+            assert after[row, c] == (1.0 if margin > 0 else -1.0)
+            assert abs(abs(margins.reshape(-1, C)[idx, c]) - abs(margin)) < 1e-9
