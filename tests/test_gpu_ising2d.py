@@ -303,3 +303,41 @@ def test_resident_lattice_samples_the_same_law_as_the_table_kernel(cuda_device):
                                           init_state_free=init)
         res.append(np.abs(m).mean() / 512.0)
     assert abs(res[0] - res[1]) < 0.02, res
+
+
+@pytest.mark.parametrize("W,offset", [(64, 0), (128, 0), (192, 0), (256, 0), (384, 0), (512, 1), (512, 2)])
+def test_bit_packed_halfsweep_any_word_count(cuda_device, W, offset):
+    """tthrml_ising2d_halfsweep_bits takes 4, 2 or 1 words per thread by the row's word count and the
+    other colour's alignment (offset: words before the buffer's start); every choice evolves the same
+    lattice as the int8 kernel tthrml_ising2d_halfsweep_planes on the same draws, whole lattice, wrapped."""
+    import torch
+
+    from tt_thrml_b200 import _native as nat
+    from tt_thrml_b200.compiler import ising_pattern_tables
+
+    H, seed, n_sweeps = 16, 0x1234_5678_9ABC, 3
+    prog = workloads.IsingLattice2D(H, W, beta=0.4407)
+    st = prog.tt_stencil()
+    _, thr = ising_pattern_tables(st["edge_weight"], st["site_bias"])
+    thresholds = torch.from_numpy(thr.view(np.int32)).to(cuda_device)
+    lib, stream = nat.lib(), nat.stream_handle(torch.cuda.current_stream(cuda_device))
+    rng = np.random.default_rng(W + offset)
+    int8 = [torch.from_numpy(rng.choice(np.array([-1, 1], np.int8), (H, W // 2))).to(cuda_device) for _ in range(2)]
+    words = W // 64
+    bits = []
+    for c in range(2):
+        buf = torch.zeros(offset + H * words, dtype=torch.int32, device=cuda_device)
+        view = buf[offset:].view(H, words)
+        view.copy_(LatticeStrips.pack_rows(int8[c]))
+        bits.append((buf, view))
+    for sweep in range(n_sweeps):
+        for c in range(2):
+            args = (W, H, 1, 0, H, 0, H, c, int(st["block_rows"][c]), thresholds.data_ptr(), 0, seed, sweep, None,
+                    0, H, None, 0, None, stream)
+            nat.check(lib.tthrml_ising2d_halfsweep_planes(int8[c].data_ptr(), int8[1 - c].data_ptr(), *args),
+                      "tthrml_ising2d_halfsweep_planes")
+            nat.check(lib.tthrml_ising2d_halfsweep_bits(bits[c][1].data_ptr(), bits[1 - c][1].data_ptr(), *args),
+                      "tthrml_ising2d_halfsweep_bits")
+            torch.cuda.synchronize(cuda_device)
+            assert torch.equal(LatticeStrips.unpack_rows(bits[c][1]), int8[c]), (sweep, c)
+    assert all(int(b[0][:offset].abs().sum()) == 0 for b in bits)  # nothing written before the rows

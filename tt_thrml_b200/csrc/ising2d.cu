@@ -49,6 +49,12 @@ constexpr int kBitsQueue = 64;  // queue slots per warp: fewer than 32 wait betw
 #ifndef TTHRML_ISING_PLANES_MIN_BLOCKS
 #define TTHRML_ISING_PLANES_MIN_BLOCKS 3
 #endif
+#ifndef TTHRML_ISING_BITS_WORDS
+#define TTHRML_ISING_BITS_WORDS 4  // k_ising2d_bits: most words per thread where rows allow (1, 2 or 4)
+#endif
+#ifndef TTHRML_ISING_BITS2_MIN_BLOCKS
+#define TTHRML_ISING_BITS2_MIN_BLOCKS 2  // k_ising2d_bits with two or four words per thread
+#endif
 
 __device__ __forceinline__ uint4 ld16(const int8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
@@ -327,9 +333,15 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
 // edge bit comes from the neighbouring word of the middle row, and the
 // decision and random bits are those of k_ising2d_planes, so both kernels
 // produce the same lattice.  Rows are 8x smaller than int8 rows and need no
-// sign gathering; the halo export stores words.
-template <bool TRACE>
-__global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS) k_ising2d_bits(
+// sign gathering; the halo export stores words.  With NW = 4 (rows of a
+// multiple of 4 words, 16-byte aligned; else NW = 2 for an even number of
+// 8-byte aligned words) a thread takes NW adjacent words of a row: one vector
+// load each of the middle, up and down rows and one edge word serve all of
+// them, the row arithmetic is shared, and the words' Philox and plane chains
+// are independent work for the same warp slot.
+template <bool TRACE, int NW>
+__global__ void __launch_bounds__(kIsingThreads, NW >= 2 ? TTHRML_ISING_BITS2_MIN_BLOCKS : TTHRML_ISING_PLANES_MIN_BLOCKS)
+    k_ising2d_bits(
     uint32_t* __restrict__ cc, const uint32_t* __restrict__ co, int64_t words, FastDiv div_words, int64_t rows_local,
     int32_t wrap, int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
     int64_t block_row0, const uint32_t* __restrict__ thresholds, int64_t chain, uint64_t seed, uint32_t sweep_base,
@@ -414,60 +426,111 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
     __syncwarp();
   };
   const uint32_t stride = gridDim.x * blockDim.x;
-  for (uint32_t it0 = blockIdx.x * blockDim.x + threadIdx.x - lane; it0 < items; it0 += stride) {
-    const uint32_t it = it0 + lane;
-    bool pend = false;
-    uint32_t L = 0u, R = 0u, U = 0u, D = 0u;
-    PlaneState st;
-    st.lt = 0u;
-    st.eq = 0u;
-    if (it < items) {
+  const uint32_t groups = items / NW;  // words % NW == 0 (the launcher's choice)
+  for (uint32_t g0 = blockIdx.x * blockDim.x + threadIdx.x - lane; g0 < groups; g0 += stride) {
+    const uint32_t it = (g0 + lane) * NW;  // this lane's first word
+    bool pend[NW];
+    uint32_t L[NW], R[NW], U[NW], D[NW];
+    PlaneState st[NW];
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      pend[k] = false;
+      L[k] = R[k] = U[k] = D[k] = 0u;
+      st[k].lt = 0u;
+      st[k].eq = 0u;
+    }
+    if (g0 + lane < groups) {
       int64_t i, w, Y;
       locate(it, i, w, Y);
       const int p = (int)((Y + colour) & 1);
       const int64_t iu = i == 0 ? (wrap ? rows_local - 1 : 0) : i - 1;
       const int64_t id = i == rows_local - 1 ? (wrap ? 0 : i) : i + 1;
       const uint32_t* rowc = co + i * words;
-      const uint32_t M = __ldg(rowc + w);
-      U = __ldg(co + iu * words + w);
-      D = __ldg(co + id * words + w);
-      if (p) {  // right neighbours: site 0 of the next word (bit 0) is the edge
-        L = M;
-        R = sites_plus1(M, __ldg(rowc + (w + 1 == words ? 0 : w + 1)) & 1u);
-      } else {  // left neighbours: site 31 of the previous word (bit 31) is the edge
-        L = sites_minus1(M, __ldg(rowc + (w == 0 ? words - 1 : w - 1)) >> 31);
-        R = M;
+      uint32_t M[NW];
+      if constexpr (NW == 4) {
+        const uint4 m = __ldg(reinterpret_cast<const uint4*>(rowc + w));
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(co + iu * words + w));
+        const uint4 d = __ldg(reinterpret_cast<const uint4*>(co + id * words + w));
+        const uint32_t mv[4] = {m.x, m.y, m.z, m.w}, uv[4] = {u.x, u.y, u.z, u.w}, dv[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+        for (int k = 0; k < NW; ++k) {
+          M[k] = mv[k];
+          U[k] = uv[k];
+          D[k] = dv[k];
+        }
+      } else if constexpr (NW == 2) {
+        const uint2 m = __ldg(reinterpret_cast<const uint2*>(rowc + w));
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(co + iu * words + w));
+        const uint2 d = __ldg(reinterpret_cast<const uint2*>(co + id * words + w));
+        M[0] = m.x;
+        M[1] = m.y;
+        U[0] = u.x;
+        U[1] = u.y;
+        D[0] = d.x;
+        D[1] = d.y;
+      } else {
+        M[0] = __ldg(rowc + w);
+        U[0] = __ldg(co + iu * words + w);
+        D[0] = __ldg(co + id * words + w);
       }
+      if (p) {  // right neighbours: site 0 of the next word (bit 0) is the edge
+        const uint32_t edge = __ldg(rowc + (w + NW == words ? 0 : w + NW));
+#pragma unroll
+        for (int k = 0; k < NW; ++k) {
+          L[k] = M[k];
+          R[k] = sites_plus1(M[k], (k + 1 < NW ? M[(k + 1) % NW] : edge) & 1u);
+        }
+      } else {  // left neighbours: site 31 of the previous word (bit 31) is the edge
+        const uint32_t edge = __ldg(rowc + (w == 0 ? words - 1 : w - 1));
+#pragma unroll
+        for (int k = 0; k < NW; ++k) {
+          L[k] = sites_minus1(M[k], (k > 0 ? M[(k + NW - 1) % NW] : edge) >> 31);
+          R[k] = M[k];
+        }
+      }
+      // word w + k draws from counter g32 + k: (x + 32k) >> 5 = (x >> 5) + k
       const uint32_t g32 = (uint32_t)((block_row0 + Y * half_w + 32 * w) >> 5);
-      planes_begin(st, L, R, U, D, MS);
+#pragma unroll
+      for (int k = 0; k < NW; ++k) planes_begin(st[k], L[k], R[k], U[k], D[k], MS);
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch)
-        planes_chunk(st, MS, philox4x32_10(u32x4{(uint32_t)chain, g32, sweep, kSaltLatticePlanes + (uint32_t)ch}, keys),
-                     ch);
-      pend = st.eq != 0u;
-      if (!pend) finish(it, L, R, U, D, ~st.lt);  // bit set: -1
-    }
-    const uint32_t pm = __ballot_sync(0xffffffffu, pend);
-    if (pm) {
-      if (pend) {
-        const int k = qn + __popc(pm & ((1u << lane) - 1u));
-        q[0][k] = L;
-        q[1][k] = R;
-        q[2][k] = U;
-        q[3][k] = D;
-        q[4][k] = st.lt;
-        q[5][k] = st.eq;
-        q[6][k] = it;
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+          planes_chunk(st[k], MS,
+                       philox4x32_10(u32x4{(uint32_t)chain, g32 + (uint32_t)k, sweep, kSaltLatticePlanes + (uint32_t)ch},
+                                     keys),
+                       ch);
+#pragma unroll
+      for (int k = 0; k < NW; ++k) {
+        pend[k] = st[k].eq != 0u;
+        if (!pend[k]) finish(it + k, L[k], R[k], U[k], D[k], ~st[k].lt);  // bit set: -1
       }
-      qn += __popc(pm);
-      if (qn >= 32) {
-        drain(qn - 32, 32);
-        qn -= 32;
+    }
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      const uint32_t pm = __ballot_sync(0xffffffffu, pend[k]);
+      if (pm) {
+        if (pend[k]) {
+          const int slot = qn + __popc(pm & ((1u << lane) - 1u));
+          q[0][slot] = L[k];
+          q[1][slot] = R[k];
+          q[2][slot] = U[k];
+          q[3][slot] = D[k];
+          q[4][slot] = st[k].lt;
+          q[5][slot] = st[k].eq;
+          q[6][slot] = it + k;
+        }
+        qn += __popc(pm);
+        if (qn >= 32) {
+          drain(qn - 32, 32);
+          qn -= 32;
+        }
       }
     }
   }
   if (qn > 0) drain(0, qn);
 #else
+  static_assert(NW == 1, "two words per thread need the queued loop");
   for (uint32_t it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
     const uint32_t ri = fdiv(it, div_words);
     const int64_t i = row_lo + ri;
@@ -534,32 +597,55 @@ __global__ void __launch_bounds__(kIsingThreads, TTHRML_ISING_PLANES_MIN_BLOCKS)
   }
 }
 
-template <bool TRACE>
-int launch_ising_bits(uint32_t* cc, const uint32_t* co, int64_t words, int64_t rows_local, int32_t wrap,
-                      int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
-                      int64_t block_row0, const uint32_t* thresholds, int64_t chain, uint64_t seed, uint32_t sweep,
-                      const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi, unsigned long long* trace,
-                      int64_t trace_len, const tthrml_halo_export& ex, cudaStream_t s) {
+template <bool TRACE, int NW>
+int launch_ising_bits_nw(uint32_t* cc, const uint32_t* co, int64_t words, int64_t rows_local, int32_t wrap,
+                         int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
+                         int64_t block_row0, const uint32_t* thresholds, int64_t chain, uint64_t seed, uint32_t sweep,
+                         const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi, unsigned long long* trace,
+                         int64_t trace_len, const tthrml_halo_export& ex, cudaStream_t s) {
   static int per_sm = 0, sms = 0;  // same values from every thread: a benign race
   if (!per_sm) {
     int dev = 0, n = 0, b = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_ising2d_bits<TRACE>, kIsingThreads, 0);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_ising2d_bits<TRACE, NW>, kIsingThreads, 0);
     if (e != cudaSuccess) return cuda_status(e, "k_ising2d_bits set-up");
     sms = n;
     per_sm = b > 0 ? b : 1;
   }
-  const int64_t items = (row_hi - row_lo) * words;
-  const int64_t need = (items + kIsingThreads - 1) / kIsingThreads;
+  const int64_t groups = (row_hi - row_lo) * words / NW;
+  const int64_t need = (groups + kIsingThreads - 1) / kIsingThreads;
   const int64_t full = (int64_t)sms * per_sm;
   const int grid = (int)(need < full ? (need > 0 ? need : 1) : full);
-  k_ising2d_bits<TRACE><<<grid, kIsingThreads, 0, s>>>(cc, co, words, make_fastdiv((uint32_t)words), rows_local, wrap,
-                                                      row_lo, row_hi, global_row0, height, colour, block_row0,
-                                                      thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace,
-                                                      trace_len, ex);
+  k_ising2d_bits<TRACE, NW><<<grid, kIsingThreads, 0, s>>>(
+      cc, co, words, make_fastdiv((uint32_t)words), rows_local, wrap, row_lo, row_hi, global_row0, height, colour,
+      block_row0, thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace, trace_len, ex);
   return launch_status("k_ising2d_bits launch");
+}
+
+// four (or two) words per thread where the rows' word count and alignment allow
+template <bool TRACE>
+int launch_ising_bits(uint32_t* cc, const uint32_t* co, int64_t words, int64_t rows_local, int32_t wrap,
+                      int64_t row_lo, int64_t row_hi, int64_t global_row0, int64_t height, int32_t colour,
+                      int64_t block_row0, const uint32_t* thresholds, int64_t chain, uint64_t seed, uint32_t sweep,
+                      const tthrml_run_ctl* ctl, int64_t count_lo, int64_t count_hi, unsigned long long* trace,
+                      int64_t trace_len, const tthrml_halo_export& ex, cudaStream_t s) {
+#if TTHRML_ISING_BITS_QUEUE && TTHRML_ISING_BITS_WORDS == 4
+  if (words % 4 == 0 && reinterpret_cast<uintptr_t>(co) % 16 == 0)
+    return launch_ising_bits_nw<TRACE, 4>(cc, co, words, rows_local, wrap, row_lo, row_hi, global_row0, height, colour,
+                                          block_row0, thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace,
+                                          trace_len, ex, s);
+#endif
+#if TTHRML_ISING_BITS_QUEUE && TTHRML_ISING_BITS_WORDS >= 2
+  if (words % 2 == 0 && reinterpret_cast<uintptr_t>(co) % 8 == 0)
+    return launch_ising_bits_nw<TRACE, 2>(cc, co, words, rows_local, wrap, row_lo, row_hi, global_row0, height, colour,
+                                          block_row0, thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace,
+                                          trace_len, ex, s);
+#endif
+  return launch_ising_bits_nw<TRACE, 1>(cc, co, words, rows_local, wrap, row_lo, row_hi, global_row0, height, colour,
+                                        block_row0, thresholds, chain, seed, sweep, ctl, count_lo, count_hi, trace,
+                                        trace_len, ex, s);
 }
 
 template <bool TRACE>
