@@ -55,6 +55,87 @@ def test_library_rejects_bad_arguments_without_a_gpu():
     assert lib.tthrml_group_step(ctypes.byref(g), None) == -1
 
 
+
+_A, _M = 4096, 4100  # a 16-byte aligned and a misaligned stand-in address: rejected calls never dereference them
+_BAD_CALLS = [
+    ("tthrml_spin_bits_step", (_A, _A, _A, None, 0, 10, _A, 100, 0, None, 0, 0, 0, None, None), b"multiple of 256"),
+    ("tthrml_spin_bits_step", (_A, _A, _A, None, 0, 10, _M, 256, 0, None, 0, 0, 0, None, None), b"16-byte aligned"),
+    ("tthrml_spin_bits_step_ordered", (_A, _A, _A, None, 0, 10, _A, 256, 0, None, 0, 0, 0, None, None, None),
+     b"NULL row order"),
+    ("tthrml_dense_field_sample", (_A, _A, 100, 256, 64, None, 0, 1.0, _A, None, 1, 0, 0, None, 0, 0, 0, None, _A,
+                                   None), b"chains must be a multiple of 128"),
+    ("tthrml_dense_field_sample", (_A, _A, 128, 256, 64, None, 1, 1.0, _A, None, 1, 0, 0, None, 0, 0, 0, None, _A,
+                                   None), b"family must be spin or gaussian"),
+    ("tthrml_dense_field_sample", (_A, _A, 128, 256, 64, None, 0, 1.0, _A, None, 4, 0, 0, None, 0, 0, 0, None, _A,
+                                   None), b"out_pieces must be 1, 2 or 3"),
+    ("tthrml_dense_field_sample_ties", (_A, _A, 128, 256, 64, None, 0, 1.0, _A, None, 1, 0, 0, None, 0, 0, 0, None,
+                                        _A, _M, 10, None), b"ties must be 16-byte aligned"),
+    ("tthrml_dense_field_sample_ties", (_A, _A, 128, 256, 64, None, 0, 1.0, _A, None, 1, 0, 0, None, 0, 0, 0, None,
+                                        _A, None, 10, None), b"NULL tie list"),
+    ("tthrml_potts3d_step", (_A, 64, 5, 4, 4, 0, 0, 40, _A, _A, 8, 0, None, 0, 0, 0, None, None),
+     b"positive and even"),
+    ("tthrml_potts3d_step", (_A, 64, 4, 4, 4, 0, 0, 40, _A, _A, 9, 0, None, 0, 0, 0, None, None), b"q must be in [1, 8]"),
+    ("tthrml_potts3d_step", (_A, 64, 4, 4, 4, 0, 0, 16, _A, _A, 8, 0, None, 0, 0, 0, None, None),
+     b"disjoint row ranges"),
+    ("tthrml_potts3d_step_weights", (_A, 64, 4, 4, 4, 0, 0, 40, _A, _A, 8, 0, None, 0, 0, 0, None, _M, None),
+     b"16-byte aligned device array"),
+    ("tthrml_potts3d_bias_weights", (_A, 64, 4, _A, None), b"q must be 8"),
+    ("tthrml_ising2d_halfsweep_bits", (_A, _A, 96, 8, 1, 0, 8, 0, 8, 0, 0, _A, 0, 0, 0, None, 0, 8, None, 0, None,
+                                       None), b"positive multiple of 64"),
+    ("tthrml_ising2d_halfsweep_bits", (_A, _A, 128, 8, 1, 0, 10, 0, 8, 0, 0, _A, 0, 0, 0, None, 0, 8, None, 0, None,
+                                       None), b"row range [0, 10) outside the 8 local rows"),
+    ("tthrml_ising2d_halfsweep_bits", (_A, _A, 128, 12, 1, 0, 8, 0, 8, 0, 0, _A, 0, 0, 0, None, 0, 8, None, 0, None,
+                                       None), b"rows_local == height"),
+    ("tthrml_ising2d_halfsweep_bits", (_A, _A, 128, 8, 0, 0, 8, 0, 8, 0, 0, _A, 0, 0, 0, None, 0, 8, None, 0, None,
+                                       None), b"halo row on both sides"),
+    ("tthrml_ising2d_halfsweep_bits", (_A + 2, _A, 128, 8, 1, 0, 8, 0, 8, 0, 0, _A, 0, 0, 0, None, 0, 8, None, 0,
+                                       None, None), b"4-byte aligned"),
+    ("tthrml_ising2d_halfsweep_planes", (_A, _A, 96, 8, 1, 0, 8, 0, 8, 0, 0, _A, 0, 0, 0, None, 0, 8, None, 0, None,
+                                         None), b"width % 64 == 0"),
+    ("tthrml_ising2d_resident", (_A, 48, 8, 8, 0, 32, _A, 0, 0, 0, 4, None, 0, 0, 0, 0, 0, None, _A, None),
+     b"n_chains % 32 == 0"),
+    ("tthrml_ising2d_resident_planes", (_A, 64, 8, 8, 0, 32, _A, 0, 0, 0, 4, _A, 1, 5, 2, 3, 0, None, _A, None),
+     b"observation schedule outside the run"),
+    ("tthrml_decode_rows", (_A, 0, 64, 0, 4, 3, _A, None), b"invalid arguments"),
+    ("tthrml_encode_rows", (_A, 5, 1, 4, 0, 64, 0, _A, None), b"unknown input dtype 5"),
+    ("tthrml_encode_rows", (_A, 0, 1, 4, 2, 48, 0, _A, None), b"n_chains % 32 == 0"),
+    ("tthrml_sum_rows", (_A, 0, 64, 0, 4, None, None), b"invalid arguments"),
+    ("tthrml_moments_accumulate", (_A, 2, 64, _A, None, 0, 3, 0, _A, None), b"invalid arguments"),
+    ("tthrml_halo_import", (_A, _A, 48, 2, 0, 10, _A, _A, 1, 0, None, _A, None), b"invalid arguments"),
+    ("tthrml_ctl_advance", (None, 1, None), b"ctl is NULL"),
+]
+
+
+@pytest.mark.parametrize("name,args,message", _BAD_CALLS, ids=[f"{c[0]}-{i}" for i, c in enumerate(_BAD_CALLS)])
+def test_entry_points_reject_bad_arguments_before_any_cuda_call(name, args, message):
+    """Argument checks come first in every entry point: a rejected call returns TTHRML_ERR_ARG with the reason
+    in tthrml_last_error() and touches neither the device nor the (stand-in) pointers, so it runs without a GPU."""
+    lib = nat.lib()
+    assert getattr(lib, name)(*args) == -1
+    err = lib.tthrml_last_error()
+    assert name.encode() in err or name.rsplit("_", 1)[0].encode() in err, err
+    assert message in err, err
+
+
+def test_static_scratch_step_rejects_an_empty_descriptor_without_a_gpu():
+    lib = nat.lib()
+    g = nat.GroupDesc()
+    assert lib.tthrml_group_step_static_scratch(ctypes.byref(g), None) == -1
+    assert b"invalid group descriptor" in lib.tthrml_last_error()
+
+
+@pytest.mark.parametrize("call", [
+    ("tthrml_spin_bits_step", (None, None, None, None, 0, 0, None, 0, 0, None, 0, 0, 0, None, None)),
+    ("tthrml_decode_rows", (None, 0, 64, 0, 0, 0, None, None)),
+    ("tthrml_encode_rows", (None, 0, 1, 0, 0, 64, 0, None, None)),
+    ("tthrml_sum_rows", (None, 0, 64, 0, 0, None, None)),
+    ("tthrml_moments_accumulate", (None, 0, 64, None, None, 1, 0, 0, None, None)),
+], ids=lambda c: c[0])
+def test_empty_inputs_are_no_ops_without_a_gpu(call):
+    """Zero rows (or zero moments) launch nothing and succeed, whatever the pointers."""
+    name, args = call
+    assert getattr(nat.lib(), name)(*args) == 0
+
 def test_greedy_colouring_is_proper():
     rp, cols = workloads.lattice_2d_csr(6, 8)
     col = workloads.greedy_colouring(rp, cols)
